@@ -1,0 +1,538 @@
+// attention.cu -- paged-KV GQA attention for mixed prefill-chunk + decode batches.
+//
+// Reference op: `attention` (cpp/src/cpu/llama.cpp:67-112): causal GQA (query
+// head h reads kv head h / (Hq/Hkv)), scores scaled by 1/sqrt(d), softmax with
+// the row maximum subtracted, over the per-sequence cache.  The reference CUDA
+// worker materialises GQA-expanded F32 K/V and an [Hq, T, C] score matrix per
+// sequence (cpp/src/cuda/stage.cpp:279-302, looped per batch member :326-333);
+// here one launch covers the whole ragged batch, K/V stay F16 in 16-token
+// pages, every query head of a GQA group shares one pass over its KV pages,
+// and no score matrix is stored (online softmax).
+//
+//   decode rows:  split-K over the context.  Each CTA takes one (kv head,
+//                 context split); a single thread streams the split's 16-token
+//                 K and V pages into a shared-memory ring with cp.async.bulk
+//                 (TMA bulk copies, mbarrier completion, bounded waits); a
+//                 combine pass merges the splits.
+//   prefill rows: causal flash tiles on the tensor cores (mma.sync F16 -> F32),
+//                 64 query rows per CTA = (tokens x heads of one GQA group),
+//                 K/V pages gathered by block table with cp.async.
+#include <math.h>
+
+#include "attention.cuh"
+#include "common.cuh"
+
+namespace hb {
+namespace {
+
+constexpr int kDecThreads = 128;
+constexpr int kDecStages = 4;
+constexpr int kMaxGroup = 8;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ int find_row(const int32_t* cu, int rows, int idx) {
+  int lo = 0, hi = rows;  // cu[lo] <= idx < cu[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (cu[mid] <= idx) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// ---------------------------------------------------------------- decode
+__global__ void __launch_bounds__(kDecThreads)
+    decode_attn_kernel(const AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int d = a.dim;
+  const int G = a.hq / a.hkv;
+  const int kvh = blockIdx.x;
+  const int split = blockIdx.y;
+  const int r = find_row(a.cu_splits, a.rows, split);
+  if (a.row_count[r] != 1) return;
+  const int local = split - a.cu_splits[r];
+  const int ctx = a.seq_lens[r];
+  const int key0 = local * a.split_tokens;
+  const int key1 = min(ctx, key0 + a.split_tokens);
+  const int kb0 = key0 / 16, kb1 = (key1 + 15) / 16;
+  const int nblk = kb1 - kb0;
+  const int t = a.cu_seqlens[r];
+
+  const uint32_t page_bytes = 16u * d * 2u;
+  __half* ring = reinterpret_cast<__half*>(smem);                       // [S][2][16][d]
+  float* qs = reinterpret_cast<float*>(smem + kDecStages * 2 * page_bytes);  // [G][d]
+  float* sc = qs + G * d;                                               // [G][16]
+  float* pr = sc + G * 16;                                              // [G][16]
+  float* st = pr + G * 16;                                              // m[G], l[G], alpha[G]
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(st + 3 * kMaxGroup) + 7) & ~static_cast<uintptr_t>(7));
+
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kDecStages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  for (int i = tid; i < G * d; i += kDecThreads)
+    qs[i] = __half2float(a.q[static_cast<size_t>(t) * a.hq * d + (kvh * G) * d + i]);
+  if (tid < G) {
+    st[tid] = -INFINITY;
+    st[kMaxGroup + tid] = 0.f;
+  }
+  __syncthreads();
+
+  const int32_t* table = a.block_tables + static_cast<size_t>(r) * a.max_blocks;
+  auto issue = [&](int i) {
+    const int s = i % kDecStages;
+    const int bid = table[kb0 + i];
+    if (bid < 0) {  // no page: complete the phase without a copy and report it
+      atomicOr(a.status, kDevBadIndex);
+      mbar_arrive(&full[s]);
+      return;
+    }
+    const size_t page = (static_cast<size_t>(bid) * a.hkv + kvh) * 16 * d;
+    __half* dst = ring + static_cast<size_t>(s) * 2 * 16 * d;
+    mbar_arrive_expect_tx(&full[s], 2 * page_bytes);
+    bulk_load(dst, a.k_cache + page, page_bytes, &full[s]);
+    bulk_load(dst + 16 * d, a.v_cache + page, page_bytes, &full[s]);
+  };
+  if (tid == 0)
+    for (int i = 0; i < min(nblk, kDecStages); ++i) issue(i);
+
+  // Per-thread PV accumulators: chunks of 4 dims, chunk c = tid + 128 k over G*d/4.
+  const int chunks = G * d / 4;
+  float acc[4][4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[k][e] = 0.f;
+
+  const int grp = tid >> 3, sub = tid & 7;  // QK: 16 groups of 8 lanes, one key each
+  bool ok = true;
+  for (int i = 0; i < nblk; ++i) {
+    const int s = i % kDecStages;
+    if (!mbar_wait(&full[s], (i / kDecStages) & 1u, a.status)) { ok = false; }
+    if (__syncthreads_or(!ok)) break;
+    const __half* kp = ring + static_cast<size_t>(s) * 2 * 16 * d;
+    const __half* vp = kp + 16 * d;
+    // Phase 1: scores for key `grp` of this page, all G heads.
+    {
+      const int key = (kb0 + i) * 16 + grp;
+      float part[kMaxGroup];
+#pragma unroll
+      for (int g = 0; g < kMaxGroup; ++g) part[g] = 0.f;
+      for (int base = sub * 4; base < d; base += 32) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(kp + grp * d + base);
+        const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+#pragma unroll
+        for (int g = 0; g < kMaxGroup; ++g) {
+          if (g < G) {
+            const float* qg = qs + g * d + base;
+            part[g] += qg[0] * k01.x + qg[1] * k01.y + qg[2] * k23.x + qg[3] * k23.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kMaxGroup; ++g) {
+        if (g < G) {
+          float v = part[g];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          if (sub == 0) sc[g * 16 + grp] = (key >= key0 && key < key1) ? v * a.scale : -INFINITY;
+        }
+      }
+    }
+    __syncthreads();
+    // The previous page's slot is free now: refill it.
+    if (tid == 0 && i >= 1 && i - 1 + kDecStages < nblk) issue(i - 1 + kDecStages);
+    // Phase 2: online-softmax statistics per head.
+    if (tid < G) {
+      const float m_old = st[tid];
+      float mx = m_old;
+      for (int j = 0; j < 16; ++j) mx = fmaxf(mx, sc[tid * 16 + j]);
+      const float alpha = expf(m_old - mx);
+      float sum = 0.f;
+      for (int j = 0; j < 16; ++j) {
+        const float p = expf(sc[tid * 16 + j] - mx);
+        pr[tid * 16 + j] = p;
+        sum += p;
+      }
+      st[tid] = mx;
+      st[kMaxGroup + tid] = st[kMaxGroup + tid] * alpha + sum;
+      st[2 * kMaxGroup + tid] = alpha;
+    }
+    __syncthreads();
+    // Phase 3: acc = acc * alpha + sum_j p_j V_j.
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = tid + k * kDecThreads;
+      if (c < chunks) {
+        const int g = c / (d / 4), i0 = (c % (d / 4)) * 4;
+        const float alpha = st[2 * kMaxGroup + g];
+        float o0 = acc[k][0] * alpha, o1 = acc[k][1] * alpha, o2 = acc[k][2] * alpha,
+              o3 = acc[k][3] * alpha;
+        for (int j = 0; j < 16; ++j) {
+          const float p = pr[g * 16 + j];
+          const uint2 raw = *reinterpret_cast<const uint2*>(vp + j * d + i0);
+          const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+          const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+          o0 += p * v01.x;
+          o1 += p * v01.y;
+          o2 += p * v23.x;
+          o3 += p * v23.y;
+        }
+        acc[k][0] = o0; acc[k][1] = o1; acc[k][2] = o2; acc[k][3] = o3;
+      }
+    }
+  }
+  // Write this split's unnormalised output and statistics.
+  const int h0 = kvh * G;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int c = tid + k * kDecThreads;
+    if (c < chunks) {
+      const int g = c / (d / 4), i0 = (c % (d / 4)) * 4;
+      float* dst = a.part_o + (static_cast<size_t>(split) * a.hq + h0 + g) * d + i0;
+      *reinterpret_cast<float4*>(dst) = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+    }
+  }
+  if (tid < G) {
+    float* ml = a.part_ml + (static_cast<size_t>(split) * a.hq + h0 + tid) * 2;
+    ml[0] = st[tid];
+    ml[1] = st[kMaxGroup + tid];
+  }
+}
+
+// One CTA per (decode row, query head): merge the row's splits.
+__global__ void decode_combine_kernel(const AttnArgs a) {
+  const int r = blockIdx.x, h = blockIdx.y;
+  if (a.row_count[r] != 1) return;
+  const int s0 = a.cu_splits[r], s1 = a.cu_splits[r + 1];
+  const int d = a.dim;
+  float m = -INFINITY;
+  for (int s = s0; s < s1; ++s) m = fmaxf(m, a.part_ml[(static_cast<size_t>(s) * a.hq + h) * 2]);
+  float l = 0.f;
+  for (int s = s0; s < s1; ++s) {
+    const float* ml = a.part_ml + (static_cast<size_t>(s) * a.hq + h) * 2;
+    l += ml[1] * expf(ml[0] - m);
+  }
+  const int t = a.cu_seqlens[r];
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    float o = 0.f;
+    for (int s = s0; s < s1; ++s) {
+      const float w = expf(a.part_ml[(static_cast<size_t>(s) * a.hq + h) * 2] - m);
+      o += a.part_o[(static_cast<size_t>(s) * a.hq + h) * d + i] * w;
+    }
+    a.out[static_cast<size_t>(t) * a.ld_out + h * d + i] = __float2half_rn(o / l);
+  }
+}
+
+// ---------------------------------------------------------------- prefill
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Byte offset of 16-byte chunk c of row `row` in a [rows][DP] F16 tile, with an
+// XOR swizzle over the low three chunk bits so ldmatrix rows hit distinct banks.
+template <int DP>
+__device__ __forceinline__ uint32_t tile_off(int row, int c) {
+  const int sc = DP >= 64 ? (c ^ (row & 7)) : c;
+  return static_cast<uint32_t>(row * DP * 2 + sc * 16);
+}
+
+template <int DP, int KT>
+struct PrefillShape {
+  static constexpr int kRows = 64;
+  static constexpr uint32_t kQBytes = kRows * DP * 2;
+  static constexpr uint32_t kKvBytes = KT * DP * 2;
+  static constexpr uint32_t kSmem = kQBytes + 4 * kKvBytes;  // Q + 2 x (K, V)
+};
+
+// Loads `rows` rows of a [*][d] F16 source into a swizzled [rows][DP] tile;
+// row_src(i) gives the source row pointer or null (zero row).
+template <int DP, class RowSrc>
+__device__ __forceinline__ void load_tile(uint8_t* tile, int rows, int d, RowSrc row_src) {
+  const int chunks = DP / 8;
+  const uint32_t base = smem_u32(tile);
+  const bool vec = (d % 8) == 0;
+  for (int idx = threadIdx.x; idx < rows * chunks; idx += blockDim.x) {
+    const int rr = idx / chunks, c = idx % chunks;
+    const __half* src = row_src(rr);
+    const uint32_t off = tile_off<DP>(rr, c);
+    if (src && vec && c * 8 < d) {
+      cp_async16(base + off, src + c * 8);
+    } else {
+      __half tmp[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int dim = c * 8 + e;
+        tmp[e] = (src && dim < d) ? src[dim] : __float2half(0.f);
+      }
+      *reinterpret_cast<uint4*>(tile + off) = *reinterpret_cast<uint4*>(tmp);
+    }
+  }
+}
+
+template <int DP, int KT>
+__global__ void __launch_bounds__(128)
+    prefill_attn_kernel(const AttnArgs a) {
+  using S = PrefillShape<DP, KT>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* qs = smem;
+  uint8_t* ks[2] = {smem + S::kQBytes, smem + S::kQBytes + S::kKvBytes};
+  uint8_t* vs[2] = {smem + S::kQBytes + 2 * S::kKvBytes, smem + S::kQBytes + 3 * S::kKvBytes};
+
+  const int d = a.dim;
+  const int G = a.hq / a.hkv;
+  const int QT = a.qtile_tokens;
+  const int kvh = blockIdx.x;
+  const int tile = blockIdx.y;
+  const int r = find_row(a.cu_qtiles, a.rows, tile);
+  const int count = a.row_count[r];
+  if (count <= 1) return;
+  const int tok0 = (tile - a.cu_qtiles[r]) * QT;  // first local token of this tile
+  const int first = a.row_first[r];
+  const int t_base = a.cu_seqlens[r];
+  const int ntok = min(QT, count - tok0);
+  const int ctx_hi = first + tok0 + ntok;  // keys [0, ctx_hi)
+  const int32_t* table = a.block_tables + static_cast<size_t>(r) * a.max_blocks;
+
+  // Q tile: query row qr = (token qr / G, head qr % G of this group).
+  load_tile<DP>(qs, S::kRows, d, [&](int qr) -> const __half* {
+    const int tl = qr / G, g = qr % G;
+    if (tl >= ntok) return nullptr;
+    return a.q + static_cast<size_t>(t_base + tok0 + tl) * a.hq * d + (kvh * G + g) * d;
+  });
+  auto kv_src = [&](const __half* cache, int key) -> const __half* {
+    if (key >= ctx_hi) return nullptr;
+    const int bid = table[key >> 4];
+    if (bid < 0) return nullptr;
+    return cache + ((static_cast<size_t>(bid) * a.hkv + kvh) * 16 + (key & 15)) * d;
+  };
+  const int n_kt = (ctx_hi + KT - 1) / KT;
+  load_tile<DP>(ks[0], KT, d, [&](int i) { return kv_src(a.k_cache, i); });
+  load_tile<DP>(vs[0], KT, d, [&](int i) { return kv_src(a.v_cache, i); });
+  cp_async_commit();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = warp * 16 + (lane >> 2), row1 = row0 + 8;
+  const int pos0 = first + tok0 + row0 / G, pos1 = first + tok0 + row1 / G;
+  const float sl2 = a.scale * kLog2e;
+
+  float o[DP / 8][4];
+#pragma unroll
+  for (int i = 0; i < DP / 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[i][e] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const uint32_t q_base = smem_u32(qs);
+
+  for (int kt = 0; kt < n_kt; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < n_kt) {
+      load_tile<DP>(ks[buf ^ 1], KT, d, [&](int i) { return kv_src(a.k_cache, (kt + 1) * KT + i); });
+      load_tile<DP>(vs[buf ^ 1], KT, d, [&](int i) { return kv_src(a.v_cache, (kt + 1) * KT + i); });
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint32_t k_base = smem_u32(ks[buf]);
+    const uint32_t v_base = smem_u32(vs[buf]);
+
+    float s[KT / 8][4];
+#pragma unroll
+    for (int i = 0; i < KT / 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[i][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < DP / 16; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      {
+        const int rr = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = kk * 2 + (lane >> 4);
+        ldsm_x4(q_base + tile_off<DP>(rr, c), a0, a1, a2, a3);
+      }
+#pragma unroll
+      for (int nb = 0; nb < KT / 8; nb += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int key = nb * 8 + (lane & 7) + (lane >> 4) * 8;
+        const int c = kk * 2 + ((lane >> 3) & 1);
+        ldsm_x4(k_base + tile_off<DP>(key, c), b0, b1, b2, b3);
+        mma16816(s[nb], a0, a1, a2, a3, b0, b1);
+        mma16816(s[nb + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    // Scale, causal mask, online softmax (base-2 exponent of scale*log2(e)*s).
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int nb = 0; nb < KT / 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = kt * KT + nb * 8 + (lane & 3) * 2 + (e & 1);
+        const int pos = e < 2 ? pos0 : pos1;
+        const float v = (key <= pos && key < ctx_hi) ? s[nb][e] * sl2 : -INFINITY;
+        s[nb][e] = v;
+        if (e < 2) mx0 = fmaxf(mx0, v); else mx1 = fmaxf(mx1, v);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    // A query row always sees key 0 in the first tile, so the maxima are finite
+    // from the first tile on; padded rows (beyond the tile's tokens) are masked
+    // like their last valid token and never stored.
+    const float al0 = exp2f(m0 - mx0), al1 = exp2f(m1 - mx1);
+    m0 = mx0;
+    m1 = mx1;
+    float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+    for (int nb = 0; nb < KT / 8; ++nb) {
+      s[nb][0] = exp2f(s[nb][0] - m0);
+      s[nb][1] = exp2f(s[nb][1] - m0);
+      s[nb][2] = exp2f(s[nb][2] - m1);
+      s[nb][3] = exp2f(s[nb][3] - m1);
+      rs0 += s[nb][0] + s[nb][1];
+      rs1 += s[nb][2] + s[nb][3];
+    }
+    l0 = l0 * al0 + rs0;
+    l1 = l1 * al1 + rs1;
+#pragma unroll
+    for (int i = 0; i < DP / 8; ++i) {
+      o[i][0] *= al0;
+      o[i][1] *= al0;
+      o[i][2] *= al1;
+      o[i][3] *= al1;
+    }
+    // O += P V.
+#pragma unroll
+    for (int k2 = 0; k2 < KT / 16; ++k2) {
+      const uint32_t p0 = pack_half2(s[2 * k2][0], s[2 * k2][1]);
+      const uint32_t p1 = pack_half2(s[2 * k2][2], s[2 * k2][3]);
+      const uint32_t p2 = pack_half2(s[2 * k2 + 1][0], s[2 * k2 + 1][1]);
+      const uint32_t p3 = pack_half2(s[2 * k2 + 1][2], s[2 * k2 + 1][3]);
+#pragma unroll
+      for (int db = 0; db < DP / 8; db += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int key = k2 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = db + (lane >> 4);
+        ldsm_x4_t(v_base + tile_off<DP>(key, c), b0, b1, b2, b3);
+        mma16816(o[db], p0, p1, p2, p3, b0, b1);
+        mma16816(o[db + 1], p0, p1, p2, p3, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+  const int tl0 = row0 / G, g0 = row0 % G, tl1 = row1 / G, g1 = row1 % G;
+  __half* out0 = tl0 < ntok ? a.out + static_cast<size_t>(t_base + tok0 + tl0) * a.ld_out +
+                                  (kvh * G + g0) * d
+                            : nullptr;
+  __half* out1 = tl1 < ntok ? a.out + static_cast<size_t>(t_base + tok0 + tl1) * a.ld_out +
+                                  (kvh * G + g1) * d
+                            : nullptr;
+#pragma unroll
+  for (int db = 0; db < DP / 8; ++db) {
+    const int dim = db * 8 + (lane & 3) * 2;
+    if (dim < d) {
+      if (out0) {
+        out0[dim] = __float2half_rn(o[db][0] * inv0);
+        if (dim + 1 < d) out0[dim + 1] = __float2half_rn(o[db][1] * inv0);
+      }
+      if (out1) {
+        out1[dim] = __float2half_rn(o[db][2] * inv1);
+        if (dim + 1 < d) out1[dim + 1] = __float2half_rn(o[db][3] * inv1);
+      }
+    }
+  }
+}
+
+template <int DP, int KT>
+cudaError_t launch_prefill(const AttnArgs& a, int total_qtiles, cudaStream_t stream) {
+  using S = PrefillShape<DP, KT>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<DP, KT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(S::kSmem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  prefill_attn_kernel<DP, KT><<<dim3(a.hkv, total_qtiles), 128, S::kSmem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int attn_qtile_tokens(int group) { return 64 / group; }
+
+cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t stream) {
+  if (total_splits <= 0) return cudaSuccess;
+  const int G = a.hq / a.hkv;
+  if (G > kMaxGroup || a.dim % 4 != 0 || a.dim > 256 || G * a.dim / 4 > 4 * kDecThreads ||
+      a.split_tokens % 16 != 0)
+    return cudaErrorInvalidValue;
+  const size_t smem = kDecStages * 2 * 16 * a.dim * 2 +
+                      (G * a.dim + 2 * G * 16 + 3 * kMaxGroup) * sizeof(float) + 8 +
+                      kDecStages * sizeof(uint64_t);
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  decode_attn_kernel<<<dim3(a.hkv, total_splits), kDecThreads, smem, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  decode_combine_kernel<<<dim3(a.rows, a.hq), 128, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t attn_prefill_launch(const AttnArgs& a, int total_qtiles, cudaStream_t stream) {
+  if (total_qtiles <= 0) return cudaSuccess;
+  const int G = a.hq / a.hkv;
+  if (64 % G != 0 && G > 64) return cudaErrorInvalidValue;
+  if (a.dim <= 16) return launch_prefill<16, 64>(a, total_qtiles, stream);
+  if (a.dim <= 64) return launch_prefill<64, 64>(a, total_qtiles, stream);
+  if (a.dim <= 128) return launch_prefill<128, 64>(a, total_qtiles, stream);
+  if (a.dim <= 256) return launch_prefill<256, 32>(a, total_qtiles, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace hb

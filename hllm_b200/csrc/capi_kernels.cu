@@ -1,0 +1,285 @@
+// capi_kernels.cu -- device-pointer C entry points of the individual kernels
+// (include/hllm_b200.h, "kernel entry points"): used by the parity tests and
+// the per-operator benchmarks.  They launch exactly the kernels the stage
+// executor launches.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "hllm_b200.h"
+#include "kernels.cuh"
+#include "sampler.cuh"
+
+namespace hb {
+void set_last_error(const std::string& message);  // stage.cu
+}
+
+namespace {
+
+void set_error(const std::string& m) { hb::set_last_error(m); }
+
+hllm_b200_status cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return HLLM_B200_OK;
+  set_error(cudaGetErrorString(e));
+  return e == cudaErrorInvalidValue ? HLLM_B200_INVALID_REQUEST : HLLM_B200_INTERNAL;
+}
+
+// GEMM scratch owned by the library, one per device, allocated on first use.
+struct DeviceScratch {
+  hb::GemmScratch gemm{};
+  size_t counters_for_tiles = 0;
+};
+std::mutex g_scratch_mutex;
+std::map<int, DeviceScratch> g_scratch;
+
+hllm_b200_status scratch_for_device(hb::GemmScratch* out, size_t tiles) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  std::scoped_lock lock(g_scratch_mutex);
+  DeviceScratch& s = g_scratch[dev];
+  if (!s.gemm.partials) {
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_status(e);
+    s.gemm.sm_count = sms;
+    s.gemm.partial_floats = hb::gemm_partial_floats(sms);
+    e = cudaMalloc(&s.gemm.partials, s.gemm.partial_floats * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&s.gemm.status, 256);
+    if (e == cudaSuccess) e = cudaMemset(s.gemm.status, 0, 256);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  if (s.counters_for_tiles < tiles) {
+    if (s.gemm.counters) cudaFree(s.gemm.counters);
+    s.gemm.counters = nullptr;
+    const size_t n = std::max<size_t>(tiles, 4096);
+    e = cudaMalloc(&s.gemm.counters, n * sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(s.gemm.counters, 0, n * sizeof(unsigned));
+    if (e != cudaSuccess) return cuda_status(e);
+    s.counters_for_tiles = n;
+    s.gemm.counter_count = n;
+  }
+  *out = s.gemm;
+  return HLLM_B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint32_t pair,
+                                uint64_t second_row, const void* x, uint64_t n, uint32_t epilogue,
+                                void* y, uint64_t ldy, uint32_t bn, uint32_t grid, void* stream) {
+  if (!w || !x || !y || m == 0 || n == 0 || k_pad == 0 || k_pad % 64 != 0 || epilogue > 3 ||
+      (pair != 1 && pair != 2))
+    return HLLM_B200_INVALID_REQUEST;
+  hb::GemmWeight gw{};
+  const int rows_total = pair == 2 ? static_cast<int>(second_row + m) : static_cast<int>(m);
+  if (!hb::gemm_make_weight(&gw, w, rows_total, static_cast<int>(m), static_cast<int>(k_pad),
+                            static_cast<int>(pair), static_cast<int>(second_row)))
+    return HLLM_B200_INTERNAL;
+  hb::GemmInput gx{};
+  if (!hb::gemm_make_input(&gx, x, static_cast<int>(n), static_cast<int>(k_pad),
+                           static_cast<int>(k_pad)))
+    return HLLM_B200_INTERNAL;
+  hb::GemmScratch sc{};
+  const size_t tiles = ((m + 127) / 128) * ((n + 15) / 16);
+  const hllm_b200_status st = scratch_for_device(&sc, tiles);
+  if (st != HLLM_B200_OK) return st;
+  return cuda_status(hb::gemm_run(gw, gx, static_cast<int>(n), static_cast<int>(epilogue), y,
+                                  static_cast<int>(ldy), sc, static_cast<cudaStream_t>(stream),
+                                  static_cast<int>(bn), static_cast<int>(grid)));
+}
+
+hllm_b200_status hllm_b200_rmsnorm(const float* x, uint64_t rows, uint64_t width, const float* w,
+                                   float eps, uint16_t* out, uint64_t ld_out, void* stream) {
+  return cuda_status(hb::rmsnorm_launch(x, static_cast<int>(rows), static_cast<int>(width), w, eps,
+                                        reinterpret_cast<__half*>(out), static_cast<int>(ld_out),
+                                        nullptr, static_cast<cudaStream_t>(stream)));
+}
+
+hllm_b200_status hllm_b200_pack(const int32_t* row_slot, const int32_t* row_first,
+                                const int32_t* row_count, uint32_t rows, uint32_t tokens,
+                                const int32_t* slot_blocks, uint32_t max_blocks,
+                                uint32_t split_tokens, uint32_t qtile_tokens, int32_t* cu_seqlens,
+                                int32_t* positions, int32_t* slot_mapping, int32_t* token_row,
+                                int32_t* seq_lens, int32_t* block_tables, int32_t* cu_splits,
+                                int32_t* cu_qtiles, uint32_t* status, void* stream) {
+  if (split_tokens == 0 || qtile_tokens == 0) return HLLM_B200_INVALID_REQUEST;
+  hb::StepTensors s{};
+  s.row_slot = row_slot;
+  s.row_first = row_first;
+  s.row_count = row_count;
+  s.cu_seqlens = cu_seqlens;
+  s.positions = positions;
+  s.slot_mapping = slot_mapping;
+  s.token_row = token_row;
+  s.seq_lens = seq_lens;
+  s.block_tables = block_tables;
+  s.cu_splits = cu_splits;
+  s.cu_qtiles = cu_qtiles;
+  s.rows = static_cast<int>(rows);
+  s.tokens = static_cast<int>(tokens);
+  s.max_blocks = static_cast<int>(max_blocks);
+  s.split_tokens = static_cast<int>(split_tokens);
+  s.qtile_tokens = static_cast<int>(qtile_tokens);
+  return cuda_status(hb::pack_launch(s, slot_blocks, status, static_cast<cudaStream_t>(stream)));
+}
+
+uint32_t hllm_b200_attention_qtile_tokens(uint32_t group) {
+  return group ? static_cast<uint32_t>(hb::attn_qtile_tokens(static_cast<int>(group))) : 0u;
+}
+
+hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
+                                     const uint16_t* v_cache, const int32_t* row_first,
+                                     const int32_t* row_count, const int32_t* cu_seqlens,
+                                     const int32_t* seq_lens, const int32_t* block_tables,
+                                     const int32_t* cu_splits, const int32_t* cu_qtiles,
+                                     uint32_t rows, uint32_t total_splits, uint32_t total_qtiles,
+                                     uint32_t hq, uint32_t hkv, uint32_t dim, uint32_t max_blocks,
+                                     uint32_t split_tokens, uint16_t* out, uint64_t ld_out,
+                                     uint32_t* status, void* stream) {
+  if (hkv == 0 || hq % hkv != 0 || dim == 0) return HLLM_B200_INVALID_REQUEST;
+  hb::AttnArgs a{};
+  a.q = reinterpret_cast<const __half*>(q);
+  a.k_cache = reinterpret_cast<const __half*>(k_cache);
+  a.v_cache = reinterpret_cast<const __half*>(v_cache);
+  a.row_count = row_count;
+  a.row_first = row_first;
+  a.cu_seqlens = cu_seqlens;
+  a.seq_lens = seq_lens;
+  a.block_tables = block_tables;
+  a.cu_splits = cu_splits;
+  a.cu_qtiles = cu_qtiles;
+  a.rows = static_cast<int>(rows);
+  a.hq = static_cast<int>(hq);
+  a.hkv = static_cast<int>(hkv);
+  a.dim = static_cast<int>(dim);
+  a.max_blocks = static_cast<int>(max_blocks);
+  a.split_tokens = static_cast<int>(split_tokens);
+  a.qtile_tokens = hb::attn_qtile_tokens(static_cast<int>(hq / hkv));
+  a.scale = 1.0f / std::sqrt(static_cast<float>(dim));
+  a.out = reinterpret_cast<__half*>(out);
+  a.ld_out = static_cast<int>(ld_out);
+  a.status = status;
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (total_splits) {
+    cudaError_t e = cudaMallocAsync(&part_o, static_cast<size_t>(total_splits) * hq * dim * 4, st);
+    if (e == cudaSuccess) e = cudaMallocAsync(&part_ml, static_cast<size_t>(total_splits) * hq * 8, st);
+    if (e != cudaSuccess) return cuda_status(e);
+    a.part_o = part_o;
+    a.part_ml = part_ml;
+    e = hb::attn_decode_launch(a, static_cast<int>(total_splits), st);
+    cudaFreeAsync(part_o, st);
+    cudaFreeAsync(part_ml, st);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  return cuda_status(hb::attn_prefill_launch(a, static_cast<int>(total_qtiles), st));
+}
+
+hllm_b200_status hllm_b200_qkv_post(const float* qkv, uint64_t tokens, uint32_t hq, uint32_t hkv,
+                                    uint32_t dim, const int32_t* positions,
+                                    const int32_t* slot_mapping, const float* q_norm,
+                                    const float* k_norm, float eps, const float* rope_pow,
+                                    uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache,
+                                    void* stream) {
+  hb::QkvPostArgs a{};
+  a.qkv = qkv;
+  a.tokens = static_cast<int>(tokens);
+  a.hq = static_cast<int>(hq);
+  a.hkv = static_cast<int>(hkv);
+  a.dim = static_cast<int>(dim);
+  a.positions = positions;
+  a.slot_mapping = slot_mapping;
+  a.q_norm = q_norm;
+  a.k_norm = k_norm;
+  a.eps = eps;
+  a.rope_pow = rope_pow;
+  a.q_out = reinterpret_cast<__half*>(q_out);
+  a.k_cache = reinterpret_cast<__half*>(k_cache);
+  a.v_cache = reinterpret_cast<__half*>(v_cache);
+  return cuda_status(hb::qkv_post_launch(a, static_cast<cudaStream_t>(stream)));
+}
+
+hllm_b200_status hllm_b200_sample(const float* logits, uint32_t rows, uint64_t vocab, uint64_t ld,
+                                  const hllm_b200_sampling* options,
+                                  const uint64_t* generated_index, hllm_b200_sampled* out,
+                                  void* stream) {
+  if (!logits || !options || !out || rows == 0 || vocab == 0 || ld < vocab)
+    return HLLM_B200_INVALID_REQUEST;
+  for (uint32_t i = 0; i < rows; ++i) {
+    const auto& o = options[i];
+    if (!std::isfinite(o.temperature) || o.temperature < 0.0 || o.temperature > 100.0 ||
+        !std::isfinite(o.top_p) || o.top_p <= 0.0 || o.top_p > 1.0 || o.top_logprobs > 5U ||
+        (!o.return_logprobs && o.top_logprobs != 0U)) {
+      set_error("invalid sampling parameters");
+      return HLLM_B200_INVALID_REQUEST;
+    }
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<hb::SampleParams> params(rows);
+  for (uint32_t i = 0; i < rows; ++i)
+    params[i] = hb::SampleParams{options[i].temperature, options[i].top_p, options[i].top_k,
+                                 options[i].seed, generated_index ? generated_index[i] : 0,
+                                 options[i].return_logprobs, options[i].top_logprobs};
+  hb::SampleParams* dp = nullptr;
+  hb::SampleResult* dr = nullptr;
+  double* scratch = nullptr;
+  uint32_t* status = nullptr;
+  cudaError_t e = cudaMalloc(&dp, rows * sizeof(hb::SampleParams));
+  if (e == cudaSuccess) e = cudaMalloc(&dr, rows * sizeof(hb::SampleResult));
+  if (e == cudaSuccess) e = cudaMalloc(&scratch, static_cast<size_t>(rows) * vocab * sizeof(double));
+  if (e == cudaSuccess) e = cudaMalloc(&status, 4);
+  if (e == cudaSuccess) e = cudaMemsetAsync(status, 0, 4, st);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(dp, params.data(), rows * sizeof(hb::SampleParams), cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess)
+    e = hb::sample_launch(logits, static_cast<int>(rows), static_cast<int>(vocab),
+                          static_cast<int>(ld), dp, scratch, dr, status, st);
+  std::vector<hb::SampleResult> res(rows);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(res.data(), dr, rows * sizeof(hb::SampleResult), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  cudaFree(dp);
+  cudaFree(dr);
+  cudaFree(scratch);
+  cudaFree(status);
+  if (e != cudaSuccess) return cuda_status(e);
+  hllm_b200_status code = HLLM_B200_OK;
+  for (uint32_t i = 0; i < rows; ++i) {
+    out[i].token_id = static_cast<uint64_t>(res[i].token);
+    out[i].logprob = res[i].logprob;
+    out[i].has_logprob = options[i].return_logprobs ? 1u : 0u;
+    out[i].n_top = static_cast<uint32_t>(res[i].n_top);
+    for (int k = 0; k < 5; ++k) {
+      out[i].top_ids[k] = static_cast<uint64_t>(res[i].top_ids[k]);
+      out[i].top_logprobs[k] = res[i].top_logprobs[k];
+    }
+    if (res[i].status != 0) {
+      set_error("cannot sample nonfinite logits");
+      code = HLLM_B200_INTERNAL;
+    }
+  }
+  return code;
+}
+
+hllm_b200_status hllm_b200_synth_matrix(uint64_t seed, uint64_t tag, uint64_t rows, uint64_t cols,
+                                        uint64_t ld, float stddev, uint16_t* out, void* stream) {
+  return cuda_status(hb::synth_matrix_launch(seed, tag, static_cast<int>(rows),
+                                             static_cast<int>(cols), static_cast<int>(ld), stddev,
+                                             reinterpret_cast<__half*>(out),
+                                             static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

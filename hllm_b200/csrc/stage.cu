@@ -1,0 +1,1067 @@
+// stage.cu -- the B200 stage executor behind the C ABI in include/hllm_b200.h.
+//
+// Host side of one hLLM stage: weight upload and seeded initialisation, the
+// paged KV pool and its block allocator, per-sequence block lists, and the
+// per-step launch sequence
+//
+//   H2D(row descriptors, ids) -> pack -> embed | boundary-in
+//   per layer: rmsnorm -> QKV GEMM -> q/k-norm+RoPE+KV write -> attention
+//              -> O GEMM (+residual) -> rmsnorm -> gate/up GEMM (SwiGLU)
+//              -> down GEMM (+residual)
+//   final stage: last-row gather + final norm -> LM-head GEMM -> sampler
+//   other stages: F16 boundary
+//   D2H(status, sampled tokens | boundary)
+//
+// which restates, in one ragged pass, what the reference CUDA stage does per
+// sequence (cpp/src/cuda/stage.cpp:340-470) and the CPU oracle defines
+// (cpp/src/cpu/stage.cpp:129-191, cpp/src/cpu/llama.cpp:242-308).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <new>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "hllm_b200.h"
+#include "kernels.cuh"
+#include "sampler.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Fail {
+  hllm_b200_status code;
+  std::string message;
+};
+[[noreturn]] void fail(hllm_b200_status code, const std::string& message) {
+  throw Fail{code, message};
+}
+void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    if (e == cudaErrorMemoryAllocation)
+      fail(HLLM_B200_RESOURCE_EXHAUSTED, std::string(what) + ": device memory exhausted");
+    fail(HLLM_B200_INTERNAL, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+template <class F>
+hllm_b200_status guarded(F&& f) {
+  try {
+    f();
+    return HLLM_B200_OK;
+  } catch (const Fail& e) {
+    g_last_error = e.message;
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    g_last_error = "host allocation failed";
+    return HLLM_B200_RESOURCE_EXHAUSTED;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return HLLM_B200_INTERNAL;
+  }
+}
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+constexpr uint32_t kInputNonFinite = hb::kDevNonFiniteInput;
+
+struct DeviceBuffer {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  DeviceBuffer() = default;
+  DeviceBuffer(const DeviceBuffer&) = delete;
+  DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+  ~DeviceBuffer() {
+    if (ptr) cudaFree(ptr);
+  }
+};
+
+struct Layer {
+  __half* qkv = nullptr;      // [Hq d + 2 Hkv d][h_pad]
+  __half* o = nullptr;        // [h][qw_pad]
+  __half* gate_up = nullptr;  // [2I][h_pad]: gate rows then up rows
+  __half* down = nullptr;     // [h][I_pad]
+  float* in_norm = nullptr;
+  float* post_norm = nullptr;
+  float* q_norm = nullptr;
+  float* k_norm = nullptr;
+  hb::GemmWeight g_qkv{}, g_o{}, g_gu{}, g_down{};
+};
+
+// Where a named tensor lands on the device.
+struct Target {
+  enum Kind { kMatrix, kNorm } kind;
+  __half* matrix = nullptr;  // base of the destination matrix
+  size_t row_offset = 0;     // first destination row
+  size_t ld = 0;             // destination row stride (elements)
+  float* norm = nullptr;
+  size_t rows = 0, cols = 0;  // expected source shape
+  uint64_t tag = 0;           // synthetic-weight tag
+};
+
+}  // namespace
+
+namespace hb {
+void set_last_error(const std::string& message) { g_last_error = message; }
+}  // namespace hb
+
+struct hllm_b200_seq {
+  hllm_b200_stage* owner = nullptr;
+  int slot = -1;
+  std::vector<int32_t> blocks;
+  uint64_t capacity = 0;
+  uint64_t length = 0;
+  bool failed = false;
+};
+
+struct hllm_b200_stage {
+  hllm_b200_stage_desc desc{};
+  int device = 0;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  size_t h = 0, I = 0, hq = 0, hkv = 0, dim = 0, qw = 0, kw = 0, qkvw = 0, V = 0;
+  size_t h_pad = 0, qw_pad = 0, I_pad = 0;
+  size_t n_layers = 0;
+  size_t max_blocks = 0, num_blocks = 0;
+  size_t T_max = 0, R_max = 0, max_seqs = 0, max_splits = 0;
+  size_t weight_bytes = 0, workspace_bytes = 0;
+  std::vector<std::unique_ptr<DeviceBuffer>> owned;
+
+  __half* embed = nullptr;
+  __half* head = nullptr;
+  float* final_norm = nullptr;
+  std::vector<Layer> layers;
+  hb::GemmWeight g_head{};
+  __half* kv = nullptr;  // [layers][2][blocks][Hkv][16][d]
+  size_t kv_layer_elems = 0;
+  float* rope_pow = nullptr;
+
+  // per-step device tensors
+  int32_t* up = nullptr;  // row_slot | row_first | row_count | sample_rows | ids
+  hb::SampleParams* d_params = nullptr;
+  size_t up_bytes = 0;
+  int32_t *row_slot = nullptr, *row_first = nullptr, *row_count = nullptr, *sample_rows = nullptr,
+          *ids = nullptr;
+  int32_t *cu_seqlens = nullptr, *positions = nullptr, *slot_mapping = nullptr,
+          *token_row = nullptr, *seq_lens = nullptr, *block_tables = nullptr,
+          *cu_splits = nullptr, *cu_qtiles = nullptr, *last_idx = nullptr;
+  int32_t* slot_blocks = nullptr;  // [max_seqs][max_blocks]
+  uint8_t* down = nullptr;         // status (8 bytes) | SampleResult[R_max]
+  uint32_t* status = nullptr;
+  hb::SampleResult* results = nullptr;
+  float* hidden = nullptr;
+  __half *xn = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *xs = nullptr,
+         *bin = nullptr, *bout = nullptr;
+  float* qkv = nullptr;
+  float* logits = nullptr;
+  double* sample_scratch = nullptr;
+  float *part_o = nullptr, *part_ml = nullptr;
+  hb::GemmInput in_xn{}, in_attn{}, in_act{}, in_xs{};
+  hb::GemmScratch gscratch{};
+
+  // pinned host staging
+  uint8_t* h_up = nullptr;
+  uint8_t* h_down = nullptr;
+  __half* h_act = nullptr;  // boundary in/out staging [T_max][h]
+
+  std::map<std::string, Target> targets;
+  std::set<std::string> loaded;
+  bool finalized = false;
+  std::vector<int32_t> free_blocks;
+  std::vector<int> free_slots;
+  std::set<hllm_b200_seq*> live;
+  uint32_t launches = 0;
+  uint32_t last_samples = 0;
+  uint64_t last_tokens = 0;
+  std::vector<hllm_b200_seq*> pending;  // sequences of steps enqueued since the last sync
+  std::mutex mutex;
+
+  ~hllm_b200_stage() {
+    if (stream) {
+      cudaStreamSynchronize(stream);
+      cudaStreamDestroy(stream);
+    }
+    if (h_up) cudaFreeHost(h_up);
+    if (h_down) cudaFreeHost(h_down);
+    if (h_act) cudaFreeHost(h_act);
+    for (auto* s : live) delete s;
+  }
+
+  template <class T>
+  T* alloc(size_t count, bool track_weight = false) {
+    auto b = std::make_unique<DeviceBuffer>();
+    b->bytes = std::max<size_t>(count * sizeof(T), 256);
+    check_cuda(cudaMalloc(&b->ptr, b->bytes), "cudaMalloc");
+    check_cuda(cudaMemsetAsync(b->ptr, 0, b->bytes, stream), "cudaMemset");
+    if (track_weight) weight_bytes += b->bytes;
+    else workspace_bytes += b->bytes;
+    T* p = static_cast<T*>(b->ptr);
+    owned.push_back(std::move(b));
+    return p;
+  }
+};
+
+namespace {
+
+constexpr uint64_t kTagEmbed = 0xE0000, kTagHead = 0xE0001, kTagFinalNorm = 0xE0002;
+constexpr float kWeightStd = 0.02f, kNormSpread = 0.1f;
+
+void add_matrix(hllm_b200_stage* s, const std::string& name, __half* base, size_t row_offset,
+                size_t ld, size_t rows, size_t cols, uint64_t tag) {
+  Target t{Target::kMatrix};
+  t.matrix = base;
+  t.row_offset = row_offset;
+  t.ld = ld;
+  t.rows = rows;
+  t.cols = cols;
+  t.tag = tag;
+  s->targets[name] = t;
+}
+void add_norm(hllm_b200_stage* s, const std::string& name, float* dst, size_t n, uint64_t tag) {
+  Target t{Target::kNorm};
+  t.norm = dst;
+  t.rows = n;
+  t.cols = 1;
+  t.tag = tag;
+  s->targets[name] = t;
+}
+
+void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
+  s->desc = d;
+  if (d.hidden_size == 0 || d.intermediate_size == 0 || d.attention_heads == 0 ||
+      d.key_value_heads == 0 || d.head_dimension == 0 || d.maximum_sequence_length == 0 ||
+      d.vocabulary_size == 0 || !(d.rms_norm_epsilon > 0.f) || !(d.rope_theta > 0.f) ||
+      !std::isfinite(d.rms_norm_epsilon) || !std::isfinite(d.rope_theta))
+    fail(HLLM_B200_INVALID_REQUEST, "stage configuration values must be positive");
+  if (d.attention_heads % d.key_value_heads != 0 || d.head_dimension % 4 != 0 ||
+      d.head_dimension > 256 || d.attention_heads / d.key_value_heads > 8)
+    fail(HLLM_B200_INCOMPATIBLE_WORKER,
+         "attention geometry unsupported (head_dim % 4, head_dim <= 256, group <= 8)");
+  if (d.layer_end < d.layer_start) fail(HLLM_B200_INVALID_REQUEST, "invalid layer range");
+  if (d.hidden_size > (1u << 20) || d.vocabulary_size > (1u << 30) ||
+      d.maximum_sequence_length > (1u << 24))
+    fail(HLLM_B200_INCOMPATIBLE_WORKER, "stage dimensions exceed executor limits");
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess) count = 0;
+  if (d.device_id < 0 || d.device_id >= count)
+    fail(HLLM_B200_INCOMPATIBLE_WORKER, "no such CUDA device");
+  s->device = d.device_id;
+  check_cuda(cudaSetDevice(s->device), "cudaSetDevice");
+  cudaDeviceProp prop{};
+  check_cuda(cudaGetDeviceProperties(&prop, s->device), "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    fail(HLLM_B200_INCOMPATIBLE_WORKER, "the B200 executor needs an sm_100 device");
+  s->sm_count = prop.multiProcessorCount;
+  check_cuda(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+
+  s->h = d.hidden_size;
+  s->I = d.intermediate_size;
+  s->hq = d.attention_heads;
+  s->hkv = d.key_value_heads;
+  s->dim = d.head_dimension;
+  s->qw = s->hq * s->dim;
+  s->kw = s->hkv * s->dim;
+  s->qkvw = s->qw + 2 * s->kw;
+  s->V = d.vocabulary_size;
+  s->h_pad = round_up(s->h, 64);
+  s->qw_pad = round_up(s->qw, 64);
+  s->I_pad = round_up(s->I, 64);
+  s->n_layers = d.layer_end - d.layer_start;
+  s->max_blocks = (d.maximum_sequence_length + hb::kBlockTokens - 1) / hb::kBlockTokens;
+  s->num_blocks = std::max<uint64_t>(1, (d.kv_pool_tokens + hb::kBlockTokens - 1) / hb::kBlockTokens);
+  s->T_max = d.max_step_tokens ? d.max_step_tokens : 2048;
+  s->R_max = d.max_step_rows ? d.max_step_rows : 256;
+  s->max_seqs = d.max_sequences ? d.max_sequences : 512;
+  s->max_splits = std::max<size_t>(4096, 2 * s->R_max);
+  if (s->R_max > s->T_max) s->R_max = s->T_max;
+
+  // ---- weights
+  if (d.first || (d.final && d.tied_head)) {
+    s->embed = s->alloc<__half>(s->V * s->h_pad, true);
+    add_matrix(s, "model.embed_tokens.weight", s->embed, 0, s->h_pad, s->V, s->h, kTagEmbed);
+  }
+  if (d.final) {
+    s->final_norm = s->alloc<float>(s->h, true);
+    add_norm(s, "model.norm.weight", s->final_norm, s->h, kTagFinalNorm);
+    if (!d.tied_head) {
+      s->head = s->alloc<__half>(s->V * s->h_pad, true);
+      add_matrix(s, "lm_head.weight", s->head, 0, s->h_pad, s->V, s->h, kTagHead);
+    }
+  }
+  s->layers.resize(s->n_layers);
+  for (size_t li = 0; li < s->n_layers; ++li) {
+    const size_t gl = d.layer_start + li;
+    Layer& L = s->layers[li];
+    const std::string p = "model.layers." + std::to_string(gl) + ".";
+    const uint64_t tb = gl * 16;
+    L.in_norm = s->alloc<float>(s->h, true);
+    L.post_norm = s->alloc<float>(s->h, true);
+    L.qkv = s->alloc<__half>(s->qkvw * s->h_pad, true);
+    L.o = s->alloc<__half>(s->h * s->qw_pad, true);
+    L.gate_up = s->alloc<__half>(2 * s->I * s->h_pad, true);
+    L.down = s->alloc<__half>(s->h * s->I_pad, true);
+    add_norm(s, p + "input_layernorm.weight", L.in_norm, s->h, tb + 0);
+    add_matrix(s, p + "self_attn.q_proj.weight", L.qkv, 0, s->h_pad, s->qw, s->h, tb + 1);
+    add_matrix(s, p + "self_attn.k_proj.weight", L.qkv, s->qw, s->h_pad, s->kw, s->h, tb + 2);
+    add_matrix(s, p + "self_attn.v_proj.weight", L.qkv, s->qw + s->kw, s->h_pad, s->kw, s->h,
+               tb + 3);
+    add_matrix(s, p + "self_attn.o_proj.weight", L.o, 0, s->qw_pad, s->h, s->qw, tb + 4);
+    add_norm(s, p + "post_attention_layernorm.weight", L.post_norm, s->h, tb + 5);
+    add_matrix(s, p + "mlp.gate_proj.weight", L.gate_up, 0, s->h_pad, s->I, s->h, tb + 6);
+    add_matrix(s, p + "mlp.up_proj.weight", L.gate_up, s->I, s->h_pad, s->I, s->h, tb + 7);
+    add_matrix(s, p + "mlp.down_proj.weight", L.down, 0, s->I_pad, s->h, s->I, tb + 8);
+    if (d.query_key_norm) {
+      L.q_norm = s->alloc<float>(s->dim, true);
+      L.k_norm = s->alloc<float>(s->dim, true);
+      add_norm(s, p + "self_attn.q_norm.weight", L.q_norm, s->dim, tb + 9);
+      add_norm(s, p + "self_attn.k_norm.weight", L.k_norm, s->dim, tb + 10);
+    }
+    if (!hb::gemm_make_weight(&L.g_qkv, L.qkv, static_cast<int>(s->qkvw), static_cast<int>(s->qkvw),
+                              static_cast<int>(s->h_pad), 1, 0) ||
+        !hb::gemm_make_weight(&L.g_o, L.o, static_cast<int>(s->h), static_cast<int>(s->h),
+                              static_cast<int>(s->qw_pad), 1, 0) ||
+        !hb::gemm_make_weight(&L.g_gu, L.gate_up, static_cast<int>(2 * s->I),
+                              static_cast<int>(s->I), static_cast<int>(s->h_pad), 2,
+                              static_cast<int>(s->I)) ||
+        !hb::gemm_make_weight(&L.g_down, L.down, static_cast<int>(s->h), static_cast<int>(s->h),
+                              static_cast<int>(s->I_pad), 1, 0))
+      fail(HLLM_B200_INTERNAL, "tensor map creation failed");
+  }
+  if (d.final) {
+    const __half* hm = d.tied_head ? s->embed : s->head;
+    if (!hb::gemm_make_weight(&s->g_head, hm, static_cast<int>(s->V), static_cast<int>(s->V),
+                              static_cast<int>(s->h_pad), 1, 0))
+      fail(HLLM_B200_INTERNAL, "tensor map creation failed");
+  }
+
+  // ---- KV pool and sequence tables
+  s->kv_layer_elems = 2 * s->num_blocks * s->hkv * hb::kBlockTokens * s->dim;
+  s->kv = s->alloc<__half>(std::max<size_t>(1, s->n_layers) * s->kv_layer_elems);
+  s->slot_blocks = s->alloc<int32_t>(s->max_seqs * s->max_blocks);
+  for (size_t b = s->num_blocks; b-- > 0;) s->free_blocks.push_back(static_cast<int32_t>(b));
+  for (size_t i = s->max_seqs; i-- > 0;) s->free_slots.push_back(static_cast<int>(i));
+
+  // RoPE divisors theta^(2i/d), computed on the host with the reference's
+  // F32 expression (cpp/src/cpu/llama.cpp:225-228).
+  std::vector<float> pw(s->dim / 2);
+  for (size_t i = 0; i < pw.size(); ++i)
+    pw[i] = std::pow(d.rope_theta,
+                     static_cast<float>(2U * i) / static_cast<float>(s->dim));
+  s->rope_pow = s->alloc<float>(pw.size());
+  check_cuda(cudaMemcpyAsync(s->rope_pow, pw.data(), pw.size() * sizeof(float),
+                             cudaMemcpyHostToDevice, s->stream), "rope upload");
+
+  // ---- step workspaces
+  const size_t R = s->R_max, T = s->T_max;
+  s->up_bytes = (4 * R + T) * sizeof(int32_t);
+  s->up_bytes = round_up(s->up_bytes, 16) + R * sizeof(hb::SampleParams);
+  s->up = s->alloc<int32_t>(s->up_bytes / sizeof(int32_t) + 4);
+  s->row_slot = s->up;
+  s->row_first = s->up + R;
+  s->row_count = s->up + 2 * R;
+  s->sample_rows = s->up + 3 * R;
+  s->ids = s->up + 4 * R;
+  s->d_params = reinterpret_cast<hb::SampleParams*>(
+      reinterpret_cast<uint8_t*>(s->up) + round_up((4 * R + T) * sizeof(int32_t), 16));
+  s->cu_seqlens = s->alloc<int32_t>(R + 1);
+  s->positions = s->alloc<int32_t>(T);
+  s->slot_mapping = s->alloc<int32_t>(T);
+  s->token_row = s->alloc<int32_t>(T);
+  s->seq_lens = s->alloc<int32_t>(R);
+  s->block_tables = s->alloc<int32_t>(R * s->max_blocks);
+  s->cu_splits = s->alloc<int32_t>(R + 1);
+  s->cu_qtiles = s->alloc<int32_t>(R + 1);
+  s->last_idx = s->alloc<int32_t>(R);
+  s->down = s->alloc<uint8_t>(8 + R * sizeof(hb::SampleResult));
+  s->status = reinterpret_cast<uint32_t*>(s->down);
+  s->results = reinterpret_cast<hb::SampleResult*>(s->down + 8);
+  s->hidden = s->alloc<float>(T * s->h);
+  s->xn = s->alloc<__half>(T * s->h_pad);
+  s->qkv = s->alloc<float>(T * s->qkvw);
+  s->q = s->alloc<__half>(T * s->qw);
+  s->attn = s->alloc<__half>(T * s->qw_pad);
+  s->act = s->alloc<__half>(T * s->I_pad);
+  s->bin = s->alloc<__half>(T * s->h);
+  s->bout = s->alloc<__half>(T * s->h);
+  if (d.final) {
+    s->xs = s->alloc<__half>(R * s->h_pad);
+    s->logits = s->alloc<float>(R * s->V);
+    s->sample_scratch = s->alloc<double>(R * s->V);
+  }
+  s->part_o = s->alloc<float>(s->max_splits * s->hq * s->dim);
+  s->part_ml = s->alloc<float>(s->max_splits * s->hq * 2);
+  s->gscratch.sm_count = s->sm_count;
+  s->gscratch.partial_floats = hb::gemm_partial_floats(s->sm_count);
+  s->gscratch.partials = s->alloc<float>(s->gscratch.partial_floats);
+  const size_t max_m = std::max({s->V, s->qkvw, 2 * s->I, s->h});
+  s->gscratch.counter_count = hb::gemm_counter_count(static_cast<int>(max_m), static_cast<int>(T));
+  s->gscratch.counters = s->alloc<unsigned>(s->gscratch.counter_count);
+  s->gscratch.status = s->status;
+  if (!hb::gemm_make_input(&s->in_xn, s->xn, static_cast<int>(T), static_cast<int>(s->h_pad),
+                           static_cast<int>(s->h_pad)) ||
+      !hb::gemm_make_input(&s->in_attn, s->attn, static_cast<int>(T), static_cast<int>(s->qw_pad),
+                           static_cast<int>(s->qw_pad)) ||
+      !hb::gemm_make_input(&s->in_act, s->act, static_cast<int>(T), static_cast<int>(s->I_pad),
+                           static_cast<int>(s->I_pad)) ||
+      (d.final && !hb::gemm_make_input(&s->in_xs, s->xs, static_cast<int>(R),
+                                       static_cast<int>(s->h_pad), static_cast<int>(s->h_pad))))
+    fail(HLLM_B200_INTERNAL, "tensor map creation failed");
+
+  check_cuda(cudaMallocHost(&s->h_up, s->up_bytes), "cudaMallocHost");
+  check_cuda(cudaMallocHost(&s->h_down, 8 + R * sizeof(hb::SampleResult)), "cudaMallocHost");
+  check_cuda(cudaMallocHost(&s->h_act, T * s->h * sizeof(__half)), "cudaMallocHost");
+  check_cuda(cudaStreamSynchronize(s->stream), "stage setup");
+}
+
+void check_finite_f16(const std::vector<__half>& v, const std::string& name) {
+  for (const auto x : v)
+    if ((__half_as_ushort(x) & 0x7c00u) == 0x7c00u)
+      fail(HLLM_B200_INCOMPATIBLE_WORKER, "weight is not representable as finite F16: " + name);
+}
+
+float source_float(hllm_b200_dtype dt, const void* data, size_t i) {
+  switch (dt) {
+    case HLLM_B200_F32: return static_cast<const float*>(data)[i];
+    case HLLM_B200_F16: return __half2float(__ushort_as_half(static_cast<const uint16_t*>(data)[i]));
+    default: {
+      const uint32_t b = static_cast<uint32_t>(static_cast<const uint16_t*>(data)[i]) << 16;
+      float f;
+      std::memcpy(&f, &b, 4);
+      return f;
+    }
+  }
+}
+
+void load_tensor(hllm_b200_stage* s, const char* name, hllm_b200_dtype dt, const void* data,
+                 const uint64_t* shape, uint32_t rank) {
+  if (s->finalized) fail(HLLM_B200_INVALID_REQUEST, "stage already finalized");
+  if (!name || !data || !shape) fail(HLLM_B200_INVALID_REQUEST, "null tensor argument");
+  const auto it = s->targets.find(name);
+  if (it == s->targets.end())
+    fail(HLLM_B200_INVALID_REQUEST, std::string("tensor is not part of this stage: ") + name);
+  const Target& t = it->second;
+  const bool ok_shape = t.kind == Target::kNorm ? (rank == 1 && shape[0] == t.rows)
+                                                : (rank == 2 && shape[0] == t.rows && shape[1] == t.cols);
+  if (!ok_shape) fail(HLLM_B200_INVALID_REQUEST, std::string("tensor shape mismatch: ") + name);
+  if (dt != HLLM_B200_F32 && dt != HLLM_B200_F16 && dt != HLLM_B200_BF16)
+    fail(HLLM_B200_INCOMPATIBLE_WORKER, "unsupported tensor dtype");
+  check_cuda(cudaSetDevice(s->device), "cudaSetDevice");
+  if (t.kind == Target::kNorm) {
+    std::vector<float> v(t.rows);
+    for (size_t i = 0; i < t.rows; ++i) v[i] = source_float(dt, data, i);
+    std::vector<__half> hv(t.rows);
+    for (size_t i = 0; i < t.rows; ++i) hv[i] = __float2half_rn(v[i]);
+    check_finite_f16(hv, name);
+    check_cuda(cudaMemcpy(t.norm, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice),
+               "norm upload");
+  } else {
+    const size_t n = t.rows * t.cols;
+    std::vector<__half> hv(n);
+    if (dt == HLLM_B200_F16) std::memcpy(hv.data(), data, n * sizeof(__half));
+    else
+      for (size_t i = 0; i < n; ++i) hv[i] = __float2half_rn(source_float(dt, data, i));
+    check_finite_f16(hv, name);
+    check_cuda(cudaMemcpy2D(t.matrix + t.row_offset * t.ld, t.ld * sizeof(__half), hv.data(),
+                            t.cols * sizeof(__half), t.cols * sizeof(__half), t.rows,
+                            cudaMemcpyHostToDevice),
+               "weight upload");
+  }
+  s->loaded.insert(name);
+}
+
+void init_synthetic(hllm_b200_stage* s, uint64_t seed) {
+  if (s->finalized) fail(HLLM_B200_INVALID_REQUEST, "stage already finalized");
+  check_cuda(cudaSetDevice(s->device), "cudaSetDevice");
+  for (const auto& [name, t] : s->targets) {
+    if (t.kind == Target::kNorm) {
+      check_cuda(hb::synth_norm_launch(seed, t.tag, static_cast<int>(t.rows), kNormSpread, t.norm,
+                                       s->stream), "synth");
+    } else {
+      check_cuda(hb::synth_matrix_launch(seed, t.tag, static_cast<int>(t.rows),
+                                         static_cast<int>(t.cols), static_cast<int>(t.ld),
+                                         kWeightStd, t.matrix + t.row_offset * t.ld, s->stream),
+                 "synth");
+    }
+    s->loaded.insert(name);
+  }
+  check_cuda(cudaStreamSynchronize(s->stream), "synthetic init");
+}
+
+// ------------------------------------------------------------------ step
+struct StepPlan {
+  uint32_t rows = 0;
+  uint64_t tokens = 0;
+  uint32_t samples = 0;
+  int split_tokens = 16;
+  int total_splits = 0;
+  int total_qtiles = 0;
+  int qtile_tokens = 0;
+};
+
+void validate_sampling(const hllm_b200_sampling& o) {
+  if (!std::isfinite(o.temperature) || o.temperature < 0.0 || o.temperature > 100.0 ||
+      !std::isfinite(o.top_p) || o.top_p <= 0.0 || o.top_p > 1.0 || o.top_logprobs > 5U ||
+      (!o.return_logprobs && o.top_logprobs != 0U))
+    fail(HLLM_B200_INVALID_REQUEST, "invalid sampling parameters");
+}
+
+StepPlan plan_step(hllm_b200_stage* s, const hllm_b200_row* rows, uint32_t n, bool device_input) {
+  if (!s->finalized) fail(HLLM_B200_INVALID_REQUEST, "stage weights are not finalized");
+  if (n == 0 || !rows) fail(HLLM_B200_INVALID_REQUEST, "empty step");
+  if (n > s->R_max) fail(HLLM_B200_RESOURCE_EXHAUSTED, "step has more rows than max_step_rows");
+  StepPlan p;
+  p.rows = n;
+  std::set<const hllm_b200_seq*> seen;
+  uint64_t decode_keys = 0;
+  int decode_rows = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    const auto& r = rows[i];
+    const hllm_b200_seq* q = r.sequence;
+    if (!q || q->owner != s || !s->live.count(const_cast<hllm_b200_seq*>(q)) || q->failed ||
+        r.first_position != q->length)
+      fail(HLLM_B200_INVALID_REQUEST, "sequence state or position is invalid");
+    if (!seen.insert(q).second)
+      fail(HLLM_B200_INVALID_REQUEST, "a step requires distinct sequences");
+    if (r.tokens == 0 || r.first_position > q->capacity || r.tokens > q->capacity - r.first_position)
+      fail(HLLM_B200_INVALID_REQUEST, "invalid stage input or context capacity");
+    if (!device_input) {
+      if (s->desc.first && !r.token_ids)
+        fail(HLLM_B200_INVALID_REQUEST, "stage zero requires tokens");
+      if (!s->desc.first && !r.activations)
+        fail(HLLM_B200_INVALID_REQUEST, "only stage zero accepts tokens");
+      if (s->desc.first)
+        for (uint64_t k = 0; k < r.tokens; ++k)
+          if (r.token_ids[k] >= s->V) fail(HLLM_B200_INVALID_REQUEST, "token ID exceeds vocabulary");
+    }
+    if (r.sample && s->desc.final) {
+      validate_sampling(r.sampling);
+      ++p.samples;
+    }
+    p.tokens += r.tokens;
+    if (r.tokens == 1) {
+      decode_keys += r.first_position + 1;
+      ++decode_rows;
+    }
+  }
+  if (p.tokens > s->T_max) fail(HLLM_B200_RESOURCE_EXHAUSTED, "step exceeds max_step_tokens");
+  // Decode split size: enough context splits to cover ~2 CTAs per SM across
+  // the KV heads, at least 64 keys each, within the split workspace.
+  const uint64_t target = std::max<uint64_t>(1, (2ull * s->sm_count) / s->hkv);
+  uint64_t split = std::max<uint64_t>(64, round_up((decode_keys + target - 1) / target, 16));
+  auto count_splits = [&](uint64_t sp) {
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < n; ++i)
+      if (rows[i].tokens == 1) total += (rows[i].first_position + 1 + sp - 1) / sp;
+    return total;
+  };
+  while (count_splits(split) > s->max_splits) split *= 2;
+  p.split_tokens = static_cast<int>(std::min<uint64_t>(split, 1u << 30));
+  p.total_splits = static_cast<int>(count_splits(split));
+  p.qtile_tokens = hb::attn_qtile_tokens(static_cast<int>(s->hq / s->hkv));
+  for (uint32_t i = 0; i < n; ++i)
+    if (rows[i].tokens > 1)
+      p.total_qtiles += static_cast<int>((rows[i].tokens + p.qtile_tokens - 1) / p.qtile_tokens);
+  (void)decode_rows;
+  return p;
+}
+
+#define LAUNCH(expr)                                    \
+  do {                                                  \
+    check_cuda((expr), #expr);                          \
+    ++s->launches;                                      \
+  } while (0)
+
+void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan& p,
+                  const void* device_input) {
+  const size_t R = s->R_max;
+  const int T = static_cast<int>(p.tokens);
+  s->launches = 0;
+  // ---- upload row descriptors (and ids / activations)
+  int32_t* hu = reinterpret_cast<int32_t*>(s->h_up);
+  int t = 0;
+  uint32_t si = 0;
+  auto* hp = reinterpret_cast<hb::SampleParams*>(
+      s->h_up + round_up((4 * R + s->T_max) * sizeof(int32_t), 16));
+  for (uint32_t i = 0; i < p.rows; ++i) {
+    const auto& r = rows[i];
+    hu[i] = r.sequence->slot;
+    hu[R + i] = static_cast<int32_t>(r.first_position);
+    hu[2 * R + i] = static_cast<int32_t>(r.tokens);
+    if (r.sample && s->desc.final) {
+      hu[3 * R + si] = static_cast<int32_t>(i);
+      hp[si] = hb::SampleParams{r.sampling.temperature, r.sampling.top_p, r.sampling.top_k,
+                                r.sampling.seed, r.generated_index, r.sampling.return_logprobs,
+                                r.sampling.top_logprobs};
+      ++si;
+    }
+    if (!device_input) {
+      if (s->desc.first) {
+        for (uint64_t k = 0; k < r.tokens; ++k) hu[4 * R + t + k] = static_cast<int32_t>(r.token_ids[k]);
+      } else {
+        std::memcpy(s->h_act + static_cast<size_t>(t) * s->h, r.activations,
+                    r.tokens * s->h * sizeof(__half));
+      }
+    }
+    t += static_cast<int>(r.tokens);
+  }
+  check_cuda(cudaMemcpyAsync(s->up, s->h_up, s->up_bytes, cudaMemcpyHostToDevice, s->stream),
+             "descriptor upload");
+  if (s->desc.first && device_input)
+    check_cuda(cudaMemcpyAsync(s->ids, device_input, T * sizeof(int32_t),
+                               cudaMemcpyDeviceToDevice, s->stream), "id copy");
+  if (!s->desc.first)
+    check_cuda(cudaMemcpyAsync(s->bin, device_input ? device_input : s->h_act,
+                               static_cast<size_t>(T) * s->h * sizeof(__half),
+                               device_input ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                               s->stream), "activation upload");
+
+  // ---- pack
+  hb::StepTensors st{};
+  st.row_slot = s->row_slot;
+  st.row_first = s->row_first;
+  st.row_count = s->row_count;
+  st.cu_seqlens = s->cu_seqlens;
+  st.positions = s->positions;
+  st.slot_mapping = s->slot_mapping;
+  st.token_row = s->token_row;
+  st.seq_lens = s->seq_lens;
+  st.block_tables = s->block_tables;
+  st.cu_splits = s->cu_splits;
+  st.cu_qtiles = s->cu_qtiles;
+  st.rows = static_cast<int>(p.rows);
+  st.tokens = T;
+  st.max_blocks = static_cast<int>(s->max_blocks);
+  st.split_tokens = p.split_tokens;
+  st.qtile_tokens = p.qtile_tokens;
+  LAUNCH(hb::pack_launch(st, s->slot_blocks, s->status, s->stream));
+
+  // ---- input
+  if (s->desc.first) {
+    LAUNCH(hb::embed_launch(s->ids, T, s->embed, static_cast<int>(s->V), static_cast<int>(s->h),
+                            static_cast<int>(s->h_pad), s->hidden, s->status, s->stream));
+  } else {
+    LAUNCH(hb::boundary_in_launch(s->bin, T, static_cast<int>(s->h), s->hidden, s->status,
+                                  s->stream));
+  }
+
+  // ---- layers
+  const float eps = s->desc.rms_norm_epsilon;
+  const int h = static_cast<int>(s->h);
+  for (size_t li = 0; li < s->n_layers; ++li) {
+    const Layer& L = s->layers[li];
+    __half* kc = s->kv + li * s->kv_layer_elems;
+    __half* vc = kc + s->kv_layer_elems / 2;
+    LAUNCH(hb::rmsnorm_launch(s->hidden, T, h, L.in_norm, eps, s->xn, static_cast<int>(s->h_pad),
+                              nullptr, s->stream));
+    LAUNCH(hb::gemm_run(L.g_qkv, s->in_xn, T, hb::kEpiStoreF32, s->qkv, static_cast<int>(s->qkvw),
+                        s->gscratch, s->stream));
+    hb::QkvPostArgs qa{};
+    qa.qkv = s->qkv;
+    qa.tokens = T;
+    qa.hq = static_cast<int>(s->hq);
+    qa.hkv = static_cast<int>(s->hkv);
+    qa.dim = static_cast<int>(s->dim);
+    qa.positions = s->positions;
+    qa.slot_mapping = s->slot_mapping;
+    qa.q_norm = L.q_norm;
+    qa.k_norm = L.k_norm;
+    qa.eps = eps;
+    qa.rope_pow = s->rope_pow;
+    qa.q_out = s->q;
+    qa.k_cache = kc;
+    qa.v_cache = vc;
+    LAUNCH(hb::qkv_post_launch(qa, s->stream));
+    hb::AttnArgs aa{};
+    aa.q = s->q;
+    aa.k_cache = kc;
+    aa.v_cache = vc;
+    aa.row_count = s->row_count;
+    aa.row_first = s->row_first;
+    aa.cu_seqlens = s->cu_seqlens;
+    aa.seq_lens = s->seq_lens;
+    aa.block_tables = s->block_tables;
+    aa.cu_splits = s->cu_splits;
+    aa.cu_qtiles = s->cu_qtiles;
+    aa.rows = static_cast<int>(p.rows);
+    aa.hq = static_cast<int>(s->hq);
+    aa.hkv = static_cast<int>(s->hkv);
+    aa.dim = static_cast<int>(s->dim);
+    aa.max_blocks = static_cast<int>(s->max_blocks);
+    aa.split_tokens = p.split_tokens;
+    aa.qtile_tokens = p.qtile_tokens;
+    aa.scale = 1.0f / std::sqrt(static_cast<float>(s->dim));
+    aa.part_o = s->part_o;
+    aa.part_ml = s->part_ml;
+    aa.out = s->attn;
+    aa.ld_out = static_cast<int>(s->qw_pad);
+    aa.status = s->status;
+    if (p.total_splits) {
+      LAUNCH(hb::attn_decode_launch(aa, p.total_splits, s->stream));
+      ++s->launches;  // combine pass
+    }
+    if (p.total_qtiles) LAUNCH(hb::attn_prefill_launch(aa, p.total_qtiles, s->stream));
+    LAUNCH(hb::gemm_run(L.g_o, s->in_attn, T, hb::kEpiResidual, s->hidden, h, s->gscratch,
+                        s->stream));
+    LAUNCH(hb::rmsnorm_launch(s->hidden, T, h, L.post_norm, eps, s->xn,
+                              static_cast<int>(s->h_pad), nullptr, s->stream));
+    LAUNCH(hb::gemm_run(L.g_gu, s->in_xn, T, hb::kEpiSwiGLU, s->act, static_cast<int>(s->I_pad),
+                        s->gscratch, s->stream));
+    LAUNCH(hb::gemm_run(L.g_down, s->in_act, T, hb::kEpiResidual, s->hidden, h, s->gscratch,
+                        s->stream));
+  }
+
+  // ---- output
+  if (s->desc.final) {
+    if (p.samples) {
+      const int S = static_cast<int>(p.samples);
+      LAUNCH(hb::last_token_launch(s->cu_seqlens, s->sample_rows, S, s->last_idx, s->stream));
+      LAUNCH(hb::rmsnorm_launch(s->hidden, S, h, s->final_norm, eps, s->xs,
+                                static_cast<int>(s->h_pad), s->last_idx, s->stream));
+      LAUNCH(hb::gemm_run(s->g_head, s->in_xs, S, hb::kEpiStoreF32, s->logits,
+                          static_cast<int>(s->V), s->gscratch, s->stream));
+      LAUNCH(hb::sample_launch(s->logits, S, static_cast<int>(s->V), static_cast<int>(s->V),
+                               s->d_params, s->sample_scratch, s->results, s->status, s->stream));
+    }
+  } else {
+    LAUNCH(hb::boundary_out_launch(s->hidden, T, h, s->bout, s->status, s->stream));
+  }
+  s->last_samples = p.samples;
+  s->last_tokens = p.tokens;
+}
+
+hllm_b200_status status_to_code(uint32_t bits, std::string* msg) {
+  if (bits == 0) return HLLM_B200_OK;
+  if (bits & kInputNonFinite) {
+    *msg = "non-finite activation";
+    return HLLM_B200_INVALID_REQUEST;
+  }
+  if (bits & hb::kDevWaitTimeout) *msg = "a device wait ran past its time limit";
+  else if (bits & hb::kDevBadIndex) *msg = "a device index was out of range";
+  else if (bits & hb::kDevNonFinite) *msg = "non-finite CUDA tensor";
+  else *msg = "device error";
+  return HLLM_B200_INTERNAL;
+}
+
+void mark_failed(const hllm_b200_row* rows, uint32_t n) {
+  for (uint32_t i = 0; i < n; ++i)
+    if (rows[i].sequence) rows[i].sequence->failed = true;
+}
+
+void copy_sampled(const hb::SampleResult& r, hllm_b200_sampled* o) {
+  o->token_id = static_cast<uint64_t>(r.token);
+  o->has_logprob = 0;
+  o->logprob = 0;
+  o->n_top = 0;
+  o->has_logprob = 0;
+  for (int k = 0; k < 5; ++k) {
+    o->top_ids[k] = static_cast<uint64_t>(r.top_ids[k]);
+    o->top_logprobs[k] = r.top_logprobs[k];
+  }
+  o->logprob = r.logprob;
+  o->n_top = static_cast<uint32_t>(r.n_top);
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+extern "C" {
+
+size_t hllm_b200_last_error(char* buffer, size_t size) {
+  if (buffer && size) {
+    const size_t n = std::min(size - 1, g_last_error.size());
+    std::memcpy(buffer, g_last_error.data(), n);
+    buffer[n] = 0;
+  }
+  return g_last_error.size();
+}
+
+hllm_b200_status hllm_b200_stage_create(const hllm_b200_stage_desc* desc, hllm_b200_stage** out) {
+  return guarded([&] {
+    if (!desc || !out) fail(HLLM_B200_INVALID_REQUEST, "null argument");
+    *out = nullptr;
+    auto s = std::make_unique<hllm_b200_stage>();
+    build_stage(s.get(), *desc);
+    *out = s.release();
+  });
+}
+
+void hllm_b200_stage_destroy(hllm_b200_stage* stage) {
+  if (!stage) return;
+  cudaSetDevice(stage->device);
+  delete stage;
+}
+
+hllm_b200_status hllm_b200_stage_load_tensor(hllm_b200_stage* stage, const char* name,
+                                             hllm_b200_dtype dtype, const void* data,
+                                             const uint64_t* shape, uint32_t rank) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    std::scoped_lock lock(stage->mutex);
+    load_tensor(stage, name, dtype, data, shape, rank);
+  });
+}
+
+hllm_b200_status hllm_b200_stage_init_synthetic(hllm_b200_stage* stage, uint64_t seed) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    std::scoped_lock lock(stage->mutex);
+    init_synthetic(stage, seed);
+  });
+}
+
+hllm_b200_status hllm_b200_stage_finalize(hllm_b200_stage* stage) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    std::scoped_lock lock(stage->mutex);
+    for (const auto& [name, t] : stage->targets)
+      if (!stage->loaded.count(name))
+        fail(HLLM_B200_INVALID_REQUEST, "missing tensor for stage: " + name);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    check_cuda(cudaDeviceSynchronize(), "finalize");
+    stage->finalized = true;
+  });
+}
+
+hllm_b200_status hllm_b200_stage_info(const hllm_b200_stage* stage, uint64_t* weight_device_bytes,
+                                      uint64_t* hidden_size, uint64_t* vocabulary_size,
+                                      uint64_t* maximum_tokens) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    if (weight_device_bytes) *weight_device_bytes = stage->weight_bytes;
+    if (hidden_size) *hidden_size = stage->h;
+    if (vocabulary_size) *vocabulary_size = stage->V;
+    if (maximum_tokens) *maximum_tokens = stage->desc.maximum_sequence_length;
+  });
+}
+
+hllm_b200_status hllm_b200_sequence_memory(const hllm_b200_stage* stage, uint64_t tokens,
+                                           uint64_t maximum_query_tokens,
+                                           uint64_t* cache_device_bytes,
+                                           uint64_t* workspace_device_bytes) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    if (tokens == 0 || tokens > stage->desc.maximum_sequence_length)
+      fail(HLLM_B200_INVALID_REQUEST, "request exceeds model context capacity");
+    const uint64_t rows = (maximum_query_tokens == 0 || maximum_query_tokens > tokens)
+                              ? tokens : maximum_query_tokens;
+    if (rows > stage->T_max)
+      fail(HLLM_B200_RESOURCE_EXHAUSTED, "prefill rows exceed max_step_tokens");
+    const uint64_t blocks = (tokens + hb::kBlockTokens - 1) / hb::kBlockTokens;
+    if (cache_device_bytes)
+      *cache_device_bytes = blocks * hb::kBlockTokens * stage->n_layers * stage->hkv *
+                            stage->dim * 2 * sizeof(__half);
+    if (workspace_device_bytes) *workspace_device_bytes = stage->workspace_bytes;
+  });
+}
+
+hllm_b200_status hllm_b200_seq_alloc(hllm_b200_stage* stage, uint64_t tokens, hllm_b200_seq** out) {
+  return guarded([&] {
+    if (!stage || !out) fail(HLLM_B200_INVALID_REQUEST, "null argument");
+    std::scoped_lock lock(stage->mutex);
+    *out = nullptr;
+    if (tokens == 0 || tokens > stage->desc.maximum_sequence_length)
+      fail(HLLM_B200_INVALID_REQUEST, "request exceeds model context capacity");
+    const size_t need = (tokens + hb::kBlockTokens - 1) / hb::kBlockTokens;
+    if (stage->free_slots.empty()) fail(HLLM_B200_RESOURCE_EXHAUSTED, "no free sequence slot");
+    if (stage->free_blocks.size() < need)
+      fail(HLLM_B200_RESOURCE_EXHAUSTED, "paged KV pool exhausted");
+    auto seq = std::make_unique<hllm_b200_seq>();
+    seq->owner = stage;
+    seq->capacity = tokens;
+    seq->slot = stage->free_slots.back();
+    seq->blocks.assign(stage->free_blocks.end() - static_cast<std::ptrdiff_t>(need),
+                       stage->free_blocks.end());
+    std::reverse(seq->blocks.begin(), seq->blocks.end());
+    std::vector<int32_t> row(stage->max_blocks, -1);
+    std::copy(seq->blocks.begin(), seq->blocks.end(), row.begin());
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    check_cuda(cudaMemcpyAsync(stage->slot_blocks + static_cast<size_t>(seq->slot) * stage->max_blocks,
+                               row.data(), row.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                               stage->stream),
+               "block table upload");
+    check_cuda(cudaStreamSynchronize(stage->stream), "block table upload");
+    stage->free_slots.pop_back();
+    stage->free_blocks.resize(stage->free_blocks.size() - need);
+    stage->live.insert(seq.get());
+    *out = seq.release();
+  });
+}
+
+void hllm_b200_seq_free(hllm_b200_stage* stage, hllm_b200_seq* seq) {
+  if (!stage || !seq || seq->owner != stage) return;
+  std::scoped_lock lock(stage->mutex);
+  if (!stage->live.erase(seq)) return;
+  for (auto it = seq->blocks.rbegin(); it != seq->blocks.rend(); ++it)
+    stage->free_blocks.push_back(*it);
+  stage->free_slots.push_back(seq->slot);
+  delete seq;
+}
+
+hllm_b200_status hllm_b200_seq_info(const hllm_b200_seq* seq, uint64_t* length, uint64_t* capacity,
+                                    uint32_t* failed) {
+  return guarded([&] {
+    if (!seq) fail(HLLM_B200_INVALID_REQUEST, "null sequence");
+    if (length) *length = seq->length;
+    if (capacity) *capacity = seq->capacity;
+    if (failed) *failed = seq->failed ? 1u : 0u;
+  });
+}
+
+hllm_b200_status hllm_b200_step(hllm_b200_stage* stage, const hllm_b200_row* rows, uint32_t n_rows,
+                                hllm_b200_sampled* sampled, uint16_t* boundary) {
+  bool enqueued = false;
+  const hllm_b200_status st = guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    std::scoped_lock lock(stage->mutex);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    const StepPlan p = plan_step(stage, rows, n_rows, false);
+    if (stage->desc.final && p.samples && !sampled)
+      fail(HLLM_B200_INVALID_REQUEST, "sampled output buffer required");
+    if (!stage->desc.final && !boundary)
+      fail(HLLM_B200_INVALID_REQUEST, "boundary output buffer required");
+    check_cuda(cudaMemsetAsync(stage->status, 0, sizeof(uint32_t), stage->stream), "status reset");
+    enqueued = true;
+    enqueue_step(stage, rows, p, nullptr);
+    const size_t down_bytes = 8 + p.samples * sizeof(hb::SampleResult);
+    check_cuda(cudaMemcpyAsync(stage->h_down, stage->down, down_bytes, cudaMemcpyDeviceToHost,
+                               stage->stream), "result download");
+    if (!stage->desc.final)
+      check_cuda(cudaMemcpyAsync(stage->h_act, stage->bout, p.tokens * stage->h * sizeof(__half),
+                                 cudaMemcpyDeviceToHost, stage->stream), "boundary download");
+    check_cuda(cudaStreamSynchronize(stage->stream), "step");
+    uint32_t bits;
+    std::memcpy(&bits, stage->h_down, sizeof(bits));
+    std::string msg;
+    const hllm_b200_status code = status_to_code(bits, &msg);
+    if (code != HLLM_B200_OK) fail(code, msg);
+    if (stage->desc.final) {
+      const auto* res = reinterpret_cast<const hb::SampleResult*>(stage->h_down + 8);
+      for (uint32_t i = 0; i < p.samples; ++i) copy_sampled(res[i], &sampled[i]);
+    } else {
+      std::memcpy(boundary, stage->h_act, p.tokens * stage->h * sizeof(__half));
+    }
+    for (uint32_t i = 0; i < n_rows; ++i) rows[i].sequence->length += rows[i].tokens;
+  });
+  if (st != HLLM_B200_OK && enqueued) mark_failed(rows, n_rows);
+  return st;
+}
+
+hllm_b200_status hllm_b200_step_async(hllm_b200_stage* stage, const hllm_b200_row* rows,
+                                      uint32_t n_rows, const void* device_input) {
+  bool enqueued = false;
+  const hllm_b200_status st = guarded([&] {
+    if (!stage || !device_input) fail(HLLM_B200_INVALID_REQUEST, "null argument");
+    std::scoped_lock lock(stage->mutex);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    const StepPlan p = plan_step(stage, rows, n_rows, true);
+    enqueued = true;
+    enqueue_step(stage, rows, p, device_input);
+    for (uint32_t i = 0; i < n_rows; ++i) {
+      rows[i].sequence->length += rows[i].tokens;
+      stage->pending.push_back(rows[i].sequence);
+    }
+  });
+  if (st != HLLM_B200_OK && enqueued) mark_failed(rows, n_rows);
+  return st;
+}
+
+hllm_b200_status hllm_b200_stage_sync(hllm_b200_stage* stage) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    std::scoped_lock lock(stage->mutex);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    uint32_t bits = 0;
+    check_cuda(cudaMemcpyAsync(&bits, stage->status, sizeof(bits), cudaMemcpyDeviceToHost,
+                               stage->stream), "status download");
+    check_cuda(cudaStreamSynchronize(stage->stream), "sync");
+    check_cuda(cudaMemsetAsync(stage->status, 0, sizeof(uint32_t), stage->stream), "status reset");
+    std::string msg;
+    const hllm_b200_status code = status_to_code(bits, &msg);
+    if (code != HLLM_B200_OK) {
+      for (auto* q : stage->pending)
+        if (stage->live.count(q)) q->failed = true;
+      stage->pending.clear();
+      fail(code, msg);
+    }
+    stage->pending.clear();
+  });
+}
+
+hllm_b200_status hllm_b200_stage_results(hllm_b200_stage* stage, hllm_b200_sampled* sampled,
+                                         uint32_t count) {
+  return guarded([&] {
+    if (!stage || (count && !sampled)) fail(HLLM_B200_INVALID_REQUEST, "null argument");
+    std::scoped_lock lock(stage->mutex);
+    if (count > stage->last_samples) fail(HLLM_B200_INVALID_REQUEST, "more results than samples");
+    std::vector<hb::SampleResult> res(count);
+    check_cuda(cudaMemcpyAsync(res.data(), stage->results, count * sizeof(hb::SampleResult),
+                               cudaMemcpyDeviceToHost, stage->stream), "results");
+    check_cuda(cudaStreamSynchronize(stage->stream), "results");
+    for (uint32_t i = 0; i < count; ++i) copy_sampled(res[i], &sampled[i]);
+  });
+}
+
+void* hllm_b200_stage_stream(hllm_b200_stage* stage) { return stage ? stage->stream : nullptr; }
+int32_t hllm_b200_stage_device(const hllm_b200_stage* stage) { return stage ? stage->device : -1; }
+uint32_t hllm_b200_stage_last_launches(const hllm_b200_stage* stage) {
+  return stage ? stage->launches : 0;
+}
+
+hllm_b200_status hllm_b200_seq_read_kv(hllm_b200_stage* stage, const hllm_b200_seq* seq,
+                                       uint64_t layer, uint32_t values, uint16_t* out) {
+  return guarded([&] {
+    if (!stage || !seq || !out || seq->owner != stage) fail(HLLM_B200_INVALID_REQUEST, "bad argument");
+    if (layer < stage->desc.layer_start || layer >= stage->desc.layer_end)
+      fail(HLLM_B200_INVALID_REQUEST, "layer not owned by this stage");
+    std::scoped_lock lock(stage->mutex);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    const size_t li = layer - stage->desc.layer_start;
+    const __half* base = stage->kv + li * stage->kv_layer_elems + (values ? stage->kv_layer_elems / 2 : 0);
+    const size_t d = stage->dim, hkv = stage->hkv;
+    for (uint64_t pos = 0; pos < seq->length; ++pos) {
+      const int32_t blk = seq->blocks[pos / hb::kBlockTokens];
+      for (size_t hh = 0; hh < hkv; ++hh) {
+        const __half* src = base + ((static_cast<size_t>(blk) * hkv + hh) * hb::kBlockTokens +
+                                    pos % hb::kBlockTokens) * d;
+        check_cuda(cudaMemcpyAsync(out + (pos * hkv + hh) * d, src, d * sizeof(__half),
+                                   cudaMemcpyDeviceToHost, stage->stream), "kv read");
+      }
+    }
+    check_cuda(cudaStreamSynchronize(stage->stream), "kv read");
+  });
+}
+
+hllm_b200_status hllm_b200_stage_read_hidden(hllm_b200_stage* stage, float* out, uint64_t tokens) {
+  return guarded([&] {
+    if (!stage || !out || tokens > stage->T_max) fail(HLLM_B200_INVALID_REQUEST, "bad argument");
+    std::scoped_lock lock(stage->mutex);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    check_cuda(cudaMemcpyAsync(out, stage->hidden, tokens * stage->h * sizeof(float),
+                               cudaMemcpyDeviceToHost, stage->stream), "hidden read");
+    check_cuda(cudaStreamSynchronize(stage->stream), "hidden read");
+  });
+}
+
+hllm_b200_status hllm_b200_stage_read_logits(hllm_b200_stage* stage, float* out, uint64_t rows) {
+  return guarded([&] {
+    if (!stage || !out || !stage->logits || rows > stage->R_max)
+      fail(HLLM_B200_INVALID_REQUEST, "bad argument");
+    std::scoped_lock lock(stage->mutex);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    check_cuda(cudaMemcpyAsync(out, stage->logits, rows * stage->V * sizeof(float),
+                               cudaMemcpyDeviceToHost, stage->stream), "logits read");
+    check_cuda(cudaStreamSynchronize(stage->stream), "logits read");
+  });
+}
+
+}  // extern "C"

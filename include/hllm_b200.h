@@ -1,0 +1,277 @@
+/*
+ * hllm_b200.h -- C ABI of the B200 stage executor (libhllm_b200.so).
+ *
+ * The executor runs one contiguous layer range of a Llama / Qwen3 decoder
+ * (a hLLM "stage") on one B200.  It is the drop-in for hLLM's per-step hot path
+ * behind runtime::StageBackend / runtime::BackendFactory
+ * (cpp/include/hllm/runtime/stage_backend.hpp:69-107,
+ *  cpp/include/hllm/runtime/backend_factory.hpp:28-47); the C++ adapter in
+ * hllm_b200/adapter/ implements those classes over this ABI.
+ *
+ * Conventions: plain C types, caller-owned host pointers valid for the call,
+ * device state owned by the stage.  No exception crosses the ABI; every call
+ * returns an hllm_b200_status and hllm_b200_last_error() describes the last
+ * failure on the calling thread.  One caller at a time per stage (the
+ * reference scheduler serialises passes, cpp/src/worker/scheduler.cpp:60-63).
+ */
+#ifndef HLLM_B200_H_
+#define HLLM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Mirrors runtime::ErrorCode (cpp/include/hllm/runtime/error.hpp:10-17). */
+typedef enum {
+  HLLM_B200_OK = 0,
+  HLLM_B200_INVALID_REQUEST = 1,
+  HLLM_B200_INCOMPATIBLE_WORKER = 2,
+  HLLM_B200_RESOURCE_EXHAUSTED = 3,
+  HLLM_B200_DEADLINE_EXCEEDED = 4,
+  HLLM_B200_CANCELLED = 5,
+  HLLM_B200_INTERNAL = 6
+} hllm_b200_status;
+
+/* Source tensor types accepted by hllm_b200_stage_load_tensor
+ * (runtime::DataType kF32 / kF16 / kBF16, cpp/include/hllm/runtime/safetensors.hpp:15-29). */
+typedef enum { HLLM_B200_F32 = 0, HLLM_B200_F16 = 1, HLLM_B200_BF16 = 2 } hllm_b200_dtype;
+
+typedef struct hllm_b200_stage hllm_b200_stage;
+typedef struct hllm_b200_seq hllm_b200_seq;
+
+/* Stage description: model::DenseConfig (cpp/include/hllm/model/dense_source.hpp:15-25)
+ * plus the fields of model::DenseSource that select the layer range
+ * (:35-45), plus executor capacities. */
+typedef struct {
+  uint64_t hidden_size;
+  uint64_t intermediate_size;
+  uint64_t attention_heads;
+  uint64_t key_value_heads;
+  uint64_t head_dimension;
+  uint64_t maximum_sequence_length;
+  float rms_norm_epsilon;
+  float rope_theta;
+  uint32_t query_key_norm;     /* Qwen3 per-head q/k RMSNorm */
+  uint64_t vocabulary_size;
+  uint64_t layer_start;        /* [layer_start, layer_end) of the model */
+  uint64_t layer_end;
+  uint32_t first;              /* stage embeds token ids */
+  uint32_t final;              /* stage owns final norm + LM head and samples */
+  uint32_t tied_head;          /* LM head is the embedding matrix */
+  int32_t device_id;
+  uint64_t kv_pool_tokens;     /* paged-KV capacity in tokens (16-token blocks) */
+  uint32_t max_step_tokens;    /* most tokens in one step (all rows) */
+  uint32_t max_step_rows;      /* most rows (sequences) in one step */
+  uint32_t max_sequences;      /* most live sequences */
+} hllm_b200_stage_desc;
+
+/* runtime::SamplingOptions (cpp/include/hllm/runtime/sampling.hpp:10-17). */
+typedef struct {
+  double temperature;
+  double top_p;
+  uint64_t top_k;
+  uint64_t seed;
+  uint32_t return_logprobs;
+  uint32_t top_logprobs;
+} hllm_b200_sampling;
+
+/* One row of a step: one sequence's input for this pass.  Replaces
+ * StageBackend::execute's (input, first_position, state) triple and one
+ * runtime::DecodeBatchItem (stage_backend.hpp:52-58, 90-92). */
+typedef struct {
+  hllm_b200_seq* sequence;
+  uint64_t first_position;     /* must equal the sequence's current length */
+  uint64_t tokens;             /* rows of input (prefill chunk) or 1 (decode) */
+  const uint64_t* token_ids;   /* first stage: `tokens` ids */
+  const uint16_t* activations; /* other stages: F16 [tokens][hidden] little-endian */
+  uint32_t sample;             /* final stage: produce a SampledToken from the last row */
+  hllm_b200_sampling sampling;
+  uint64_t generated_index;    /* counter of the request's seeded draws */
+} hllm_b200_row;
+
+/* runtime::SampledToken (cpp/include/hllm/runtime/sampling.hpp:22-27). */
+typedef struct {
+  uint64_t token_id;
+  double logprob;
+  uint32_t has_logprob;
+  uint32_t n_top;
+  uint64_t top_ids[5];
+  double top_logprobs[5];
+} hllm_b200_sampled;
+
+/* ---------------------------------------------------------------- errors */
+/* Copies the calling thread's last error message (NUL-terminated, truncated). */
+size_t hllm_b200_last_error(char* buffer, size_t size);
+
+/* ------------------------------------------------------------ stage life */
+/* Replaces BackendFactory::load (backend_factory.hpp:44-46) and the CUDA stage
+ * constructor (cpp/src/cuda/stage.cpp:87-143): allocates device weights, the
+ * paged KV pool and step workspaces.  Weights are then supplied tensor by
+ * tensor (load_tensor) or generated (init_synthetic); finalize checks that
+ * every tensor of the range is present. */
+hllm_b200_status hllm_b200_stage_create(const hllm_b200_stage_desc* desc, hllm_b200_stage** out);
+void hllm_b200_stage_destroy(hllm_b200_stage* stage);
+
+/* One named Safetensors tensor (names as in cpp/src/cpu/stage.cpp:236-259),
+ * row-major, converted to F16 on upload.  A value not representable as a
+ * finite F16 is rejected (cpp/src/cuda/stage.cpp:127-133). */
+hllm_b200_status hllm_b200_stage_load_tensor(hllm_b200_stage* stage, const char* name,
+                                             hllm_b200_dtype dtype, const void* data,
+                                             const uint64_t* shape, uint32_t rank);
+/* Fills every tensor of the stage with the seeded synthetic weights of this
+ * executor (bit-identical with the CPU oracle's generator).  No reference
+ * counterpart: used for benchmarks on random-init models. */
+hllm_b200_status hllm_b200_stage_init_synthetic(hllm_b200_stage* stage, uint64_t seed);
+hllm_b200_status hllm_b200_stage_finalize(hllm_b200_stage* stage);
+
+/* StageBackend::weight_memory / hidden_size / vocabulary_size / maximum_tokens
+ * (stage_backend.hpp:72-75). */
+hllm_b200_status hllm_b200_stage_info(const hllm_b200_stage* stage, uint64_t* weight_device_bytes,
+                                      uint64_t* hidden_size, uint64_t* vocabulary_size,
+                                      uint64_t* maximum_tokens);
+
+/* StageBackend::sequence_memory (stage_backend.hpp:80-81; SequenceMemory
+ * memory.hpp:46-49): device bytes a sequence of `tokens` positions holds for
+ * its life (whole 16-token KV blocks over this stage's layers), and the shared
+ * per-pass workspace, for prefill inputs of at most `maximum_query_tokens`
+ * rows. */
+hllm_b200_status hllm_b200_sequence_memory(const hllm_b200_stage* stage, uint64_t tokens,
+                                           uint64_t maximum_query_tokens,
+                                           uint64_t* cache_device_bytes,
+                                           uint64_t* workspace_device_bytes);
+
+/* StageBackend::allocate_sequence (stage_backend.hpp:84-85): reserves the KV
+ * blocks for `tokens` positions from the paged pool (RESOURCE_EXHAUSTED when
+ * the pool cannot hold them). */
+hllm_b200_status hllm_b200_seq_alloc(hllm_b200_stage* stage, uint64_t tokens, hllm_b200_seq** out);
+/* Returns the sequence's blocks to the pool (the reference frees a request's
+ * KV when release() resets its state, cpp/src/worker/control_service.cpp:509-515). */
+void hllm_b200_seq_free(hllm_b200_stage* stage, hllm_b200_seq* seq);
+/* Current length and capacity; failed != 0 once a pass that included it failed
+ * (cpp/src/cuda/stage.cpp:463-468 poisons such sequences). */
+hllm_b200_status hllm_b200_seq_info(const hllm_b200_seq* seq, uint64_t* length, uint64_t* capacity,
+                                    uint32_t* failed);
+
+/* ------------------------------------------------------------------ step */
+/* One pass over a ragged batch: StageBackend::execute for one row and
+ * execute_decode_batch for many (stage_backend.hpp:90-97; CUDA
+ * cpp/src/cuda/stage.cpp:204-232, 340-470).  Rows may mix prefill chunks and
+ * decode tokens.  Rows must name distinct sequences.
+ *   final stage: sampled[i] is written for every row with sample != 0;
+ *   other stages: boundary receives F16 [sum of tokens][hidden], rows in order.
+ * Host outputs are ready when the call returns.  On failure every sequence of
+ * the step is marked failed. */
+hllm_b200_status hllm_b200_step(hllm_b200_stage* stage, const hllm_b200_row* rows, uint32_t n_rows,
+                                hllm_b200_sampled* sampled, uint16_t* boundary);
+
+/* Enqueue-only variant for device-resident inputs: token ids (or F16
+ * activations) are read from device memory `device_input` (ids as int32, or
+ * F16 [tokens][hidden]) in row order; nothing is copied back and the call does
+ * not wait.  Results stay on the device (hllm_b200_stage_results reads them).
+ * hllm_b200_stage_sync waits and returns the first failure since the last
+ * sync.  No reference counterpart: used to time the hot path with inputs
+ * resident in HBM. */
+hllm_b200_status hllm_b200_step_async(hllm_b200_stage* stage, const hllm_b200_row* rows,
+                                      uint32_t n_rows, const void* device_input);
+hllm_b200_status hllm_b200_stage_sync(hllm_b200_stage* stage);
+/* Copies the last step's sampled results (one per sampling row, in order). */
+hllm_b200_status hllm_b200_stage_results(hllm_b200_stage* stage, hllm_b200_sampled* sampled,
+                                         uint32_t count);
+
+/* The stage's CUDA stream (cudaStream_t) and device, for callers that time or
+ * order work around steps. */
+void* hllm_b200_stage_stream(hllm_b200_stage* stage);
+int32_t hllm_b200_stage_device(const hllm_b200_stage* stage);
+/* Kernel launches of the last step (for launch accounting). */
+uint32_t hllm_b200_stage_last_launches(const hllm_b200_stage* stage);
+
+/* Reads back one layer's K or V for positions [0, length) of a sequence as
+ * F16 [length][kv_heads][head_dim] (the reference's contiguous cache layout,
+ * cpp/src/cpu/llama.cpp:152-158), gathering the paged blocks.  Test trace;
+ * the reference's CUDA execute_traced snapshots the same
+ * (cpp/include/hllm/cuda/stage.hpp:8-21). */
+hllm_b200_status hllm_b200_seq_read_kv(hllm_b200_stage* stage, const hllm_b200_seq* seq,
+                                       uint64_t layer, uint32_t values, uint16_t* out);
+/* Copies the stage's F32 hidden state of the last step, [tokens][hidden]. */
+hllm_b200_status hllm_b200_stage_read_hidden(hllm_b200_stage* stage, float* out, uint64_t tokens);
+/* Copies the last step's F32 logits of the sampling rows, [rows][vocab]. */
+hllm_b200_status hllm_b200_stage_read_logits(hllm_b200_stage* stage, float* out, uint64_t rows);
+
+/* ------------------------------------------------------ kernel entry points */
+/* Device-pointer entry points of the individual kernels, for parity tests and
+ * benchmarks of one operator.  All pointers are device memory; `stream` is a
+ * cudaStream_t (0 = legacy default stream).  Each call is asynchronous. */
+
+/* Y[n][m] = sum_k X[n][k] W[m][k] on tcgen05 (reference `linear`,
+ * cpp/src/cpu/tensor.cpp:47-62).  W: F16 [m][k_pad] (pair == 2: [2*second_row..]
+ * gate rows then up rows), X: F16 [n][k_pad] with zero padding columns,
+ * k_pad % 64 == 0.  epilogue: 0 store F32, 1 store F16, 2 add into F32 Y,
+ * 3 SwiGLU of the pair into F16 Y.  Uses a scratch area owned by the library
+ * (allocated on first use per device). */
+hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint32_t pair,
+                                uint64_t second_row, const void* x, uint64_t n, uint32_t epilogue,
+                                void* y, uint64_t ldy, uint32_t bn, uint32_t grid, void* stream);
+
+/* RMSNorm of rows of F32 x into F16 out (cpp/src/cpu/llama.cpp:193-212). */
+hllm_b200_status hllm_b200_rmsnorm(const float* x, uint64_t rows, uint64_t width, const float* w,
+                                   float eps, uint16_t* out, uint64_t ld_out, void* stream);
+
+/* The ragged packer (no reference counterpart; oracle_pack restates it):
+ * from row_slot/row_first/row_count [rows] and slot_blocks [slots][max_blocks]
+ * writes cu_seqlens [rows+1], positions, slot_mapping, token_row [tokens],
+ * seq_lens [rows], block_tables [rows][max_blocks], cu_splits and cu_qtiles
+ * [rows+1].  status (device u32) receives error bits. */
+hllm_b200_status hllm_b200_pack(const int32_t* row_slot, const int32_t* row_first,
+                                const int32_t* row_count, uint32_t rows, uint32_t tokens,
+                                const int32_t* slot_blocks, uint32_t max_blocks,
+                                uint32_t split_tokens, uint32_t qtile_tokens, int32_t* cu_seqlens,
+                                int32_t* positions, int32_t* slot_mapping, int32_t* token_row,
+                                int32_t* seq_lens, int32_t* block_tables, int32_t* cu_splits,
+                                int32_t* cu_qtiles, uint32_t* status, void* stream);
+
+/* Paged GQA attention over a packed batch (reference `attention`,
+ * cpp/src/cpu/llama.cpp:67-112).  q F16 [tokens][Hq*d]; caches F16
+ * [blocks][Hkv][16][d]; packer outputs as above; out F16 [tokens][ld_out].
+ * Decode rows (one token) use split-K over `split_tokens`-key splits; prefill
+ * rows use causal tensor-core tiles of attn_qtile_tokens(Hq/Hkv) tokens. */
+hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
+                                     const uint16_t* v_cache, const int32_t* row_first,
+                                     const int32_t* row_count, const int32_t* cu_seqlens,
+                                     const int32_t* seq_lens, const int32_t* block_tables,
+                                     const int32_t* cu_splits, const int32_t* cu_qtiles,
+                                     uint32_t rows, uint32_t total_splits, uint32_t total_qtiles,
+                                     uint32_t hq, uint32_t hkv, uint32_t dim, uint32_t max_blocks,
+                                     uint32_t split_tokens, uint16_t* out, uint64_t ld_out,
+                                     uint32_t* status, void* stream);
+/* Query tokens per prefill tile for a GQA group size. */
+uint32_t hllm_b200_attention_qtile_tokens(uint32_t group);
+
+/* q/k RMSNorm + RoPE + paged K/V write for a packed batch (reference
+ * cpp/src/cpu/llama.cpp:255-264).  qkv F32 [tokens][(Hq+2Hkv)d];
+ * rope_pow [d/2] = theta^(2i/d) as the reference computes it. */
+hllm_b200_status hllm_b200_qkv_post(const float* qkv, uint64_t tokens, uint32_t hq, uint32_t hkv,
+                                    uint32_t dim, const int32_t* positions,
+                                    const int32_t* slot_mapping, const float* q_norm,
+                                    const float* k_norm, float eps, const float* rope_pow,
+                                    uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache,
+                                    void* stream);
+
+/* Sampler (reference sample_token, cpp/src/sampling.cpp:19-90): logits F32
+ * [rows][ld] on the device, options per row on the host; results to host. */
+hllm_b200_status hllm_b200_sample(const float* logits, uint32_t rows, uint64_t vocab, uint64_t ld,
+                                  const hllm_b200_sampling* options,
+                                  const uint64_t* generated_index, hllm_b200_sampled* out,
+                                  void* stream);
+
+/* Seeded synthetic F16 matrix [rows][cols] at row stride ld (device). */
+hllm_b200_status hllm_b200_synth_matrix(uint64_t seed, uint64_t tag, uint64_t rows, uint64_t cols,
+                                        uint64_t ld, float stddev, uint16_t* out, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* HLLM_B200_H_ */

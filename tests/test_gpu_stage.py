@@ -1,0 +1,276 @@
+"""Stage-level parity of the B200 executor through its public host API
+(hllm_b200.B200Stage over the C ABI) against the reference's CPU pipeline.
+
+Bars (BASELINE north star and the reference's own tests):
+* tiny Qwen3 Transformers fixture: layers, K/V and logits within 5e-3 (the
+  reference CUDA F16 tolerance, tests/cpp/cuda_stage_test.cpp:102);
+* logits within 2e-2 max-abs of the F32 CPU path on the same F16 weights;
+  greedy tokens identical up to the first step whose oracle top-2 gap is below
+  1e-2;
+* decode-batch contract (tests/cpp/decode_batch_contract.hpp:8-47): batched ==
+  serial tokens, logprobs within 0.02, same generated_index;
+* error behaviour of cpp/src/cuda/stage.cpp (position, capacity, vocabulary,
+  non-finite boundary, poisoned sequences).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from hllm_b200 import (B200Stage, BoundaryActivation, DecodeBatchItem, ModelConfig,
+                       PrefillProgress, SampledToken, SamplingOptions, StageError, TokenInput)
+from hllm_b200 import _lib
+from tests.gpu_util import torch_cuda
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+LOGIT_TOL = 2e-2
+GAP = 1e-2
+
+
+def tiny_qwen():
+    d = np.load(os.path.join(GOLD, "qwen3_tiny_reference.npz"))
+    h, I, Hq, Hkv, dim, maxpos, L, V = [int(x) for x in d["config"]]
+    eps, theta = [float(x) for x in d["config_f"]]
+    cfg = ModelConfig(h, I, Hq, Hkv, dim, maxpos, eps, theta, True, V, L, True)
+    weights = {k[2:]: d[k].astype(np.float32) for k in d.files if k.startswith("w/")}
+    return cfg, weights, d
+
+
+def make_stage(cfg, weights, **kw):
+    torch_cuda()
+    s = B200Stage(cfg, **kw)
+    names = s.expected_tensors()
+    for n in names:
+        s.load_tensor(n, weights[n])
+    s.finalize()
+    return s
+
+
+def test_tiny_qwen_layers_caches_and_logits_match_transformers():
+    cfg, weights, d = tiny_qwen()
+    s0 = make_stage(cfg, weights, layer_start=0, layer_end=1, first=True, final=False,
+                    kv_pool_tokens=256)
+    s1 = make_stage(cfg, weights, layer_start=1, layer_end=2, first=False, final=True,
+                    kv_pool_tokens=256)
+    ids = [1, 4, 2, 8, 3]
+    a, b = s0.allocate_sequence(16), s1.allocate_sequence(16)
+    tol = 5e-3
+    for position, count in ((0, 3), (3, 1), (4, 1)):
+        out0 = s0.execute(TokenInput(ids[position:position + count]), position, a)
+        assert isinstance(out0, BoundaryActivation) and out0.tokens == count
+        layer0 = oracle.f16_decode(np.frombuffer(out0.payload, np.uint16)).reshape(count, -1)
+        np.testing.assert_allclose(layer0, d["layer_outputs/0"][0][position:position + count],
+                                   atol=tol, rtol=0)
+        out1 = s1.execute(out0, position, b)
+        assert isinstance(out1, SampledToken)
+        hidden = s1.read_hidden(count)
+        np.testing.assert_allclose(hidden, d["layer_outputs/1"][0][position:position + count],
+                                   atol=tol, rtol=0)
+        logits = s1.read_logits(1)
+        np.testing.assert_allclose(logits[0], d["logits"][0][position + count - 1], atol=tol, rtol=0)
+        assert out1.id == int(np.argmax(d["logits"][0][position + count - 1]))
+    for stage, seq, layer in ((s0, a, 0), (s1, b, 1)):
+        k = oracle.f16_decode(stage.read_kv(seq, layer, False))
+        v = oracle.f16_decode(stage.read_kv(seq, layer, True))
+        np.testing.assert_allclose(k.transpose(1, 0, 2), d[f"keys/{layer}"][0], atol=tol, rtol=0)
+        np.testing.assert_allclose(v.transpose(1, 0, 2), d[f"values/{layer}"][0], atol=tol, rtol=0)
+    s0.close()
+    s1.close()
+
+
+# ----------------------------------------------------------------------------- tiny Llama (C1)
+def c1_spec():
+    from tests.golden.make_golden import C1, C1_SEED
+    return C1, C1_SEED
+
+
+def cfg_of(spec, maxlen=None):
+    return ModelConfig(spec.hidden_size, spec.intermediate_size, spec.attention_heads,
+                       spec.key_value_heads, spec.head_dimension,
+                       maxlen or spec.maximum_sequence_length, spec.rms_norm_epsilon,
+                       spec.rope_theta, spec.query_key_norm, spec.vocabulary_size, spec.layers,
+                       spec.tied)
+
+
+def top2_gap(logits):
+    part = np.partition(logits, -2)
+    return float(part[-1] - part[-2])
+
+
+def test_tiny_llama_two_stage_pipeline_tokens_and_logits():
+    """Configuration 1 (cpp/src/cpu/stage.cpp composition, F16 boundary between
+    stages) on the B200 stages vs the reference CPU pipeline golden tokens."""
+    spec, seed = c1_spec()
+    g = np.load(os.path.join(GOLD, "tiny_llama_pipeline.npz"))
+    cfg = cfg_of(spec)
+    s0 = B200Stage(cfg, 0, 2, first=True, final=False, kv_pool_tokens=4096)
+    s1 = B200Stage(cfg, 2, 4, first=False, final=True, kv_pool_tokens=4096)
+    torch_cuda()
+    s0.init_synthetic(seed)
+    s1.init_synthetic(seed)
+    weights = oracle.synth_weights(spec, seed)
+    o0 = oracle.OracleModel(spec, weights, 0, 2)
+    o1 = oracle.OracleModel(spec, weights, 2, 4)
+    lens = g["prompt_lengths"]
+    offs = np.concatenate([[0], np.cumsum(lens)])
+    for r in range(4):
+        prompt = [int(x) for x in g["prompt_ids"][offs[r]:offs[r + 1]]]
+        a, b = s0.allocate_sequence(len(prompt) + 32), s1.allocate_sequence(len(prompt) + 32)
+        oa, ob = o0.new_sequence(len(prompt) + 32), o1.new_sequence(len(prompt) + 32)
+        inp, pos = prompt, 0
+        agree = True
+        for step in range(32):
+            out = s1.execute(s0.execute(TokenInput(inp), pos, a), pos, b)
+            gl = s1.read_logits(1)[0]
+            # oracle on the GPU's own token path (teacher forcing)
+            h = oracle.f16_round(o0.forward(o0.embed(inp), pos, oa))
+            ol = o1.logits(o1.forward(h, pos, ob)[-1:])[0]
+            assert np.max(np.abs(gl - ol)) < LOGIT_TOL, (r, step, np.max(np.abs(gl - ol)))
+            if agree:
+                if top2_gap(ol) < GAP:
+                    agree = False
+                else:
+                    assert out.id == int(np.argmax(ol)) == int(g["tokens"][r, step]), (r, step)
+            pos += len(inp)
+            inp = [out.id]
+        s0.release(a)
+        s1.release(b)
+    s0.close()
+    s1.close()
+
+
+def test_decode_batch_contract_tiny_qwen():
+    """tests/cpp/decode_batch_contract.hpp:8-47 on the B200 stage."""
+    cfg, weights, _ = tiny_qwen()
+    stage = make_stage(cfg, weights, kv_pool_tokens=1024)
+    for temperature in (0.0, 0.8):
+        lengths = [7, 2, 4, 1]
+        ref, bat, expected = [], [], []
+        for i, n in enumerate(lengths):
+            ref.append(stage.allocate_sequence(n + 1))
+            bat.append(stage.allocate_sequence(n + 1))
+            for st in (ref[-1], bat[-1]):
+                st.sampling = SamplingOptions(temperature, 0.95, 8, i + 42, True, 3)
+                stage.execute(TokenInput([1] * n), 0, st)
+            expected.append(stage.execute(TokenInput([4]), n, ref[-1]))
+        items = [DecodeBatchItem(TokenInput([4]), n, bat[i]) for i, n in enumerate(lengths)]
+        actual = stage.execute_decode_batch(items)
+        assert len(actual) == len(expected)
+        for i in range(4):
+            assert actual[i].id == expected[i].id
+            assert abs(actual[i].logprob - expected[i].logprob) < 0.02
+            assert len(actual[i].top_logprobs) == 3
+            assert bat[i].generated_index == ref[i].generated_index
+        for st in ref + bat:
+            stage.release(st)
+    stage.close()
+
+
+def test_rejections_and_poisoning():
+    cfg, weights, _ = tiny_qwen()
+    s = make_stage(cfg, weights, kv_pool_tokens=64)
+    seq = s.allocate_sequence(8)
+    with pytest.raises(StageError) as e:
+        s.execute(TokenInput([1, 2]), 1, seq)  # position must equal length
+    assert e.value.code == _lib.INVALID_REQUEST
+    with pytest.raises(StageError) as e:
+        s.execute(TokenInput([11]), 0, seq)  # token id >= vocabulary
+    assert e.value.code == _lib.INVALID_REQUEST
+    with pytest.raises(StageError) as e:
+        s.execute(TokenInput([1] * 9), 0, seq)  # beyond capacity
+    assert e.value.code == _lib.INVALID_REQUEST
+    out = s.execute(TokenInput([1, 2, 3]), 0, seq)
+    assert isinstance(out, SampledToken)
+    assert s.sequence_info(seq)[0] == 3
+    with pytest.raises(StageError) as e:
+        s.allocate_sequence(100)  # more than the context
+    assert e.value.code == _lib.INVALID_REQUEST
+    others = [s.allocate_sequence(16) for _ in range(3)]
+    with pytest.raises(StageError) as e:
+        s.allocate_sequence(16)  # pool holds 64 tokens = 4 blocks
+    assert e.value.code == _lib.RESOURCE_EXHAUSTED
+    s.release(others[0])
+    again = s.allocate_sequence(16)  # freed blocks are reused
+    s.release(again)
+    seq.prefill_only = True
+    assert s.execute(TokenInput([5]), 3, seq) == PrefillProgress()
+    s.close()
+    # Non-finite boundary input: invalid request, and the sequence is poisoned.
+    s1 = make_stage(cfg, weights, layer_start=1, layer_end=2, first=False, final=True,
+                    kv_pool_tokens=64)
+    q = s1.allocate_sequence(8)
+    bad = np.zeros(cfg.hidden_size, np.uint16)
+    bad[2] = 0x7C00
+    with pytest.raises(StageError) as e:
+        s1.execute(BoundaryActivation(1, cfg.hidden_size, bad.tobytes()), 0, q)
+    assert e.value.code == _lib.INVALID_REQUEST
+    assert s1.sequence_info(q)[2]
+    with pytest.raises(StageError):
+        s1.execute(BoundaryActivation(1, cfg.hidden_size, np.zeros(cfg.hidden_size, np.uint16).tobytes()), 0, q)
+    s1.close()
+
+
+# ----------------------------------------------------------------------------- Qwen3-4B geometry
+QWEN3_4B = oracle.ModelSpec(hidden_size=2560, intermediate_size=9728, attention_heads=32,
+                            key_value_heads=8, head_dimension=128, layers=36,
+                            vocabulary_size=151936, maximum_sequence_length=4608,
+                            rms_norm_epsilon=1e-6, rope_theta=1e6, query_key_norm=True, tied=True)
+
+
+def test_qwen3_4b_geometry_two_layers_prefill_decode_and_mixed_batch():
+    """Full Qwen3-4B shapes (h2560, 32q/8kv, d128, I9728, V151936, tied), two
+    layers, seeded synthetic weights: logits vs the F32 oracle within 2e-2,
+    greedy tokens by the top-2 gap rule, and one mixed step (a prefill chunk
+    with two decode rows) equal to the same rows run alone."""
+    spec = QWEN3_4B
+    seed = 4242
+    cfg = cfg_of(spec)
+    stage = B200Stage(cfg, 0, 2, first=True, final=True, kv_pool_tokens=8192)
+    torch_cuda()
+    stage.init_synthetic(seed)
+    weights = oracle.synth_weights(spec, seed, layers=range(2))
+    orc = oracle.OracleModel(spec, weights, 0, 2)
+    rng = np.random.default_rng(3)
+    prompt = [int(x) for x in rng.integers(0, spec.vocabulary_size, 64)]
+    seq = stage.allocate_sequence(128)
+    oseq = orc.new_sequence(128)
+    inp, pos, agree = prompt, 0, True
+    for step in range(6):
+        out = stage.execute(TokenInput(inp), pos, seq)
+        gl = stage.read_logits(1)[0]
+        ol = orc.logits(orc.forward(orc.embed(inp), pos, oseq)[-1:])[0]
+        err = float(np.max(np.abs(gl - ol)))
+        assert err < LOGIT_TOL, (step, err)
+        if agree:
+            if top2_gap(ol) < GAP:
+                agree = False
+            else:
+                assert out.id == int(np.argmax(ol)), step
+        pos += len(inp)
+        inp = [out.id]
+    # Mixed batch: a 40-token prefill chunk plus two decode rows in one pass.
+    a = stage.allocate_sequence(64)
+    b = stage.allocate_sequence(64)
+    c = stage.allocate_sequence(64)
+    stage.execute(TokenInput(prompt[:10]), 0, b)
+    stage.execute(TokenInput(prompt[10:30]), 0, c)
+    solo = [stage.allocate_sequence(64) for _ in range(3)]
+    stage.execute(TokenInput(prompt[:10]), 0, solo[1])
+    stage.execute(TokenInput(prompt[10:30]), 0, solo[2])
+    mixed = stage.execute_mixed_batch([DecodeBatchItem(TokenInput(prompt[20:60]), 0, a),
+                                       DecodeBatchItem(TokenInput([7]), 10, b),
+                                       DecodeBatchItem(TokenInput([9]), 20, c)])
+    mixed_logits = stage.read_logits(3)
+    alone = [stage.execute(TokenInput(prompt[20:60]), 0, solo[0])]
+    la = [stage.read_logits(1)[0]]
+    alone.append(stage.execute(TokenInput([7]), 10, solo[1]))
+    la.append(stage.read_logits(1)[0])
+    alone.append(stage.execute(TokenInput([9]), 20, solo[2]))
+    la.append(stage.read_logits(1)[0])
+    for i in range(3):
+        assert np.max(np.abs(mixed_logits[i] - la[i])) < 5e-3
+        if top2_gap(la[i]) > GAP:
+            assert mixed[i].id == alone[i].id
+    stage.close()
