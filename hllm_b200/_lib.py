@@ -97,9 +97,13 @@ def lib():
         "hllm_b200_step_async": (C.c_int, [vp, C.POINTER(Row), u32, vp]),
         "hllm_b200_stage_sync": (C.c_int, [vp]),
         "hllm_b200_stage_results": (C.c_int, [vp, C.POINTER(Sampled), u32]),
+        "hllm_b200_stage_profile": (C.c_int, [vp, u32]),
+        "hllm_b200_stage_profile_read": (C.c_int, [vp, u32, C.POINTER(C.c_double), C.POINTER(u64),
+                                                   C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "hllm_b200_stage_stream": (vp, [vp]),
         "hllm_b200_stage_device": (i32, [vp]),
         "hllm_b200_stage_last_launches": (u32, [vp]),
+        "hllm_b200_stage_last_transfer": (C.c_int, [vp, C.POINTER(u64), C.POINTER(u64)]),
         "hllm_b200_seq_read_kv": (C.c_int, [vp, vp, u64, u32, C.POINTER(C.c_uint16)]),
         "hllm_b200_stage_read_hidden": (C.c_int, [vp, C.POINTER(C.c_float), u64]),
         "hllm_b200_stage_read_logits": (C.c_int, [vp, C.POINTER(C.c_float), u64]),

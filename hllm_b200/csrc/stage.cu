@@ -181,10 +181,27 @@ struct hllm_b200_stage {
   std::vector<int> free_slots;
   std::set<hllm_b200_seq*> live;
   uint32_t launches = 0;
+  uint64_t last_h2d = 0, last_d2h = 0;  // host<->device bytes of the last step
   uint32_t last_samples = 0;
   uint64_t last_tokens = 0;
   std::vector<hllm_b200_seq*> pending;  // sequences of steps enqueued since the last sync
   std::mutex mutex;
+
+  // Optional per-launch timing (hllm_b200_stage_profile): CUDA events around
+  // every launch, grouped by kernel class, with each launch's algorithmic
+  // bytes and FLOPs.
+  struct ProfEvent {
+    int kind;
+    double bytes, flops;
+    cudaEvent_t a, b;
+  };
+  static constexpr int kProfKinds = 5;
+  bool profiling = false;
+  std::vector<ProfEvent> prof_pending;
+  std::vector<cudaEvent_t> event_pool;
+  double prof_ms[kProfKinds] = {}, prof_bytes[kProfKinds] = {}, prof_flops[kProfKinds] = {};
+  uint64_t prof_n[kProfKinds] = {};
+  cudaEvent_t prof_open = nullptr;
 
   ~hllm_b200_stage() {
     if (stream) {
@@ -195,6 +212,49 @@ struct hllm_b200_stage {
     if (h_down) cudaFreeHost(h_down);
     if (h_act) cudaFreeHost(h_act);
     for (auto* s : live) delete s;
+    for (auto& e : prof_pending) {
+      cudaEventDestroy(e.a);
+      cudaEventDestroy(e.b);
+    }
+    for (auto e : event_pool) cudaEventDestroy(e);
+  }
+
+  cudaEvent_t take_event() {
+    if (event_pool.empty()) {
+      cudaEvent_t e;
+      check_cuda(cudaEventCreate(&e), "cudaEventCreate");
+      return e;
+    }
+    cudaEvent_t e = event_pool.back();
+    event_pool.pop_back();
+    return e;
+  }
+  void prof_begin() {
+    if (!profiling) return;
+    prof_open = take_event();
+    check_cuda(cudaEventRecord(prof_open, stream), "cudaEventRecord");
+  }
+  void prof_end(int kind, double bytes, double flops) {
+    if (!profiling) return;
+    cudaEvent_t b = take_event();
+    check_cuda(cudaEventRecord(b, stream), "cudaEventRecord");
+    prof_pending.push_back({kind, bytes, flops, prof_open, b});
+    prof_open = nullptr;
+  }
+  // Call after the stream has drained the recorded events.
+  void prof_collect() {
+    for (auto& e : prof_pending) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, e.a, e.b) == cudaSuccess) {
+        prof_ms[e.kind] += ms;
+        prof_bytes[e.kind] += e.bytes;
+        prof_flops[e.kind] += e.flops;
+        prof_n[e.kind] += 1;
+      }
+      event_pool.push_back(e.a);
+      event_pool.push_back(e.b);
+    }
+    prof_pending.clear();
   }
 
   template <class T>
@@ -506,6 +566,8 @@ struct StepPlan {
   int total_splits = 0;
   int total_qtiles = 0;
   int qtile_tokens = 0;
+  double attn_dec_bytes = 0, attn_dec_flops = 0;  // algorithmic, per layer
+  double attn_pre_bytes = 0, attn_pre_flops = 0;
 };
 
 void validate_sampling(const hllm_b200_sampling& o) {
@@ -571,6 +633,22 @@ StepPlan plan_step(hllm_b200_stage* s, const hllm_b200_row* rows, uint32_t n, bo
   for (uint32_t i = 0; i < n; ++i)
     if (rows[i].tokens > 1)
       p.total_qtiles += static_cast<int>((rows[i].tokens + p.qtile_tokens - 1) / p.qtile_tokens);
+  // Algorithmic attention work per layer: K and V of every context position
+  // read once per kv head, q read and output written once; causal FLOPs
+  // 4 * Hq * d per (query, key) pair.
+  const double kvb = 2.0 * s->hkv * s->dim * 2.0, qb = 2.0 * s->hq * s->dim * 2.0;
+  for (uint32_t i = 0; i < n; ++i) {
+    const double ctx = static_cast<double>(rows[i].first_position + rows[i].tokens);
+    const double cnt = static_cast<double>(rows[i].tokens);
+    const double pairs = cnt * static_cast<double>(rows[i].first_position) + cnt * (cnt + 1) / 2;
+    if (rows[i].tokens == 1) {
+      p.attn_dec_bytes += ctx * kvb + qb;
+      p.attn_dec_flops += 4.0 * s->hq * s->dim * ctx;
+    } else {
+      p.attn_pre_bytes += ctx * kvb + cnt * qb;
+      p.attn_pre_flops += 4.0 * s->hq * s->dim * pairs;
+    }
+  }
   (void)decode_rows;
   return p;
 }
@@ -580,6 +658,28 @@ StepPlan plan_step(hllm_b200_stage* s, const hllm_b200_row* rows, uint32_t n, bo
     check_cuda((expr), #expr);                          \
     ++s->launches;                                      \
   } while (0)
+
+// Kernel classes of the profile: projection GEMMs at decode width (n <= 128)
+// and prefill width, decode attention (split + combine), prefill attention,
+// everything else (norms, q/k epilogue, packer, embedding, sampler, boundary).
+enum ProfKind { kProfGemmDecode = 0, kProfGemmPrefill = 1, kProfAttnDecode = 2,
+                kProfAttnPrefill = 3, kProfOther = 4 };
+
+#define PLAUNCH(kind, bytes, flops, expr)               \
+  do {                                                  \
+    s->prof_begin();                                    \
+    check_cuda((expr), #expr);                          \
+    s->prof_end((kind), (bytes), (flops));              \
+    ++s->launches;                                      \
+  } while (0)
+
+// Algorithmic traffic and work of one projection GEMM: weights once, tokens
+// once, outputs (read + write for the residual add).
+double gemm_bytes(double m, double n, double k, int pair, int epilogue) {
+  const double out = epilogue == hb::kEpiResidual ? 8.0 : (epilogue == hb::kEpiStoreF32 ? 4.0 : 2.0);
+  return pair * m * k * 2.0 + n * k * 2.0 + n * m * out;
+}
+double gemm_flops(double m, double n, double k, int pair) { return 2.0 * pair * m * n * k; }
 
 void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan& p,
                   const void* device_input) {
@@ -616,6 +716,9 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
   }
   check_cuda(cudaMemcpyAsync(s->up, s->h_up, s->up_bytes, cudaMemcpyHostToDevice, s->stream),
              "descriptor upload");
+  s->last_h2d = s->up_bytes + ((!s->desc.first && !device_input)
+                                   ? static_cast<uint64_t>(T) * s->h * sizeof(__half) : 0);
+  s->last_d2h = 0;
   if (s->desc.first && device_input)
     check_cuda(cudaMemcpyAsync(s->ids, device_input, T * sizeof(int32_t),
                                cudaMemcpyDeviceToDevice, s->stream), "id copy");
@@ -643,27 +746,29 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
   st.max_blocks = static_cast<int>(s->max_blocks);
   st.split_tokens = p.split_tokens;
   st.qtile_tokens = p.qtile_tokens;
-  LAUNCH(hb::pack_launch(st, s->slot_blocks, s->status, s->stream));
+  PLAUNCH(kProfOther, 0, 0, hb::pack_launch(st, s->slot_blocks, s->status, s->stream));
 
   // ---- input
   if (s->desc.first) {
-    LAUNCH(hb::embed_launch(s->ids, T, s->embed, static_cast<int>(s->V), static_cast<int>(s->h),
+    PLAUNCH(kProfOther, 0, 0, hb::embed_launch(s->ids, T, s->embed, static_cast<int>(s->V), static_cast<int>(s->h),
                             static_cast<int>(s->h_pad), s->hidden, s->status, s->stream));
   } else {
-    LAUNCH(hb::boundary_in_launch(s->bin, T, static_cast<int>(s->h), s->hidden, s->status,
+    PLAUNCH(kProfOther, 0, 0, hb::boundary_in_launch(s->bin, T, static_cast<int>(s->h), s->hidden, s->status,
                                   s->stream));
   }
 
   // ---- layers
   const float eps = s->desc.rms_norm_epsilon;
   const int h = static_cast<int>(s->h);
+  const int gk = T <= 128 ? kProfGemmDecode : kProfGemmPrefill;
   for (size_t li = 0; li < s->n_layers; ++li) {
     const Layer& L = s->layers[li];
     __half* kc = s->kv + li * s->kv_layer_elems;
     __half* vc = kc + s->kv_layer_elems / 2;
-    LAUNCH(hb::rmsnorm_launch(s->hidden, T, h, L.in_norm, eps, s->xn, static_cast<int>(s->h_pad),
+    PLAUNCH(kProfOther, 0, 0, hb::rmsnorm_launch(s->hidden, T, h, L.in_norm, eps, s->xn, static_cast<int>(s->h_pad),
                               nullptr, s->stream));
-    LAUNCH(hb::gemm_run(L.g_qkv, s->in_xn, T, hb::kEpiStoreF32, s->qkv, static_cast<int>(s->qkvw),
+    PLAUNCH(gk, gemm_bytes(s->qkvw, T, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->qkvw, T, s->h, 1),
+            hb::gemm_run(L.g_qkv, s->in_xn, T, hb::kEpiStoreF32, s->qkv, static_cast<int>(s->qkvw),
                         s->gscratch, s->stream));
     hb::QkvPostArgs qa{};
     qa.qkv = s->qkv;
@@ -680,7 +785,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     qa.q_out = s->q;
     qa.k_cache = kc;
     qa.v_cache = vc;
-    LAUNCH(hb::qkv_post_launch(qa, s->stream));
+    PLAUNCH(kProfOther, 0, 0, hb::qkv_post_launch(qa, s->stream));
     hb::AttnArgs aa{};
     aa.q = s->q;
     aa.k_cache = kc;
@@ -706,17 +811,21 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     aa.ld_out = static_cast<int>(s->qw_pad);
     aa.status = s->status;
     if (p.total_splits) {
-      LAUNCH(hb::attn_decode_launch(aa, p.total_splits, s->stream));
+      PLAUNCH(kProfAttnDecode, p.attn_dec_bytes, p.attn_dec_flops, hb::attn_decode_launch(aa, p.total_splits, s->stream));
       ++s->launches;  // combine pass
     }
-    if (p.total_qtiles) LAUNCH(hb::attn_prefill_launch(aa, p.total_qtiles, s->stream));
-    LAUNCH(hb::gemm_run(L.g_o, s->in_attn, T, hb::kEpiResidual, s->hidden, h, s->gscratch,
+    if (p.total_qtiles)
+      PLAUNCH(kProfAttnPrefill, p.attn_pre_bytes, p.attn_pre_flops, hb::attn_prefill_launch(aa, p.total_qtiles, s->stream));
+    PLAUNCH(gk, gemm_bytes(s->h, T, s->qw, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->qw, 1),
+            hb::gemm_run(L.g_o, s->in_attn, T, hb::kEpiResidual, s->hidden, h, s->gscratch,
                         s->stream));
-    LAUNCH(hb::rmsnorm_launch(s->hidden, T, h, L.post_norm, eps, s->xn,
+    PLAUNCH(kProfOther, 0, 0, hb::rmsnorm_launch(s->hidden, T, h, L.post_norm, eps, s->xn,
                               static_cast<int>(s->h_pad), nullptr, s->stream));
-    LAUNCH(hb::gemm_run(L.g_gu, s->in_xn, T, hb::kEpiSwiGLU, s->act, static_cast<int>(s->I_pad),
+    PLAUNCH(gk, gemm_bytes(s->I, T, s->h, 2, hb::kEpiSwiGLU), gemm_flops(s->I, T, s->h, 2),
+            hb::gemm_run(L.g_gu, s->in_xn, T, hb::kEpiSwiGLU, s->act, static_cast<int>(s->I_pad),
                         s->gscratch, s->stream));
-    LAUNCH(hb::gemm_run(L.g_down, s->in_act, T, hb::kEpiResidual, s->hidden, h, s->gscratch,
+    PLAUNCH(gk, gemm_bytes(s->h, T, s->I, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->I, 1),
+            hb::gemm_run(L.g_down, s->in_act, T, hb::kEpiResidual, s->hidden, h, s->gscratch,
                         s->stream));
   }
 
@@ -724,16 +833,18 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
   if (s->desc.final) {
     if (p.samples) {
       const int S = static_cast<int>(p.samples);
-      LAUNCH(hb::last_token_launch(s->cu_seqlens, s->sample_rows, S, s->last_idx, s->stream));
-      LAUNCH(hb::rmsnorm_launch(s->hidden, S, h, s->final_norm, eps, s->xs,
+      PLAUNCH(kProfOther, 0, 0, hb::last_token_launch(s->cu_seqlens, s->sample_rows, S, s->last_idx, s->stream));
+      PLAUNCH(kProfOther, 0, 0, hb::rmsnorm_launch(s->hidden, S, h, s->final_norm, eps, s->xs,
                                 static_cast<int>(s->h_pad), s->last_idx, s->stream));
-      LAUNCH(hb::gemm_run(s->g_head, s->in_xs, S, hb::kEpiStoreF32, s->logits,
+      PLAUNCH(S <= 128 ? kProfGemmDecode : kProfGemmPrefill,
+              gemm_bytes(s->V, S, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->V, S, s->h, 1),
+              hb::gemm_run(s->g_head, s->in_xs, S, hb::kEpiStoreF32, s->logits,
                           static_cast<int>(s->V), s->gscratch, s->stream));
-      LAUNCH(hb::sample_launch(s->logits, S, static_cast<int>(s->V), static_cast<int>(s->V),
+      PLAUNCH(kProfOther, 0, 0, hb::sample_launch(s->logits, S, static_cast<int>(s->V), static_cast<int>(s->V),
                                s->d_params, s->sample_scratch, s->results, s->status, s->stream));
     }
   } else {
-    LAUNCH(hb::boundary_out_launch(s->hidden, T, h, s->bout, s->status, s->stream));
+    PLAUNCH(kProfOther, 0, 0, hb::boundary_out_launch(s->hidden, T, h, s->bout, s->status, s->stream));
   }
   s->last_samples = p.samples;
   s->last_tokens = p.tokens;
@@ -933,12 +1044,14 @@ hllm_b200_status hllm_b200_step(hllm_b200_stage* stage, const hllm_b200_row* row
     enqueued = true;
     enqueue_step(stage, rows, p, nullptr);
     const size_t down_bytes = 8 + p.samples * sizeof(hb::SampleResult);
+    stage->last_d2h = down_bytes + (stage->desc.final ? 0 : p.tokens * stage->h * sizeof(__half));
     check_cuda(cudaMemcpyAsync(stage->h_down, stage->down, down_bytes, cudaMemcpyDeviceToHost,
                                stage->stream), "result download");
     if (!stage->desc.final)
       check_cuda(cudaMemcpyAsync(stage->h_act, stage->bout, p.tokens * stage->h * sizeof(__half),
                                  cudaMemcpyDeviceToHost, stage->stream), "boundary download");
     check_cuda(cudaStreamSynchronize(stage->stream), "step");
+    stage->prof_collect();
     uint32_t bits;
     std::memcpy(&bits, stage->h_down, sizeof(bits));
     std::string msg;
@@ -984,6 +1097,7 @@ hllm_b200_status hllm_b200_stage_sync(hllm_b200_stage* stage) {
     check_cuda(cudaMemcpyAsync(&bits, stage->status, sizeof(bits), cudaMemcpyDeviceToHost,
                                stage->stream), "status download");
     check_cuda(cudaStreamSynchronize(stage->stream), "sync");
+    stage->prof_collect();
     check_cuda(cudaMemsetAsync(stage->status, 0, sizeof(uint32_t), stage->stream), "status reset");
     std::string msg;
     const hllm_b200_status code = status_to_code(bits, &msg);
@@ -1011,10 +1125,50 @@ hllm_b200_status hllm_b200_stage_results(hllm_b200_stage* stage, hllm_b200_sampl
   });
 }
 
+hllm_b200_status hllm_b200_stage_profile(hllm_b200_stage* stage, uint32_t enable) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    std::scoped_lock lock(stage->mutex);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    check_cuda(cudaStreamSynchronize(stage->stream), "profile");
+    stage->prof_collect();
+    for (int k = 0; k < hllm_b200_stage::kProfKinds; ++k) {
+      stage->prof_ms[k] = stage->prof_bytes[k] = stage->prof_flops[k] = 0;
+      stage->prof_n[k] = 0;
+    }
+    stage->profiling = enable != 0;
+  });
+}
+
+hllm_b200_status hllm_b200_stage_profile_read(hllm_b200_stage* stage, uint32_t kind, double* ms,
+                                              uint64_t* launches, double* bytes, double* flops) {
+  return guarded([&] {
+    if (!stage || kind >= static_cast<uint32_t>(hllm_b200_stage::kProfKinds))
+      fail(HLLM_B200_INVALID_REQUEST, "bad argument");
+    std::scoped_lock lock(stage->mutex);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    check_cuda(cudaStreamSynchronize(stage->stream), "profile");
+    stage->prof_collect();
+    if (ms) *ms = stage->prof_ms[kind];
+    if (launches) *launches = stage->prof_n[kind];
+    if (bytes) *bytes = stage->prof_bytes[kind];
+    if (flops) *flops = stage->prof_flops[kind];
+  });
+}
+
 void* hllm_b200_stage_stream(hllm_b200_stage* stage) { return stage ? stage->stream : nullptr; }
 int32_t hllm_b200_stage_device(const hllm_b200_stage* stage) { return stage ? stage->device : -1; }
 uint32_t hllm_b200_stage_last_launches(const hllm_b200_stage* stage) {
   return stage ? stage->launches : 0;
+}
+
+hllm_b200_status hllm_b200_stage_last_transfer(const hllm_b200_stage* stage, uint64_t* h2d_bytes,
+                                               uint64_t* d2h_bytes) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    if (h2d_bytes) *h2d_bytes = stage->last_h2d;
+    if (d2h_bytes) *d2h_bytes = stage->last_d2h;
+  });
 }
 
 hllm_b200_status hllm_b200_seq_read_kv(hllm_b200_stage* stage, const hllm_b200_seq* seq,

@@ -187,6 +187,22 @@ void* hllm_b200_stage_stream(hllm_b200_stage* stage);
 int32_t hllm_b200_stage_device(const hllm_b200_stage* stage);
 /* Kernel launches of the last step (for launch accounting). */
 uint32_t hllm_b200_stage_last_launches(const hllm_b200_stage* stage);
+/* Host->device and device->host bytes the last step copied. */
+hllm_b200_status hllm_b200_stage_last_transfer(const hllm_b200_stage* stage, uint64_t* h2d_bytes,
+                                               uint64_t* d2h_bytes);
+
+/* Per-launch timing of the stage's kernels, for benchmarks.  enable != 0
+ * resets the counters and brackets every later launch with CUDA events on the
+ * stage stream; 0 stops.  Kernel classes: 0 projection GEMMs at decode width
+ * (<= 128 tokens), 1 projection GEMMs at prefill width, 2 decode attention
+ * (split + combine), 3 prefill attention, 4 all other kernels.  profile_read
+ * waits for the stream and returns a class's summed device milliseconds,
+ * launch count, and algorithmic bytes and FLOPs.  No reference counterpart;
+ * the reference times components with a host clock after a device
+ * synchronize (cpp/include/hllm/runtime/timing.hpp:26-47). */
+hllm_b200_status hllm_b200_stage_profile(hllm_b200_stage* stage, uint32_t enable);
+hllm_b200_status hllm_b200_stage_profile_read(hllm_b200_stage* stage, uint32_t kind, double* ms,
+                                              uint64_t* launches, double* bytes, double* flops);
 
 /* Reads back one layer's K or V for positions [0, length) of a sequence as
  * F16 [length][kv_heads][head_dim] (the reference's contiguous cache layout,

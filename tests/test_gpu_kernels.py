@@ -107,7 +107,8 @@ def test_rmsnorm_matches_oracle():
         w = (1 + 0.1 * rng.standard_normal(width)).astype(np.float32)
         ref = oracle.rms_norm(x, w, 1e-6)
         out = torch.zeros((rows, width + 64), dtype=torch.int16, device="cuda")
-        check(lib().hllm_b200_rmsnorm(ptr(dev(x)), rows, width, ptr(dev(w)), 1e-6, ptr(out),
+        xd, wd = dev(x), dev(w)  # keep device inputs alive until the kernel has run
+        check(lib().hllm_b200_rmsnorm(ptr(xd), rows, width, ptr(wd), 1e-6, ptr(out),
                                       width + 64, stream()))
         sync()
         got = f16_vals(host(out, np.uint16))
@@ -144,8 +145,9 @@ def test_pack_bit_exact_against_oracle(seed):
     cu_splits = torch.zeros(R + 1, dtype=torch.int32, device="cuda")
     cu_qtiles = torch.zeros(R + 1, dtype=torch.int32, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    check(lib().hllm_b200_pack(ptr(dev(row_slot)), ptr(dev(row_first)), ptr(dev(row_count)), R, T,
-                               ptr(dev(blocks)), MB, split, qt, ptr(o["cu_seqlens"]),
+    ins = [dev(x) for x in (row_slot, row_first, row_count, blocks)]
+    check(lib().hllm_b200_pack(ptr(ins[0]), ptr(ins[1]), ptr(ins[2]), R, T,
+                               ptr(ins[3]), MB, split, qt, ptr(o["cu_seqlens"]),
                                ptr(o["positions"]), ptr(o["slot_mapping"]), ptr(o["token_row"]),
                                ptr(o["seq_lens"]), ptr(o["block_tables"]), ptr(cu_splits),
                                ptr(cu_qtiles), ptr(status), stream()))
@@ -169,8 +171,9 @@ def test_pack_flags_missing_blocks():
     outs = [torch.zeros(n, dtype=torch.int32, device="cuda") for n in (R + 1, T, T, T, R, R * MB,
                                                                        R + 1, R + 1)]
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    check(lib().hllm_b200_pack(ptr(dev(row_slot)), ptr(dev(row_first)), ptr(dev(row_count)), R, T,
-                               ptr(dev(blocks)), MB, 64, 16, *[ptr(t) for t in outs], ptr(status),
+    ins = [dev(x) for x in (row_slot, row_first, row_count, blocks)]
+    check(lib().hllm_b200_pack(ptr(ins[0]), ptr(ins[1]), ptr(ins[2]), R, T,
+                               ptr(ins[3]), MB, 64, 16, *[ptr(t) for t in outs], ptr(status),
                                stream()))
     sync()
     assert int(host(status)[0]) != 0
@@ -194,9 +197,10 @@ def test_qkv_post_norm_rope_and_paged_write(hq, hkv, d, qk_norm):
     q_out = torch.zeros((T, hq * d), dtype=torch.int16, device="cuda")
     kc = torch.zeros((nblocks, hkv, 16, d), dtype=torch.int16, device="cuda")
     vc = torch.zeros_like(kc)
-    check(lib().hllm_b200_qkv_post(ptr(dev(qkv)), T, hq, hkv, d, ptr(dev(positions)),
-                                   ptr(dev(slots)), ptr(dev(qn)) if qk_norm else None,
-                                   ptr(dev(kn)) if qk_norm else None, 1e-6, ptr(dev(pw)),
+    ins = [dev(x) for x in (qkv, positions, slots, qn, kn, pw)]
+    check(lib().hllm_b200_qkv_post(ptr(ins[0]), T, hq, hkv, d, ptr(ins[1]), ptr(ins[2]),
+                                   ptr(ins[3]) if qk_norm else None,
+                                   ptr(ins[4]) if qk_norm else None, 1e-6, ptr(ins[5]),
                                    ptr(q_out), ptr(kc), ptr(vc), stream()))
     sync()
     q = qkv[:, :hq * d]
