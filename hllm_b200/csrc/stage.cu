@@ -170,8 +170,17 @@ struct hllm_b200_stage {
   hb::GemmScratch gscratch{};
 
   // pinned host staging
-  uint8_t* h_up = nullptr;
+  // Descriptor uploads go through a ring of pinned buffers so that enqueue-only
+  // steps never overwrite a buffer whose copy has not run; each slot's event
+  // marks its copy as consumed.
+  static constexpr int kUpRing = 8;
+  uint8_t* h_up_ring[kUpRing] = {};
+  cudaEvent_t up_done[kUpRing] = {};
+  int up_next = 0;
+  uint8_t* h_up = nullptr;  // the ring slot of the step being built
   uint8_t* h_down = nullptr;
+  int32_t* h_slot_rows = nullptr;             // pinned [max_seqs][max_blocks] block-list staging
+  std::vector<cudaEvent_t> slot_copy_done;    // per slot: its last staging copy has run
   __half* h_act = nullptr;  // boundary in/out staging [T_max][h]
 
   std::map<std::string, Target> targets;
@@ -208,9 +217,14 @@ struct hllm_b200_stage {
       cudaStreamSynchronize(stream);
       cudaStreamDestroy(stream);
     }
-    if (h_up) cudaFreeHost(h_up);
+    for (int i = 0; i < kUpRing; ++i) {
+      if (h_up_ring[i]) cudaFreeHost(h_up_ring[i]);
+      if (up_done[i]) cudaEventDestroy(up_done[i]);
+    }
     if (h_down) cudaFreeHost(h_down);
     if (h_act) cudaFreeHost(h_act);
+    if (h_slot_rows) cudaFreeHost(h_slot_rows);
+    for (auto e : slot_copy_done) cudaEventDestroy(e);
     for (auto* s : live) delete s;
     for (auto& e : prof_pending) {
       cudaEventDestroy(e.a);
@@ -477,9 +491,17 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
                                        static_cast<int>(s->h_pad), static_cast<int>(s->h_pad))))
     fail(HLLM_B200_INTERNAL, "tensor map creation failed");
 
-  check_cuda(cudaMallocHost(&s->h_up, s->up_bytes), "cudaMallocHost");
+  for (int i = 0; i < hllm_b200_stage::kUpRing; ++i) {
+    check_cuda(cudaMallocHost(&s->h_up_ring[i], s->up_bytes), "cudaMallocHost");
+    check_cuda(cudaEventCreateWithFlags(&s->up_done[i], cudaEventDisableTiming), "cudaEventCreate");
+  }
   check_cuda(cudaMallocHost(&s->h_down, 8 + R * sizeof(hb::SampleResult)), "cudaMallocHost");
   check_cuda(cudaMallocHost(&s->h_act, T * s->h * sizeof(__half)), "cudaMallocHost");
+  check_cuda(cudaMallocHost(&s->h_slot_rows, s->max_seqs * s->max_blocks * sizeof(int32_t)),
+             "cudaMallocHost");
+  s->slot_copy_done.resize(s->max_seqs);
+  for (auto& e : s->slot_copy_done)
+    check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
   check_cuda(cudaStreamSynchronize(s->stream), "stage setup");
 }
 
@@ -687,6 +709,10 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
   const int T = static_cast<int>(p.tokens);
   s->launches = 0;
   // ---- upload row descriptors (and ids / activations)
+  const int ring = s->up_next;
+  s->up_next = (s->up_next + 1) % hllm_b200_stage::kUpRing;
+  check_cuda(cudaEventSynchronize(s->up_done[ring]), "upload staging");
+  s->h_up = s->h_up_ring[ring];
   int32_t* hu = reinterpret_cast<int32_t*>(s->h_up);
   int t = 0;
   uint32_t si = 0;
@@ -716,6 +742,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
   }
   check_cuda(cudaMemcpyAsync(s->up, s->h_up, s->up_bytes, cudaMemcpyHostToDevice, s->stream),
              "descriptor upload");
+  check_cuda(cudaEventRecord(s->up_done[ring], s->stream), "upload staging");
   s->last_h2d = s->up_bytes + ((!s->desc.first && !device_input)
                                    ? static_cast<uint64_t>(T) * s->h * sizeof(__half) : 0);
   s->last_d2h = 0;
@@ -993,14 +1020,20 @@ hllm_b200_status hllm_b200_seq_alloc(hllm_b200_stage* stage, uint64_t tokens, hl
     seq->blocks.assign(stage->free_blocks.end() - static_cast<std::ptrdiff_t>(need),
                        stage->free_blocks.end());
     std::reverse(seq->blocks.begin(), seq->blocks.end());
-    std::vector<int32_t> row(stage->max_blocks, -1);
-    std::copy(seq->blocks.begin(), seq->blocks.end(), row.begin());
+    // The block list goes through the slot's own pinned staging row, copied in
+    // stream order ahead of any step that uses the sequence; the slot's event
+    // guards the staging row against reuse before its previous copy ran.
     check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    cudaEvent_t done = stage->slot_copy_done[seq->slot];
+    check_cuda(cudaEventSynchronize(done), "slot staging");
+    int32_t* row = stage->h_slot_rows + static_cast<size_t>(seq->slot) * stage->max_blocks;
+    std::fill(row, row + stage->max_blocks, -1);
+    std::copy(seq->blocks.begin(), seq->blocks.end(), row);
     check_cuda(cudaMemcpyAsync(stage->slot_blocks + static_cast<size_t>(seq->slot) * stage->max_blocks,
-                               row.data(), row.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                               row, stage->max_blocks * sizeof(int32_t), cudaMemcpyHostToDevice,
                                stage->stream),
                "block table upload");
-    check_cuda(cudaStreamSynchronize(stage->stream), "block table upload");
+    check_cuda(cudaEventRecord(done, stage->stream), "slot staging");
     stage->free_slots.pop_back();
     stage->free_blocks.resize(stage->free_blocks.size() - need);
     stage->live.insert(seq.get());

@@ -158,6 +158,14 @@ def ref():
         r.ref_float16_to_float.argtypes = [C.c_uint16]
         r.ref_combine_decode_tokens.argtypes = [_U64, _U64, _U64, C.POINTER(C.c_uint8),
                                                 C.POINTER(C.c_uint8), _I32, C.c_uint64, _U64]
+        r.ref_layer_new.restype = C.c_void_p
+        r.ref_layer_new.argtypes = [C.POINTER(Layer), C.POINTER(Config)]
+        r.ref_layer_free.argtypes = [C.c_void_p]
+        r.ref_layer_forward.argtypes = [C.c_void_p, _F, C.c_uint64, C.c_uint64, C.c_void_p, _F]
+        r.ref_head_new.restype = C.c_void_p
+        r.ref_head_new.argtypes = [_F, _F, C.c_uint64, C.c_uint64]
+        r.ref_head_free.argtypes = [C.c_void_p]
+        r.ref_head_logits.argtypes = [C.c_void_p, _F, C.c_uint64, C.c_float, _F]
         _ref = r
     return _ref
 
@@ -388,6 +396,23 @@ class OracleModel:
                     arrs[kind] = np.ascontiguousarray(f32[name], np.float32)
             lw = Layer(**{k: fp(v) for k, v in arrs.items()})
             self.layers.append((lw, arrs))
+        self._ref_layers = []
+        self._ref_head = None
+        if use_ref:
+            for lw, _ in self.layers:
+                handle = ref().ref_layer_new(C.byref(lw), C.byref(self.cfg))
+                if not handle:
+                    raise MemoryError("reference layer construction failed")
+                self._ref_layers.append(handle)
+
+    def __del__(self):
+        r = _ref
+        if r is None:
+            return
+        for h in getattr(self, "_ref_layers", []):
+            r.ref_layer_free(h)
+        if getattr(self, "_ref_head", None):
+            r.ref_head_free(self._ref_head)
 
     def new_sequence(self, capacity: int) -> OracleSequence:
         s = self.spec
@@ -415,11 +440,11 @@ class OracleModel:
     def forward(self, hidden: np.ndarray, position: int, seq: OracleSequence, trace=None):
         hidden = np.ascontiguousarray(hidden, np.float32)
         rows = hidden.shape[0]
-        for (lw, _), cache in zip(self.layers, seq.caches):
+        for li, ((lw, _), cache) in enumerate(zip(self.layers, seq.caches)):
             out = np.empty_like(hidden)
             if self.use_ref:
-                st = ref().ref_transformer_layer(fp(hidden), rows, C.byref(lw), C.byref(self.cfg),
-                                                 position, cache, fp(out))
+                st = ref().ref_layer_forward(self._ref_layers[li], fp(hidden), rows, position, cache,
+                                             fp(out))
             else:
                 st = lib().oracle_transformer_layer(fp(hidden), rows, C.byref(lw),
                                                     C.byref(self.cfg), position, C.byref(cache),
@@ -440,9 +465,17 @@ class OracleModel:
         head = np.ascontiguousarray(self.head_matrix(), np.float32)
         norm = np.ascontiguousarray(self.w["model.norm.weight"], np.float32)
         out = np.empty((hidden_rows.shape[0], head.shape[0]), np.float32)
-        fn = ref().ref_final_logits if self.use_ref else lib().oracle_final_logits
-        fn(fp(hidden_rows), hidden_rows.shape[0], hidden_rows.shape[1], fp(norm), fp(head),
-           head.shape[0], self.spec.rms_norm_epsilon, fp(out))
+        if self.use_ref:
+            if self._ref_head is None:
+                self._ref_head = ref().ref_head_new(fp(norm), fp(head), head.shape[0], head.shape[1])
+            st = ref().ref_head_logits(self._ref_head, fp(hidden_rows), hidden_rows.shape[0],
+                                       self.spec.rms_norm_epsilon, fp(out))
+            if st != 0:
+                raise ValueError(f"reference head rejected input (status {st})")
+            return out
+        lib().oracle_final_logits(fp(hidden_rows), hidden_rows.shape[0], hidden_rows.shape[1],
+                                  fp(norm), fp(head), head.shape[0], self.spec.rms_norm_epsilon,
+                                  fp(out))
         return out
 
     def kv(self, seq: OracleSequence, layer: int):

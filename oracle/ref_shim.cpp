@@ -130,6 +130,70 @@ int ref_transformer_layer(const float* input, std::uint64_t rows, const RefLayer
   }
 }
 
+// Persistent forms: the layer weights / LM head are converted into the
+// reference's Matrix objects once, so that timing a call measures the
+// reference's math rather than the shim's copies.
+struct RefLayerHandle {
+  LlamaConfig config;
+  LayerWeights weights;
+};
+void* ref_layer_new(const RefLayer* w, const RefConfig* cfg) {
+  try {
+    const auto c = config(*cfg);
+    const auto h = c.hidden_size, I = c.intermediate_size;
+    const auto qw = c.attention_heads * c.head_dimension;
+    const auto kw = c.key_value_heads * c.head_dimension;
+    return new RefLayerHandle{
+        c,
+        LayerWeights{vec(w->input_norm, h), matrix(w->query, qw, h), matrix(w->key, kw, h),
+                     matrix(w->value, kw, h), matrix(w->attention_output, h, qw),
+                     vec(w->post_attention_norm, h), matrix(w->gate, I, h), matrix(w->up, I, h),
+                     matrix(w->down, h, I),
+                     c.query_key_norm ? vec(w->query_norm, c.head_dimension) : std::vector<float>{},
+                     c.query_key_norm ? vec(w->key_norm, c.head_dimension) : std::vector<float>{}}};
+  } catch (...) {
+    return nullptr;
+  }
+}
+void ref_layer_free(void* handle) { delete static_cast<RefLayerHandle*>(handle); }
+int ref_layer_forward(void* handle, const float* input, std::uint64_t rows,
+                      std::uint64_t first_position, void* cache, float* output) {
+  try {
+    auto* L = static_cast<RefLayerHandle*>(handle);
+    const auto out = hllm::cpu::transformer_layer(matrix(input, rows, L->config.hidden_size),
+                                                  L->weights, L->config, first_position,
+                                                  *static_cast<LayerKvCache*>(cache));
+    std::memcpy(output, out.values().data(), sizeof(float) * out.size());
+    return 0;
+  } catch (const std::exception& e) {
+    return status_of(e);
+  }
+}
+struct RefHeadHandle {
+  std::vector<float> norm;
+  Matrix head;
+};
+void* ref_head_new(const float* norm, const float* head, std::uint64_t vocab, std::uint64_t h) {
+  try {
+    return new RefHeadHandle{vec(norm, h), matrix(head, vocab, h)};
+  } catch (...) {
+    return nullptr;
+  }
+}
+void ref_head_free(void* handle) { delete static_cast<RefHeadHandle*>(handle); }
+int ref_head_logits(void* handle, const float* hidden, std::uint64_t rows, float eps,
+                    float* logits) {
+  try {
+    auto* H = static_cast<RefHeadHandle*>(handle);
+    const auto out = hllm::cpu::final_logits(matrix(hidden, rows, H->norm.size()), H->norm,
+                                             H->head, eps);
+    std::memcpy(logits, out.values().data(), sizeof(float) * out.size());
+    return 0;
+  } catch (const std::exception& e) {
+    return status_of(e);
+  }
+}
+
 int ref_final_logits(const float* hidden, std::uint64_t rows, std::uint64_t h,
                      const float* norm, const float* head, std::uint64_t vocab, float eps,
                      float* logits) {
