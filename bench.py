@@ -176,6 +176,7 @@ def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, cl
     seqs = {}
     stream = torch.cuda.ExternalStream(L.hllm_b200_stage_stream(stage.handle))
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    greedy = _lib.Sampling(0.0, 1.0, 0, 0, 0, 0)
     tokens = launches = 0
     for i, (admits, rows, fin) in enumerate(steps):
         if i == first_timed:
@@ -194,6 +195,7 @@ def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, cl
             arr[j].first_position = first
             arr[j].tokens = count
             arr[j].sample = int(sample)
+            arr[j].sampling = greedy
         _lib.check(L.hllm_b200_step_async(stage.handle, arr, len(rows), base + 4 * offsets[i]))
         if i >= first_timed:
             tokens += sum(r[2] for r in rows)

@@ -39,6 +39,41 @@ __device__ __forceinline__ int find_row(const int32_t* cu, int rows, int idx) {
   return lo;
 }
 
+// ---------------------------------------------------------------- warp-level MMA helpers
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+
 // ---------------------------------------------------------------- decode
 __global__ void __launch_bounds__(kDecThreads)
     decode_attn_kernel(const AttnArgs a) {
@@ -203,6 +238,154 @@ __global__ void __launch_bounds__(kDecThreads)
   }
 }
 
+// ---------------------------------------------------------------- decode (tensor cores)
+// One warp per (decode row, kv head, context split); four independent warps
+// per CTA, no CTA-wide synchronisation.  The G query heads of the kv head are
+// the first G rows of an m16n8k16 tile (rows G..15 are zero), so QK^T and PV
+// run on the tensor cores; K/V pages (16 keys x d) stream through a per-warp
+// cp.async ring in an XOR-swizzled layout that ldmatrix reads without bank
+// conflicts.  Partial (m, l, O) per split go to the combine pass.
+constexpr int kWarpStages = 3;
+
+template <int D>
+__device__ __forceinline__ uint32_t page_off(int row, int chunk) {
+  return static_cast<uint32_t>(row * D * 2 + ((chunk ^ (row & 7)) * 16));
+}
+
+template <int D>
+__global__ void __launch_bounds__(128)
+    decode_attn_mma_kernel(const AttnArgs a, int total_items) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr uint32_t kPage = 16 * D * 2;  // bytes of one K (or V) page
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int item = blockIdx.x * 4 + warp;
+  if (item >= total_items) return;
+  const int kvh = item % a.hkv;
+  const int split = item / a.hkv;
+  const int r = find_row(a.cu_splits, a.rows, split);
+  if (a.row_count[r] != 1) return;
+  const int G = a.hq / a.hkv;
+  const int d = a.dim;
+  const int ctx = a.seq_lens[r];
+  const int key0 = (split - a.cu_splits[r]) * a.split_tokens;
+  const int key1 = min(ctx, key0 + a.split_tokens);
+  const int kb0 = key0 >> 4;
+  const int npage = ((key1 + 15) >> 4) - kb0;
+  const int t = a.cu_seqlens[r];
+  const int32_t* table = a.block_tables + static_cast<size_t>(r) * a.max_blocks;
+  uint8_t* ring = smem + warp * (kWarpStages * 2 * kPage);
+
+  auto issue = [&](int i) {
+    uint8_t* kd = ring + (i % kWarpStages) * 2 * kPage;
+    const int bid = table[kb0 + i];
+    if (bid < 0) {
+      if (lane == 0) atomicOr(a.status, kDevBadIndex);
+      return;
+    }
+    const size_t page = (static_cast<size_t>(bid) * a.hkv + kvh) * 16 * D;
+    const __half* ks = a.k_cache + page;
+    const __half* vs = a.v_cache + page;
+    const uint32_t kb = smem_u32(kd), vb = kb + kPage;
+    constexpr int kChunks = 16 * D / 8;  // 16-byte chunks per page
+#pragma unroll
+    for (int c = lane; c < kChunks; c += 32) {
+      const int row = c / (D / 8), ch = c % (D / 8);
+      cp_async16(kb + page_off<D>(row, ch), ks + row * D + ch * 8);
+      cp_async16(vb + page_off<D>(row, ch), vs + row * D + ch * 8);
+    }
+  };
+
+  // Q as A fragments (rows = heads of the group; rows >= G are zero).
+  const int g = lane >> 2;
+  uint32_t qa[D / 16][2];
+  {
+    const __half* qrow = a.q + static_cast<size_t>(t) * a.hq * d + static_cast<size_t>(kvh * G + g) * d;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int col = kk * 16 + (lane & 3) * 2;
+      qa[kk][0] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + col) : 0u;
+      qa[kk][1] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + col + 8) : 0u;
+    }
+  }
+  const float sl2 = a.scale * kLog2e;
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[i][e] = 0.f;
+  float m = -INFINITY, l = 0.f;
+
+#pragma unroll
+  for (int i = 0; i < kWarpStages - 1; ++i) {
+    if (i < npage) issue(i);
+    cp_async_commit();
+  }
+  for (int i = 0; i < npage; ++i) {
+    if (i + kWarpStages - 1 < npage) issue(i + kWarpStages - 1);
+    cp_async_commit();
+    cp_async_wait<kWarpStages - 1>();
+    __syncwarp();
+    const uint32_t kb = smem_u32(ring + (i % kWarpStages) * 2 * kPage), vb = kb + kPage;
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t b0, b1, b2, b3;
+      const int key = (lane & 7) + (lane >> 4) * 8;
+      ldsm_x4(kb + page_off<D>(key, kk * 2 + ((lane >> 3) & 1)), b0, b1, b2, b3);
+      mma16816(s[0], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
+      mma16816(s[1], qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
+    }
+    const int base = (kb0 + i) * 16;
+    float mx = m;
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = base + nb * 8 + (lane & 3) * 2 + e;
+        const float v = (key >= key0 && key < key1) ? s[nb][e] * sl2 : -INFINITY;
+        s[nb][e] = v;
+        mx = fmaxf(mx, v);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float alpha = exp2f(m - mx);
+    m = mx;
+    const float p00 = exp2f(s[0][0] - m), p01 = exp2f(s[0][1] - m);
+    const float p10 = exp2f(s[1][0] - m), p11 = exp2f(s[1][1] - m);
+    l = l * alpha + (p00 + p01 + p10 + p11);
+    const uint32_t pa0 = pack_half2(p00, p01), pa2 = pack_half2(p10, p11);
+#pragma unroll
+    for (int db = 0; db < D / 8; ++db) {
+      o[db][0] *= alpha;
+      o[db][1] *= alpha;
+    }
+#pragma unroll
+    for (int db = 0; db < D / 8; db += 2) {
+      uint32_t b0, b1, b2, b3;
+      const int key = (lane & 7) + ((lane >> 3) & 1) * 8;
+      ldsm_x4_t(vb + page_off<D>(key, db + (lane >> 4)), b0, b1, b2, b3);
+      mma16816(o[db], pa0, 0u, pa2, 0u, b0, b1);
+      mma16816(o[db + 1], pa0, 0u, pa2, 0u, b2, b3);
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  if (g < G) {
+    const int h = kvh * G + g;
+    float* dst = a.part_o + (static_cast<size_t>(split) * a.hq + h) * d;
+#pragma unroll
+    for (int db = 0; db < D / 8; ++db)
+      *reinterpret_cast<float2*>(dst + db * 8 + (lane & 3) * 2) = make_float2(o[db][0], o[db][1]);
+    if ((lane & 3) == 0) {
+      float* ml = a.part_ml + (static_cast<size_t>(split) * a.hq + h) * 2;
+      ml[0] = m * 0.6931471805599453f;  // back to the natural-log domain of the combine pass
+      ml[1] = l;
+    }
+  }
+}
+
 // One CTA per (decode row, query head): merge the row's splits.
 __global__ void decode_combine_kernel(const AttnArgs a) {
   const int r = blockIdx.x, h = blockIdx.y;
@@ -228,39 +411,6 @@ __global__ void decode_combine_kernel(const AttnArgs a) {
 }
 
 // ---------------------------------------------------------------- prefill
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
-      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
 // Byte offset of 16-byte chunk c of row `row` in a [rows][DP] F16 tile, with an
 // XOR swizzle over the low three chunk bits so ldmatrix rows hit distinct banks.
 template <int DP>
@@ -497,6 +647,22 @@ cudaError_t launch_prefill(const AttnArgs& a, int total_qtiles, cudaStream_t str
   return cudaGetLastError();
 }
 
+template <int D>
+cudaError_t launch_decode_mma(const AttnArgs& a, int total_splits, cudaStream_t stream) {
+  constexpr size_t kSmem = 4 * kWarpStages * 2 * (16 * D * 2);
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(decode_attn_mma_kernel<D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const int items = total_splits * a.hkv;
+  decode_attn_mma_kernel<D><<<(items + 3) / 4, 128, kSmem, stream>>>(a, items);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 int attn_qtile_tokens(int group) { return 64 / group; }
@@ -507,18 +673,26 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t
   if (G > kMaxGroup || a.dim % 4 != 0 || a.dim > 256 || G * a.dim / 4 > 4 * kDecThreads ||
       a.split_tokens % 16 != 0)
     return cudaErrorInvalidValue;
-  const size_t smem = kDecStages * 2 * 16 * a.dim * 2 +
-                      (G * a.dim + 2 * G * 16 + 3 * kMaxGroup) * sizeof(float) + 8 +
-                      kDecStages * sizeof(uint64_t);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    if (e != cudaSuccess) return e;
-    configured = true;
+  cudaError_t e;
+  if (a.dim == 64 || a.dim == 128 || a.dim == 256) {
+    e = a.dim == 64    ? launch_decode_mma<64>(a, total_splits, stream)
+        : a.dim == 128 ? launch_decode_mma<128>(a, total_splits, stream)
+                       : launch_decode_mma<256>(a, total_splits, stream);
+  } else {
+    // Other head sizes (e.g. the tiny fixtures): one CTA per (kv head, split).
+    const size_t smem = kDecStages * 2 * 16 * a.dim * 2 +
+                        (G * a.dim + 2 * G * 16 + 3 * kMaxGroup) * sizeof(float) + 8 +
+                        kDecStages * sizeof(uint64_t);
+    static bool configured = false;
+    if (!configured) {
+      e = cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               96 * 1024);
+      if (e != cudaSuccess) return e;
+      configured = true;
+    }
+    decode_attn_kernel<<<dim3(a.hkv, total_splits), kDecThreads, smem, stream>>>(a);
+    e = cudaGetLastError();
   }
-  decode_attn_kernel<<<dim3(a.hkv, total_splits), kDecThreads, smem, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   decode_combine_kernel<<<dim3(a.rows, a.hq), 128, 0, stream>>>(a);
   return cudaGetLastError();

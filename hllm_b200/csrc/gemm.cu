@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // Epilogue: thread t owns TMEM lane t = output feature m_tile*128 + t.
     const int t = threadIdx.x;
+    float red0[16], red1[16];
     uint32_t seg = 0;
     for (long long u = ub; u < ue; ++seg) {
       const int tile = static_cast<int>(u / KB);
@@ -260,15 +261,47 @@ __global__ void __launch_bounds__(192, 1)
         named_bar_sync(1, 128);
         if (*last_flag) {
           __threadfence();
-          for (int col = 0; col < nvalid; ++col) {
-            float a0 = 0.f, a1 = 0.f;
-            for (int c = c_first; c <= c_last; ++c) {
-              const int sl = 2 * c + (unit_begin(p.units, grid, c) >= tile_u0 ? 0 : 1);
-              const float* src = p.partials + static_cast<size_t>(sl) * NA * BN * 128;
-              a0 += __ldcg(src + col * 128 + t);
-              if (NA == 2) a1 += __ldcg(src + (BN + col) * 128 + t);
+          // Sum the tile's partials in CTA order.  Loads are issued in batches
+          // (16 columns x up to 8 segments per accumulator) before any add, so
+          // the reduction is bound by L2 bandwidth rather than load latency.
+          constexpr int kCols = 16, kSegs = 8;
+          for (int col0 = 0; col0 < nvalid; col0 += kCols) {
+            for (int acc_i = 0; acc_i < NA; ++acc_i) {
+              float sum[kCols];
+#pragma unroll
+              for (int j = 0; j < kCols; ++j) sum[j] = 0.f;
+              for (int c0 = c_first; c0 <= c_last; c0 += kSegs) {
+                float v[kSegs][kCols];
+#pragma unroll
+                for (int sidx = 0; sidx < kSegs; ++sidx) {
+                  const int c = c0 + sidx;
+                  if (c <= c_last) {
+                    const int sl = 2 * c + (unit_begin(p.units, grid, c) >= tile_u0 ? 0 : 1);
+                    const float* src = p.partials + static_cast<size_t>(sl) * NA * BN * 128 +
+                                       static_cast<size_t>(acc_i * BN + col0) * 128 + t;
+#pragma unroll
+                    for (int j = 0; j < kCols; ++j)
+                      v[sidx][j] = (col0 + j < nvalid) ? __ldcg(src + j * 128) : 0.f;
+                  }
+                }
+#pragma unroll
+                for (int sidx = 0; sidx < kSegs; ++sidx)
+                  if (c0 + sidx <= c_last)
+#pragma unroll
+                    for (int j = 0; j < kCols; ++j) sum[j] += v[sidx][j];
+              }
+              if (acc_i == 0) {
+#pragma unroll
+                for (int j = 0; j < kCols; ++j) red0[j] = sum[j];
+              } else {
+#pragma unroll
+                for (int j = 0; j < kCols; ++j) red1[j] = sum[j];
+              }
             }
-            if (m < p.m) apply_epilogue(p, n0 + col, m, a0, a1);
+#pragma unroll
+            for (int j = 0; j < kCols; ++j)
+              if (col0 + j < nvalid && m < p.m)
+                apply_epilogue(p, n0 + col0 + j, m, red0[j], NA == 2 ? red1[j] : 0.f);
           }
           if (t == 0) p.counters[tile] = 0u;
         }

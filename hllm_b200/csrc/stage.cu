@@ -638,9 +638,10 @@ StepPlan plan_step(hllm_b200_stage* s, const hllm_b200_row* rows, uint32_t n, bo
     }
   }
   if (p.tokens > s->T_max) fail(HLLM_B200_RESOURCE_EXHAUSTED, "step exceeds max_step_tokens");
-  // Decode split size: enough context splits to cover ~2 CTAs per SM across
-  // the KV heads, at least 64 keys each, within the split workspace.
-  const uint64_t target = std::max<uint64_t>(1, (2ull * s->sm_count) / s->hkv);
+  // Decode split size: one warp handles one (row, kv head, split); aim for
+  // about 16 such items per SM so that rows of very different lengths still
+  // balance, with at least 64 keys per split, within the split workspace.
+  const uint64_t target = std::max<uint64_t>(1, (16ull * s->sm_count) / s->hkv);
   uint64_t split = std::max<uint64_t>(64, round_up((decode_keys + target - 1) / target, 16));
   auto count_splits = [&](uint64_t sp) {
     uint64_t total = 0;
