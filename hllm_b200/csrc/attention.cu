@@ -390,23 +390,47 @@ __global__ void __launch_bounds__(128)
 __global__ void decode_combine_kernel(const AttnArgs a) {
   const int r = blockIdx.x, h = blockIdx.y;
   if (a.row_count[r] != 1) return;
-  const int s0 = a.cu_splits[r], s1 = a.cu_splits[r + 1];
+  const int s0 = a.cu_splits[r], ns = a.cu_splits[r + 1] - s0;
   const int d = a.dim;
+  constexpr int kMaxW = 1024;
+  __shared__ float w[kMaxW];
+  __shared__ float red[32];
+  // max of the split maxima
   float m = -INFINITY;
-  for (int s = s0; s < s1; ++s) m = fmaxf(m, a.part_ml[(static_cast<size_t>(s) * a.hq + h) * 2]);
+  for (int s = threadIdx.x; s < ns; s += blockDim.x)
+    m = fmaxf(m, a.part_ml[(static_cast<size_t>(s0 + s) * a.hq + h) * 2]);
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = red[0];
+  for (int i = 1; i < static_cast<int>(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+  __syncthreads();
+  // split weights exp(m_s - m) and the merged denominator
   float l = 0.f;
-  for (int s = s0; s < s1; ++s) {
-    const float* ml = a.part_ml + (static_cast<size_t>(s) * a.hq + h) * 2;
-    l += ml[1] * expf(ml[0] - m);
+  for (int s = threadIdx.x; s < ns; s += blockDim.x) {
+    const float* ml = a.part_ml + (static_cast<size_t>(s0 + s) * a.hq + h) * 2;
+    const float ws = expf(ml[0] - m);
+    if (s < kMaxW) w[s] = ws;
+    l += ml[1] * ws;
   }
+  l = warp_sum(l);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = l;
+  __syncthreads();
+  l = 0.f;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) l += red[i];
+  const float inv = 1.0f / l;
   const int t = a.cu_seqlens[r];
+  const float* po = a.part_o + (static_cast<size_t>(s0) * a.hq + h) * d;
+  const size_t sstride = static_cast<size_t>(a.hq) * d;
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
     float o = 0.f;
-    for (int s = s0; s < s1; ++s) {
-      const float w = expf(a.part_ml[(static_cast<size_t>(s) * a.hq + h) * 2] - m);
-      o += a.part_o[(static_cast<size_t>(s) * a.hq + h) * d + i] * w;
+#pragma unroll 8
+    for (int s = 0; s < ns; ++s) {
+      const float ws =
+          s < kMaxW ? w[s] : expf(a.part_ml[(static_cast<size_t>(s0 + s) * a.hq + h) * 2] - m);
+      o += po[s * sstride + i] * ws;
     }
-    a.out[static_cast<size_t>(t) * a.ld_out + h * d + i] = __float2half_rn(o / l);
+    a.out[static_cast<size_t>(t) * a.ld_out + h * d + i] = __float2half_rn(o * inv);
   }
 }
 

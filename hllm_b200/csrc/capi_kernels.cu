@@ -33,42 +33,34 @@ hllm_b200_status cuda_status(cudaError_t e) {
   return e == cudaErrorInvalidValue ? HLLM_B200_INVALID_REQUEST : HLLM_B200_INTERNAL;
 }
 
-// GEMM scratch owned by the library, one per device, allocated on first use.
+// GEMM slot storage owned by the library, one per device, allocated on first
+// use and kept until the process exits.
 struct DeviceScratch {
-  hb::GemmScratch gemm{};
-  size_t counters_for_tiles = 0;
+  float* slots = nullptr;
+  uint32_t* status = nullptr;
+  int sm_count = 0;
 };
 std::mutex g_scratch_mutex;
 std::map<int, DeviceScratch> g_scratch;
 
-hllm_b200_status scratch_for_device(hb::GemmScratch* out, size_t tiles) {
+hllm_b200_status scratch_for_device(DeviceScratch* out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
   std::scoped_lock lock(g_scratch_mutex);
   DeviceScratch& s = g_scratch[dev];
-  if (!s.gemm.partials) {
-    int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return cuda_status(e);
-    s.gemm.sm_count = sms;
-    s.gemm.partial_floats = hb::gemm_partial_floats(sms);
-    e = cudaMalloc(&s.gemm.partials, s.gemm.partial_floats * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&s.gemm.status, 256);
-    if (e == cudaSuccess) e = cudaMemset(s.gemm.status, 0, 256);
-    if (e != cudaSuccess) return cuda_status(e);
+  if (!s.slots) {
+    e = cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaMalloc(&s.slots, hb::gemm_max_slot_floats(s.sm_count) * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&s.status, 256);
+    if (e == cudaSuccess) e = cudaMemset(s.status, 0, 256);
+    if (e != cudaSuccess) {
+      s.slots = nullptr;
+      return cuda_status(e);
+    }
   }
-  if (s.counters_for_tiles < tiles) {
-    if (s.gemm.counters) cudaFree(s.gemm.counters);
-    s.gemm.counters = nullptr;
-    const size_t n = std::max<size_t>(tiles, 4096);
-    e = cudaMalloc(&s.gemm.counters, n * sizeof(unsigned));
-    if (e == cudaSuccess) e = cudaMemset(s.gemm.counters, 0, n * sizeof(unsigned));
-    if (e != cudaSuccess) return cuda_status(e);
-    s.counters_for_tiles = n;
-    s.gemm.counter_count = n;
-  }
-  *out = s.gemm;
+  *out = s;
   return HLLM_B200_OK;
 }
 
@@ -80,7 +72,7 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
                                 uint64_t second_row, const void* x, uint64_t n, uint32_t epilogue,
                                 void* y, uint64_t ldy, uint32_t bn, uint32_t grid, void* stream) {
   if (!w || !x || !y || m == 0 || n == 0 || k_pad == 0 || k_pad % 64 != 0 || epilogue > 3 ||
-      (pair != 1 && pair != 2))
+      (pair != 1 && pair != 2) || (pair == 2) != (epilogue == 3))
     return HLLM_B200_INVALID_REQUEST;
   hb::GemmWeight gw{};
   const int rows_total = pair == 2 ? static_cast<int>(second_row + m) : static_cast<int>(m);
@@ -91,13 +83,19 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
   if (!hb::gemm_make_input(&gx, x, static_cast<int>(n), static_cast<int>(k_pad),
                            static_cast<int>(k_pad)))
     return HLLM_B200_INTERNAL;
-  hb::GemmScratch sc{};
-  const size_t tiles = ((m + 127) / 128) * ((n + 15) / 16);
-  const hllm_b200_status st = scratch_for_device(&sc, tiles);
+  DeviceScratch sc;
+  const hllm_b200_status st = scratch_for_device(&sc);
   if (st != HLLM_B200_OK) return st;
-  return cuda_status(hb::gemm_run(gw, gx, static_cast<int>(n), static_cast<int>(epilogue), y,
-                                  static_cast<int>(ldy), sc, static_cast<cudaStream_t>(stream),
-                                  static_cast<int>(bn), static_cast<int>(grid)));
+  const hb::GemmPlan plan = hb::gemm_plan(gw, static_cast<int>(n), sc.sm_count,
+                                          static_cast<int>(bn), static_cast<int>(grid));
+  hb::GemmSlots slots{};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = hb::gemm_launch(gw, gx, static_cast<int>(n), plan, static_cast<int>(epilogue), y,
+                                  static_cast<int>(ldy), sc.slots, &slots, sc.status, s);
+  if (e == cudaSuccess && plan.stream_k)
+    e = hb::gemm_finish_launch(slots, static_cast<int>(n), static_cast<int>(epilogue), y,
+                               static_cast<int>(ldy), s);
+  return cuda_status(e);
 }
 
 hllm_b200_status hllm_b200_rmsnorm(const float* x, uint64_t rows, uint64_t width, const float* w,
@@ -171,18 +169,34 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
   a.out = reinterpret_cast<__half*>(out);
   a.ld_out = static_cast<int>(ld_out);
   a.status = status;
-  float* part_o = nullptr;
-  float* part_ml = nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (total_splits) {
-    cudaError_t e = cudaMallocAsync(&part_o, static_cast<size_t>(total_splits) * hq * dim * 4, st);
-    if (e == cudaSuccess) e = cudaMallocAsync(&part_ml, static_cast<size_t>(total_splits) * hq * 8, st);
+    // Split outputs live in a grow-only buffer per device, kept for the process.
+    static std::mutex mu;
+    static std::map<int, std::pair<float*, size_t>> buffers;
+    const size_t need = static_cast<size_t>(total_splits) * hq * (dim + 2);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_status(e);
-    a.part_o = part_o;
-    a.part_ml = part_ml;
+    float* base = nullptr;
+    {
+      std::scoped_lock lock(mu);
+      auto& buf = buffers[dev];
+      if (buf.second < need) {
+        if (buf.first) {
+          cudaStreamSynchronize(st);
+          cudaFree(buf.first);
+        }
+        buf = {nullptr, 0};
+        e = cudaMalloc(&buf.first, need * sizeof(float));
+        if (e != cudaSuccess) return cuda_status(e);
+        buf.second = need;
+      }
+      base = buf.first;
+    }
+    a.part_o = base;
+    a.part_ml = base + static_cast<size_t>(total_splits) * hq * dim;
     e = hb::attn_decode_launch(a, static_cast<int>(total_splits), st);
-    cudaFreeAsync(part_o, st);
-    cudaFreeAsync(part_ml, st);
     if (e != cudaSuccess) return cuda_status(e);
   }
   return cuda_status(hb::attn_prefill_launch(a, static_cast<int>(total_qtiles), st));

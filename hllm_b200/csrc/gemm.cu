@@ -1,24 +1,21 @@
-// gemm.cu -- tcgen05 / TMEM projection GEMM with stream-K work split.
+// gemm.cu -- tcgen05 / TMEM projection GEMM (direct and stream-K work splits).
 //
 // Reference op: `linear` (cpp/src/cpu/tensor.cpp:47-62) as used for the q/k/v,
 // o, gate/up, down and LM-head projections (cpp/src/cpu/llama.cpp:242-288);
 // the reference CUDA worker issues these as cuBLAS GEMMs
 // (cpp/src/cuda/stage.cpp:306-338, 415-419).
 //
-// Design (one CTA per SM, persistent over a contiguous range of work units):
-//   * a work unit is one 64-wide K block of one output tile (128 weight rows x
-//     BN tokens); units are ordered tile-major, tiles token-tile-fastest, and
-//     CTA c takes units [U*c/G, U*(c+1)/G).  Tiles that straddle CTAs leave
-//     F32 partial tiles in scratch; the last CTA to finish a tile (arrival
-//     counter) sums them in CTA order -- a fixed order, so results do not
-//     depend on timing -- and applies the epilogue.  Nothing waits on another
-//     CTA.
-//   * warp 4: TMA producer (weights with L2 evict-first, tokens evict-last)
-//     into a STAGES-deep ring of 128B-swizzled tiles;
-//     warp 5: TMEM allocation and the single-thread tcgen05.mma issue loop,
-//     double-buffered accumulators when they fit in 512 TMEM columns;
-//     warps 0-3: epilogue, one TMEM lane (= one output feature) per thread,
-//     fused residual add / SwiGLU / F16 store.
+// Per CTA (192 threads, one CTA per SM):
+//   warp 4: TMA producer -- 128B-swizzled weight tiles (L2 evict-first) and
+//           token tiles (evict-last) into a STAGES-deep shared-memory ring;
+//   warp 5: TMEM allocation and the single-thread tcgen05.mma issue loop into
+//           double-buffered TMEM accumulators (when they fit 512 columns);
+//   warps 0-3: epilogue, one TMEM lane (= one output feature) per thread.
+// Work: a unit is one 64-wide K block of one output tile (128 weight rows x
+// BN tokens), tiles token-tile-fastest.  Direct plans give each CTA whole
+// tiles (c, c + G, ...) and apply the epilogue; stream-K plans give CTA c the
+// units [U*c/G, U*(c+1)/G) and store each segment's F32 sums in the CTA's slot
+// for that tile (see gemm.cuh).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -35,13 +32,14 @@ struct GemmParams {
   int n;             // tokens
   int kb_count;      // K blocks
   int n_tiles;
+  long long tiles;
   long long units;   // tiles * kb_count
+  int stream_k;
   int second_row;
   int epilogue;
   void* out;
   int ldo;
-  float* partials;
-  unsigned* counters;
+  float* slots;
   uint32_t* status;
 };
 
@@ -56,23 +54,38 @@ struct GemmShape {
   static constexpr uint32_t kABytes = kGemmBlockM * kGemmBlockK * 2;  // 16 KB
   static constexpr uint32_t kBBytes = BN * kGemmBlockK * 2;
   static constexpr uint32_t kStageBytes = NA * kABytes + kBBytes;
-  static constexpr int kStages = std::min<int>(8, (200 * 1024) / kStageBytes);
+  static constexpr int kStages = (200 * 1024) / kStageBytes < 8 ? (200 * 1024) / kStageBytes : 8;
   static constexpr int kAccBufs = (2 * NA * BN <= 512) ? 2 : 1;
   static constexpr uint32_t kTmemCols = pow2_at_least(kAccBufs * NA * BN);
   static constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256;
 };
 
-__host__ __device__ __forceinline__ long long min_ll(long long a, long long b) { return a < b ? a : b; }
-
-__device__ __forceinline__ long long unit_begin(long long units, int grid, int c) {
-  return units * c / grid;
+__host__ __device__ __forceinline__ long long min_ll(long long a, long long b) {
+  return a < b ? a : b;
 }
-// The CTA whose range holds unit u.
-__device__ __forceinline__ int cta_of_unit(long long units, int grid, long long u) {
-  int c = static_cast<int>((u * grid) / units);
-  while (c + 1 < grid && unit_begin(units, grid, c + 1) <= u) ++c;
-  while (c > 0 && unit_begin(units, grid, c) > u) --c;
-  return c;
+
+// Segment j of this CTA's work: tile and K-block range.  Returns false past
+// the last segment.
+struct Segment {
+  int tile, kb0, kb1;
+  long long next;  // stream-K: first unit after this segment
+};
+__device__ __forceinline__ bool next_segment(const GemmParams& p, long long& cursor, long long end,
+                                             int j, Segment& s) {
+  if (!p.stream_k) {
+    const long long tile = blockIdx.x + static_cast<long long>(j) * gridDim.x;
+    if (tile >= p.tiles) return false;
+    s.tile = static_cast<int>(tile);
+    s.kb0 = 0;
+    s.kb1 = p.kb_count;
+    return true;
+  }
+  if (cursor >= end) return false;
+  s.tile = static_cast<int>(cursor / p.kb_count);
+  s.kb0 = static_cast<int>(cursor % p.kb_count);
+  s.kb1 = static_cast<int>(min_ll(p.kb_count, s.kb0 + (end - cursor)));
+  cursor += s.kb1 - s.kb0;
+  return true;
 }
 
 __device__ __forceinline__ void apply_epilogue(const GemmParams& p, int n, int m, float a0,
@@ -109,7 +122,6 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -138,21 +150,19 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int grid = static_cast<int>(gridDim.x);
-  const long long ub = unit_begin(p.units, grid, blockIdx.x);
-  const long long ue = unit_begin(p.units, grid, blockIdx.x + 1);
-  const int KB = p.kb_count;
+  const long long ub = p.stream_k ? gemm_unit_begin(p.units, grid, blockIdx.x) : 0;
+  const long long ue = p.stream_k ? gemm_unit_begin(p.units, grid, blockIdx.x + 1) : 0;
 
   if (warp == 4) {
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
       uint32_t it = 0;
-      for (long long u = ub; u < ue;) {
-        const int tile = static_cast<int>(u / KB);
-        const int kb0 = static_cast<int>(u % KB);
-        const int kb1 = static_cast<int>(min_ll(KB, kb0 + (ue - u)));
-        const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+      long long cursor = ub;
+      Segment sg;
+      for (int j = 0; next_segment(p, cursor, ue, j, sg); ++j) {
+        const int n_tile = sg.tile % p.n_tiles, m_tile = sg.tile / p.n_tiles;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, p.status)) goto producer_done;
@@ -165,23 +175,22 @@ __global__ void __launch_bounds__(192, 1)
           tma_load_2d_hint(st + NA * S::kABytes, &map_b, &full[s], kb * kGemmBlockK,
                            n_tile * BN, pol_x);
         }
-        u += kb1 - kb0;
       }
     producer_done:;
     }
   } else if (warp == 5) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(kGemmBlockM, BN, 0);
-      uint32_t it = 0, seg = 0;
-      for (long long u = ub; u < ue; ++seg) {
-        const int kb0 = static_cast<int>(u % KB);
-        const int kb1 = static_cast<int>(min_ll(KB, kb0 + (ue - u)));
-        const int b = seg % S::kAccBufs;
-        const uint32_t bph = (seg / S::kAccBufs) & 1u;
+      uint32_t it = 0;
+      long long cursor = ub;
+      Segment sg;
+      for (int j = 0; next_segment(p, cursor, ue, j, sg); ++j) {
+        const int b = j % S::kAccBufs;
+        const uint32_t bph = (j / S::kAccBufs) & 1u;
         if (!mbar_wait(&tempty[b], bph ^ 1u, p.status)) goto mma_done;
         tc_fence_after();
         const uint32_t d = tmem_base + b * NA * BN;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&full[s], ph, p.status)) goto mma_done;
@@ -190,7 +199,7 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t b0 = a0 + NA * S::kABytes;
 #pragma unroll
           for (int k = 0; k < kGemmBlockK / 16; ++k) {
-            const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > sg.kb0 || k > 0) ? 1u : 0u;
             const uint64_t bd = sw128_desc(b0 + k * 32);
             umma_f16(d, sw128_desc(a0 + k * 32), bd, idesc, acc);
             if (NA == 2) umma_f16(d + BN, sw128_desc(a0 + S::kABytes + k * 32), bd, idesc, acc);
@@ -198,115 +207,49 @@ __global__ void __launch_bounds__(192, 1)
           umma_commit(&empty[s]);
         }
         umma_commit(&tfull[b]);
-        u += kb1 - kb0;
       }
     mma_done:;
     }
   } else {
     // Epilogue: thread t owns TMEM lane t = output feature m_tile*128 + t.
     const int t = threadIdx.x;
-    float red0[16], red1[16];
-    uint32_t seg = 0;
-    for (long long u = ub; u < ue; ++seg) {
-      const int tile = static_cast<int>(u / KB);
-      const int kb0 = static_cast<int>(u % KB);
-      const int kb1 = static_cast<int>(min_ll(KB, kb0 + (ue - u)));
-      const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
-      const int b = seg % S::kAccBufs;
-      const uint32_t bph = (seg / S::kAccBufs) & 1u;
+    long long cursor = ub;
+    const int first_tile = static_cast<int>(ub / (p.kb_count > 0 ? p.kb_count : 1));
+    Segment sg;
+    for (int j = 0; next_segment(p, cursor, ue, j, sg); ++j) {
+      const int n_tile = sg.tile % p.n_tiles, m_tile = sg.tile / p.n_tiles;
+      const int b = j % S::kAccBufs;
+      const uint32_t bph = (j / S::kAccBufs) & 1u;
       if (!mbar_wait(&tfull[b], bph, p.status)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + b * NA * BN;
       const int m = m_tile * kGemmBlockM + t;
       const int n0 = n_tile * BN;
       const int nvalid = min(BN, p.n - n0);
-      if (kb0 == 0 && kb1 == KB) {
-        for (int c = 0; c < BN / 16; ++c) {
-          if (c * 16 >= nvalid) break;
-          float v0[16], v1[16];
-          tmem_ld16(taddr + c * 16, v0);
-          if (NA == 2) tmem_ld16(taddr + BN + c * 16, v1);
+      float* slot = nullptr;
+      if (p.stream_k)
+        slot = p.slots + (static_cast<size_t>(blockIdx.x) * kGemmSlotsPerCta +
+                          (sg.tile - first_tile)) * NA * BN * 128;
+      for (int c = 0; c < BN / 16; ++c) {
+        if (c * 16 >= nvalid) break;
+        float v0[16], v1[16];
+        tmem_ld16(taddr + c * 16, v0);
+        if (NA == 2) tmem_ld16(taddr + BN + c * 16, v1);
+        if (slot) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (c * 16 + j < nvalid && m < p.m) apply_epilogue(p, n0 + c * 16 + j, m, v0[j], NA == 2 ? v1[j] : 0.f);
-        }
-        tc_fence_before();
-        mbar_arrive(&tempty[b]);
-      } else {
-        const long long seg_start = u;
-        const int slot = 2 * blockIdx.x + (seg_start == ub ? 0 : 1);
-        float* dst = p.partials + static_cast<size_t>(slot) * NA * BN * 128;
-        for (int c = 0; c < BN / 16; ++c) {
-          if (c * 16 >= nvalid) break;
-          float v0[16], v1[16];
-          tmem_ld16(taddr + c * 16, v0);
-          if (NA == 2) tmem_ld16(taddr + BN + c * 16, v1);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            dst[(c * 16 + j) * 128 + t] = v0[j];
-            if (NA == 2) dst[(BN + c * 16 + j) * 128 + t] = v1[j];
+          for (int jj = 0; jj < 16; ++jj) {
+            slot[(c * 16 + jj) * 128 + t] = v0[jj];
+            if (NA == 2) slot[(BN + c * 16 + jj) * 128 + t] = v1[jj];
           }
-        }
-        tc_fence_before();
-        mbar_arrive(&tempty[b]);
-        __threadfence();
-        named_bar_sync(1, 128);
-        const long long tile_u0 = static_cast<long long>(tile) * KB;
-        const int c_first = cta_of_unit(p.units, grid, tile_u0);
-        const int c_last = cta_of_unit(p.units, grid, tile_u0 + KB - 1);
-        if (t == 0) {
-          const unsigned prev = atomicAdd(&p.counters[tile], 1u);
-          *last_flag = (prev == static_cast<unsigned>(c_last - c_first)) ? 1 : 0;
-        }
-        named_bar_sync(1, 128);
-        if (*last_flag) {
-          __threadfence();
-          // Sum the tile's partials in CTA order.  Loads are issued in batches
-          // (16 columns x up to 8 segments per accumulator) before any add, so
-          // the reduction is bound by L2 bandwidth rather than load latency.
-          constexpr int kCols = 16, kSegs = 8;
-          for (int col0 = 0; col0 < nvalid; col0 += kCols) {
-            for (int acc_i = 0; acc_i < NA; ++acc_i) {
-              float sum[kCols];
+        } else {
 #pragma unroll
-              for (int j = 0; j < kCols; ++j) sum[j] = 0.f;
-              for (int c0 = c_first; c0 <= c_last; c0 += kSegs) {
-                float v[kSegs][kCols];
-#pragma unroll
-                for (int sidx = 0; sidx < kSegs; ++sidx) {
-                  const int c = c0 + sidx;
-                  if (c <= c_last) {
-                    const int sl = 2 * c + (unit_begin(p.units, grid, c) >= tile_u0 ? 0 : 1);
-                    const float* src = p.partials + static_cast<size_t>(sl) * NA * BN * 128 +
-                                       static_cast<size_t>(acc_i * BN + col0) * 128 + t;
-#pragma unroll
-                    for (int j = 0; j < kCols; ++j)
-                      v[sidx][j] = (col0 + j < nvalid) ? __ldcg(src + j * 128) : 0.f;
-                  }
-                }
-#pragma unroll
-                for (int sidx = 0; sidx < kSegs; ++sidx)
-                  if (c0 + sidx <= c_last)
-#pragma unroll
-                    for (int j = 0; j < kCols; ++j) sum[j] += v[sidx][j];
-              }
-              if (acc_i == 0) {
-#pragma unroll
-                for (int j = 0; j < kCols; ++j) red0[j] = sum[j];
-              } else {
-#pragma unroll
-                for (int j = 0; j < kCols; ++j) red1[j] = sum[j];
-              }
-            }
-#pragma unroll
-            for (int j = 0; j < kCols; ++j)
-              if (col0 + j < nvalid && m < p.m)
-                apply_epilogue(p, n0 + col0 + j, m, red0[j], NA == 2 ? red1[j] : 0.f);
-          }
-          if (t == 0) p.counters[tile] = 0u;
+          for (int jj = 0; jj < 16; ++jj)
+            if (c * 16 + jj < nvalid && m < p.m)
+              apply_epilogue(p, n0 + c * 16 + jj, m, v0[jj], NA == 2 ? v1[jj] : 0.f);
         }
       }
-      u += kb1 - kb0;
+      tc_fence_before();
+      mbar_arrive(&tempty[b]);
     }
   }
 
@@ -314,6 +257,25 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 5) tmem_dealloc(tmem_base, S::kTmemCols);
+}
+
+// ---------------------------------------------------------------- generic consumer
+__global__ void gemm_finish_kernel(const GemmSlots s, int rows, int epilogue, void* out, int ldo) {
+  const int n = blockIdx.y;
+  if (n >= rows) return;
+  for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < s.m; m += gridDim.x * blockDim.x) {
+    const float a0 = gemm_slot_sum(s, n, m, 0);
+    const size_t idx = static_cast<size_t>(n) * ldo + m;
+    switch (epilogue) {
+      case kEpiStoreF32: static_cast<float*>(out)[idx] = a0; break;
+      case kEpiStoreF16: static_cast<__half*>(out)[idx] = __float2half_rn(a0); break;
+      case kEpiResidual: static_cast<float*>(out)[idx] += a0; break;
+      default: {
+        const float a1 = gemm_slot_sum(s, n, m, 1);
+        static_cast<__half*>(out)[idx] = __float2half_rn(a0 / (1.0f + expf(-a0)) * a1);
+      }
+    }
+  }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -383,70 +345,100 @@ bool gemm_make_input(GemmInput* x, const void* base, int rows_cap, int k_pad, in
   return true;
 }
 
-size_t gemm_partial_floats(int sm_count) {
-  // Two partial slots per CTA, each up to 2 accumulators x 256 tokens x 128 rows.
-  return static_cast<size_t>(sm_count) * 2 * 2 * 256 * 128;
-}
-
-size_t gemm_counter_count(int max_m, int max_n) {
-  return static_cast<size_t>((max_m + kGemmBlockM - 1) / kGemmBlockM) *
-         ((max_n + 15) / 16);
-}
-
-cudaError_t gemm_run(const GemmWeight& w, const GemmInput& x, int n, int epilogue, void* out,
-                     int ldo, const GemmScratch& scratch, cudaStream_t stream, int bn_override,
-                     int grid_override) {
-  if (n <= 0 || n > x.rows_cap || w.k_pad != x.k_pad) return cudaErrorInvalidValue;
-  if ((epilogue == kEpiSwiGLU) != (w.pair == 2)) return cudaErrorInvalidValue;
-  int bn_index = 0;
+GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override, int grid_override) {
+  GemmPlan pl;
+  int bi = 0;
   if (bn_override) {
-    bn_index = -1;
+    bi = -1;
     for (int i = 0; i < kGemmNumBn; ++i)
-      if (kGemmBn[i] == bn_override) bn_index = i;
-    if (bn_index < 0) return cudaErrorInvalidValue;
+      if (kGemmBn[i] == bn_override) bi = i;
+    if (bi < 0) bi = 0;
   } else {
-    while (bn_index + 1 < kGemmNumBn && kGemmBn[bn_index] < n) ++bn_index;
+    while (bi + 1 < kGemmNumBn && kGemmBn[bi] < n) ++bi;
   }
-  if (w.pair == 2 && kGemmBn[bn_index] > 128) bn_index = 3;  // 2 accumulators x 128 x 2 buffers
-  const int bn = kGemmBn[bn_index];
+  if (w.pair == 2 && kGemmBn[bi] > 128) bi = 3;  // 2 accumulators x 128 x 2 buffers
+  pl.bn_index = bi;
+  pl.bn = kGemmBn[bi];
+  pl.kb_count = w.k_pad / kGemmBlockK;
+  pl.n_tiles = (n + pl.bn - 1) / pl.bn;
+  pl.m_tiles = (w.m + kGemmBlockM - 1) / kGemmBlockM;
+  pl.tiles = static_cast<long long>(pl.m_tiles) * pl.n_tiles;
+  pl.units = pl.tiles * pl.kb_count;
+  long long grid = grid_override > 0 ? grid_override : sm_count;
+  // at least 4 K blocks per CTA when the units are split
+  if (grid_override <= 0) grid = std::min<long long>(grid, std::max<long long>(1, pl.units / 4));
+  grid = std::max<long long>(1, std::min<long long>(grid, pl.units));
+  pl.stream_k = pl.tiles < 2 * grid;
+  if (!pl.stream_k) grid = std::min<long long>(grid, pl.tiles);
+  pl.grid = static_cast<int>(grid);
+  return pl;
+}
+
+size_t gemm_slot_floats(const GemmPlan& plan, int pair) {
+  if (!plan.stream_k) return 0;
+  return static_cast<size_t>(plan.grid) * kGemmSlotsPerCta * pair * plan.bn * 128;
+}
+
+size_t gemm_max_slot_floats(int sm_count) {
+  // pair x bn is at most 2 x 128 or 1 x 256
+  return static_cast<size_t>(sm_count) * kGemmSlotsPerCta * 256 * 128;
+}
+
+cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const GemmPlan& pl,
+                        int epilogue, void* out, int ldo, float* slots, GemmSlots* result,
+                        uint32_t* status, cudaStream_t stream) {
+  if (n <= 0 || n > x.rows_cap || w.k_pad != x.k_pad) return cudaErrorInvalidValue;
+  if (pl.stream_k && (!slots || !result)) return cudaErrorInvalidValue;
+  if (!pl.stream_k && (epilogue == kEpiSwiGLU) != (w.pair == 2)) return cudaErrorInvalidValue;
   GemmParams p{};
   p.m = w.m;
   p.n = n;
-  p.kb_count = w.k_pad / kGemmBlockK;
-  p.n_tiles = (n + bn - 1) / bn;
-  const int m_tiles = (w.m + kGemmBlockM - 1) / kGemmBlockM;
-  const long long tiles = static_cast<long long>(m_tiles) * p.n_tiles;
-  if (static_cast<size_t>(tiles) > scratch.counter_count) return cudaErrorInvalidValue;
-  p.units = tiles * p.kb_count;
+  p.kb_count = pl.kb_count;
+  p.n_tiles = pl.n_tiles;
+  p.tiles = pl.tiles;
+  p.units = pl.units;
+  p.stream_k = pl.stream_k ? 1 : 0;
   p.second_row = w.second_row;
   p.epilogue = epilogue;
   p.out = out;
   p.ldo = ldo;
-  p.partials = scratch.partials;
-  p.counters = scratch.counters;
-  p.status = scratch.status;
-  // One CTA per SM, but never fewer than 4 K blocks per CTA (pipeline fill).
-  long long grid = grid_override > 0 ? grid_override : scratch.sm_count;
-  if (grid_override <= 0) grid = std::min<long long>(grid, std::max<long long>(1, p.units / 4));
-  grid = std::min<long long>(grid, p.units);
-  const size_t need = static_cast<size_t>(grid) * 2 * w.pair * bn * 128;
-  if (need > scratch.partial_floats) return cudaErrorInvalidValue;
-  const int g = static_cast<int>(grid);
+  p.slots = slots;
+  p.status = status;
+  if (pl.stream_k) {
+    result->slots = slots;
+    result->units = pl.units;
+    result->grid = pl.grid;
+    result->kb_count = pl.kb_count;
+    result->bn = pl.bn;
+    result->n_tiles = pl.n_tiles;
+    result->pair = w.pair;
+    result->m = w.m;
+  }
+  const int g = pl.grid;
+  const int bi = pl.bn_index;
   if (w.pair == 1) {
-    switch (bn) {
-      case 16: return launch<16, 1>(w, x, bn_index, p, g, stream);
-      case 32: return launch<32, 1>(w, x, bn_index, p, g, stream);
-      case 64: return launch<64, 1>(w, x, bn_index, p, g, stream);
-      case 128: return launch<128, 1>(w, x, bn_index, p, g, stream);
-      default: return launch<256, 1>(w, x, bn_index, p, g, stream);
+    switch (pl.bn) {
+      case 16: return launch<16, 1>(w, x, bi, p, g, stream);
+      case 32: return launch<32, 1>(w, x, bi, p, g, stream);
+      case 64: return launch<64, 1>(w, x, bi, p, g, stream);
+      case 128: return launch<128, 1>(w, x, bi, p, g, stream);
+      default: return launch<256, 1>(w, x, bi, p, g, stream);
     }
   }
-  switch (bn) {
-    case 16: return launch<16, 2>(w, x, bn_index, p, g, stream);
-    case 32: return launch<32, 2>(w, x, bn_index, p, g, stream);
-    case 64: return launch<64, 2>(w, x, bn_index, p, g, stream);
-    default: return launch<128, 2>(w, x, bn_index, p, g, stream);
+  switch (pl.bn) {
+    case 16: return launch<16, 2>(w, x, bi, p, g, stream);
+    case 32: return launch<32, 2>(w, x, bi, p, g, stream);
+    case 64: return launch<64, 2>(w, x, bi, p, g, stream);
+    default: return launch<128, 2>(w, x, bi, p, g, stream);
   }
+}
+
+cudaError_t gemm_finish_launch(const GemmSlots& s, int rows, int epilogue, void* out, int ldo,
+                               cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>((s.m + 255) / 256), static_cast<unsigned>(rows));
+  gemm_finish_kernel<<<grid, 256, 0, stream>>>(s, rows, epilogue, out, ldo);
+  return cudaGetLastError();
 }
 
 }  // namespace hb

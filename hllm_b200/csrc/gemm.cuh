@@ -6,6 +6,16 @@
 // rows of a tile are the MMA's M dimension and the tokens are its N dimension,
 // so one kernel serves GEMV-shaped decode (N = 16..64) and prefill chunks
 // (N up to 256 per tile) while streaming each weight byte once.
+//
+// Two work splits:
+//   direct   -- (at least two tiles per SM) each CTA owns whole tiles and
+//               applies the epilogue itself;
+//   stream-K -- (fewer tiles) the tiles' K blocks are dealt out evenly to one
+//               CTA per SM; each CTA writes the F32 sums of its (at most three)
+//               tile segments to its own slots, and the kernel that consumes
+//               the result adds the slots of each element in CTA order
+//               (gemm_slot_sum) -- a fixed order, so results do not depend on
+//               timing.  No CTA waits on another.
 #pragma once
 
 #include <cuda.h>
@@ -26,6 +36,7 @@ constexpr int kGemmBlockK = 64;                 // one 128-byte swizzle atom of 
 constexpr int kGemmBlockM = 128;
 constexpr int kGemmNumBn = 5;
 constexpr int kGemmBn[kGemmNumBn] = {16, 32, 64, 128, 256};
+constexpr int kGemmSlotsPerCta = 3;
 
 // A weight operand: [rows_total][k_pad] F16, k_pad a multiple of 64.  With
 // pair == 2 the matrix holds two row blocks (gate then up) of `m` rows each,
@@ -47,30 +58,70 @@ struct GemmInput {
   int k_pad;
 };
 
-// Scratch shared by every GEMM on one stream: split-K partial tiles and one
-// arrival counter per output tile.  Counters must start at zero; the kernel
-// returns each one it uses to zero.
-struct GemmScratch {
-  float* partials;
-  size_t partial_floats;
-  unsigned* counters;
-  size_t counter_count;
-  uint32_t* status;
-  int sm_count;
+struct GemmPlan {
+  int bn_index = 0, bn = 16;
+  int m_tiles = 0, n_tiles = 0, kb_count = 0;
+  long long tiles = 0, units = 0;
+  int grid = 0;
+  bool stream_k = false;
 };
+
+// Where a stream-K GEMM left its result: the consumer sums, for element
+// (n, m) of accumulator `acc`, the slots of the CTAs that covered its tile.
+struct GemmSlots {
+  const float* slots;  // [grid * 3][pair][bn][128]
+  long long units;
+  int grid, kb_count, bn, n_tiles, pair, m;
+};
+
+GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override = 0,
+                   int grid_override = 0);
+// Floats of slot storage a stream-K plan needs (0 for direct plans).
+size_t gemm_slot_floats(const GemmPlan& plan, int pair);
+size_t gemm_max_slot_floats(int sm_count);
 
 bool gemm_make_weight(GemmWeight* w, const void* base, int rows_total, int m, int k_pad, int pair,
                       int second_row);
 bool gemm_make_input(GemmInput* x, const void* base, int rows_cap, int k_pad, int row_stride);
-// Partial-tile floats the scratch needs for any call with these limits.
-size_t gemm_partial_floats(int sm_count);
-size_t gemm_counter_count(int max_m, int max_n);
 
-// Launches Y = X W^T for the first n rows of X.  `grid_override` > 0 fixes
-// the number of CTAs (tests); 0 picks one per SM.  Returns cudaSuccess or the
-// launch error; cudaErrorInvalidValue for unsupported shapes.
-cudaError_t gemm_run(const GemmWeight& w, const GemmInput& x, int n, int epilogue, void* out,
-                     int ldo, const GemmScratch& scratch, cudaStream_t stream,
-                     int bn_override = 0, int grid_override = 0);
+// Runs the plan.  Direct plans apply `epilogue` into out/ldo; stream-K plans
+// write `slots` and fill *result for the consumer.
+cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const GemmPlan& plan,
+                        int epilogue, void* out, int ldo, float* slots, GemmSlots* result,
+                        uint32_t* status, cudaStream_t stream);
+
+// Generic consumer: out = epilogue(sum of slots) for every (n < rows, m).
+cudaError_t gemm_finish_launch(const GemmSlots& s, int rows, int epilogue, void* out, int ldo,
+                               cudaStream_t stream);
+
+// ---------------------------------------------------------------- device side
+__host__ __device__ inline long long gemm_unit_begin(long long units, int grid, int c) {
+  return units * c / grid;
+}
+
+#ifdef __CUDACC__
+// Sum of the slots holding element (n, m) of accumulator `acc`, in CTA order.
+__device__ inline float gemm_slot_sum(const GemmSlots& s, int n, int m, int acc) {
+  const int tile = (m / kGemmBlockM) * s.n_tiles + n / s.bn;
+  const long long u0 = static_cast<long long>(tile) * s.kb_count;
+  const long long u1 = u0 + s.kb_count - 1;
+  // CTA ranges are [units*c/grid, units*(c+1)/grid).
+  int c0 = static_cast<int>((u0 * s.grid) / s.units);
+  while (c0 + 1 < s.grid && gemm_unit_begin(s.units, s.grid, c0 + 1) <= u0) ++c0;
+  while (c0 > 0 && gemm_unit_begin(s.units, s.grid, c0) > u0) --c0;
+  const size_t within = static_cast<size_t>(acc) * s.bn * 128 +
+                        static_cast<size_t>(n % s.bn) * 128 + (m % kGemmBlockM);
+  const size_t slot_floats = static_cast<size_t>(s.pair) * s.bn * 128;
+  float sum = 0.f;
+  for (int c = c0; c < s.grid; ++c) {
+    const long long b = gemm_unit_begin(s.units, s.grid, c);
+    if (b > u1) break;
+    const int ordinal = tile - static_cast<int>(b / s.kb_count);
+    sum += __ldcg(s.slots + (static_cast<size_t>(c) * kGemmSlotsPerCta + ordinal) * slot_floats +
+                  within);
+  }
+  return sum;
+}
+#endif
 
 }  // namespace hb

@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
     const bool is_q = h < a.hq, is_k = !is_q && h < a.hq + a.hkv;
     float ss = 0.f;
     for (int i = lane; i < d; i += 32) {
-      const float v = row[h * d + i];
+      const float v = a.from_slots ? gemm_slot_sum(a.slots, t, h * d + i, 0) : row[h * d + i];
       x[i] = v;
       ss += v * v;
     }
@@ -186,6 +186,49 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
       dst[half + i] = __float2half_rn(p1 * c + p0 * s);
     }
     __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------- residual + norm
+// One CTA per token: add the projection's slots into the F32 residual stream,
+// then RMSNorm the updated row into the next GEMM's F16 input.
+__global__ void residual_norm_kernel(float* __restrict__ hidden, int width, GemmSlots slots,
+                                     int has_slots, const float* __restrict__ w, float eps,
+                                     __half* __restrict__ out, int ld_out) {
+  const int t = blockIdx.x;
+  float* xr = hidden + static_cast<size_t>(t) * width;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+    float v = xr[c];
+    if (has_slots) {
+      v += gemm_slot_sum(slots, t, c, 0);
+      xr[c] = v;
+    }
+    ss += v * v;
+  }
+  if (!w) return;
+  __shared__ float red[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv = 1.0f / sqrtf(red[0] / static_cast<float>(width) + eps);
+  __half* o = out + static_cast<size_t>(t) * ld_out;
+  for (int c = threadIdx.x; c < width; c += blockDim.x) o[c] = __float2half_rn(xr[c] * inv * w[c]);
+}
+
+// cpp/src/cpu/llama.cpp:274-280: (g / (1 + exp(-g))) * u.
+__global__ void swiglu_kernel(GemmSlots slots, __half* __restrict__ act, int ld_act) {
+  const int t = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < slots.m; i += gridDim.x * blockDim.x) {
+    const float g = gemm_slot_sum(slots, t, i, 0);
+    const float u = gemm_slot_sum(slots, t, i, 1);
+    act[static_cast<size_t>(t) * ld_act + i] = __float2half_rn((g / (1.0f + expf(-g))) * u);
   }
 }
 
@@ -275,6 +318,26 @@ cudaError_t rmsnorm_launch(const float* x, int rows, int width, const float* w, 
 cudaError_t qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream) {
   if (a.dim > kMaxHeadDim || (a.dim & 1)) return cudaErrorInvalidValue;
   qkv_post_kernel<<<a.tokens, kQkvWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t residual_norm_launch(float* hidden, int tokens, int width, const GemmSlots* slots,
+                                 const float* norm, float eps, __half* out, int ld_out,
+                                 cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  GemmSlots s{};
+  if (slots) s = *slots;
+  const int threads = width >= 1024 ? 512 : (width >= 256 ? 256 : 64);
+  residual_norm_kernel<<<tokens, threads, 0, stream>>>(hidden, width, s, slots ? 1 : 0, norm,
+                                                       eps, out, ld_out);
+  return cudaGetLastError();
+}
+
+cudaError_t swiglu_launch(const GemmSlots& slots, int tokens, __half* act, int ld_act,
+                          cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>((slots.m + 255) / 256), static_cast<unsigned>(tokens));
+  swiglu_kernel<<<grid, 256, 0, stream>>>(slots, act, ld_act);
   return cudaGetLastError();
 }
 

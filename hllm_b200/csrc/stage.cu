@@ -167,7 +167,7 @@ struct hllm_b200_stage {
   double* sample_scratch = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
   hb::GemmInput in_xn{}, in_attn{}, in_act{}, in_xs{};
-  hb::GemmScratch gscratch{};
+  float* slots = nullptr;  // stream-K GEMM slots, consumed by the next kernel
 
   // pinned host staging
   // Descriptor uploads go through a ring of pinned buffers so that enqueue-only
@@ -474,13 +474,7 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
   }
   s->part_o = s->alloc<float>(s->max_splits * s->hq * s->dim);
   s->part_ml = s->alloc<float>(s->max_splits * s->hq * 2);
-  s->gscratch.sm_count = s->sm_count;
-  s->gscratch.partial_floats = hb::gemm_partial_floats(s->sm_count);
-  s->gscratch.partials = s->alloc<float>(s->gscratch.partial_floats);
-  const size_t max_m = std::max({s->V, s->qkvw, 2 * s->I, s->h});
-  s->gscratch.counter_count = hb::gemm_counter_count(static_cast<int>(max_m), static_cast<int>(T));
-  s->gscratch.counters = s->alloc<unsigned>(s->gscratch.counter_count);
-  s->gscratch.status = s->status;
+  s->slots = s->alloc<float>(hb::gemm_max_slot_floats(s->sm_count));
   if (!hb::gemm_make_input(&s->in_xn, s->xn, static_cast<int>(T), static_cast<int>(s->h_pad),
                            static_cast<int>(s->h_pad)) ||
       !hb::gemm_make_input(&s->in_attn, s->attn, static_cast<int>(T), static_cast<int>(s->qw_pad),
@@ -793,13 +787,20 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     const Layer& L = s->layers[li];
     __half* kc = s->kv + li * s->kv_layer_elems;
     __half* vc = kc + s->kv_layer_elems / 2;
-    PLAUNCH(kProfOther, 0, 0, hb::rmsnorm_launch(s->hidden, T, h, L.in_norm, eps, s->xn, static_cast<int>(s->h_pad),
-                              nullptr, s->stream));
+    // Layer 0's input norm runs alone; every later one is fused into the
+    // previous layer's residual consumer.
+    if (li == 0)
+      PLAUNCH(kProfOther, 0, 0, hb::rmsnorm_launch(s->hidden, T, h, L.in_norm, eps, s->xn,
+                                                   static_cast<int>(s->h_pad), nullptr, s->stream));
+    const hb::GemmPlan pq = hb::gemm_plan(L.g_qkv, T, s->sm_count);
+    hb::GemmSlots qslots{};
     PLAUNCH(gk, gemm_bytes(s->qkvw, T, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->qkvw, T, s->h, 1),
-            hb::gemm_run(L.g_qkv, s->in_xn, T, hb::kEpiStoreF32, s->qkv, static_cast<int>(s->qkvw),
-                        s->gscratch, s->stream));
+            hb::gemm_launch(L.g_qkv, s->in_xn, T, pq, hb::kEpiStoreF32, s->qkv,
+                            static_cast<int>(s->qkvw), s->slots, &qslots, s->status, s->stream));
     hb::QkvPostArgs qa{};
     qa.qkv = s->qkv;
+    qa.slots = qslots;
+    qa.from_slots = pq.stream_k ? 1 : 0;
     qa.tokens = T;
     qa.hq = static_cast<int>(s->hq);
     qa.hkv = static_cast<int>(s->hkv);
@@ -844,17 +845,37 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     }
     if (p.total_qtiles)
       PLAUNCH(kProfAttnPrefill, p.attn_pre_bytes, p.attn_pre_flops, hb::attn_prefill_launch(aa, p.total_qtiles, s->stream));
+    // o_proj, then the fused residual add + post-attention RMSNorm.
+    const hb::GemmPlan po = hb::gemm_plan(L.g_o, T, s->sm_count);
+    hb::GemmSlots oslots{};
     PLAUNCH(gk, gemm_bytes(s->h, T, s->qw, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->qw, 1),
-            hb::gemm_run(L.g_o, s->in_attn, T, hb::kEpiResidual, s->hidden, h, s->gscratch,
-                        s->stream));
-    PLAUNCH(kProfOther, 0, 0, hb::rmsnorm_launch(s->hidden, T, h, L.post_norm, eps, s->xn,
-                              static_cast<int>(s->h_pad), nullptr, s->stream));
+            hb::gemm_launch(L.g_o, s->in_attn, T, po, hb::kEpiResidual, s->hidden, h, s->slots,
+                            &oslots, s->status, s->stream));
+    PLAUNCH(kProfOther, 0, 0,
+            hb::residual_norm_launch(s->hidden, T, h, po.stream_k ? &oslots : nullptr,
+                                     L.post_norm, eps, s->xn, static_cast<int>(s->h_pad),
+                                     s->stream));
+    // gate/up with SwiGLU: in the GEMM epilogue, or from the stream-K slots.
+    const hb::GemmPlan pg = hb::gemm_plan(L.g_gu, T, s->sm_count);
+    hb::GemmSlots gslots{};
     PLAUNCH(gk, gemm_bytes(s->I, T, s->h, 2, hb::kEpiSwiGLU), gemm_flops(s->I, T, s->h, 2),
-            hb::gemm_run(L.g_gu, s->in_xn, T, hb::kEpiSwiGLU, s->act, static_cast<int>(s->I_pad),
-                        s->gscratch, s->stream));
+            hb::gemm_launch(L.g_gu, s->in_xn, T, pg, hb::kEpiSwiGLU, s->act,
+                            static_cast<int>(s->I_pad), s->slots, &gslots, s->status, s->stream));
+    if (pg.stream_k)
+      PLAUNCH(kProfOther, 0, 0,
+              hb::swiglu_launch(gslots, T, s->act, static_cast<int>(s->I_pad), s->stream));
+    // down_proj, then the residual add fused with the next layer's input norm.
+    const hb::GemmPlan pd = hb::gemm_plan(L.g_down, T, s->sm_count);
+    hb::GemmSlots dslots{};
     PLAUNCH(gk, gemm_bytes(s->h, T, s->I, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->I, 1),
-            hb::gemm_run(L.g_down, s->in_act, T, hb::kEpiResidual, s->hidden, h, s->gscratch,
-                        s->stream));
+            hb::gemm_launch(L.g_down, s->in_act, T, pd, hb::kEpiResidual, s->hidden, h, s->slots,
+                            &dslots, s->status, s->stream));
+    const float* next_norm = li + 1 < s->n_layers ? s->layers[li + 1].in_norm : nullptr;
+    if (pd.stream_k || next_norm)
+      PLAUNCH(kProfOther, 0, 0,
+              hb::residual_norm_launch(s->hidden, T, h, pd.stream_k ? &dslots : nullptr,
+                                       next_norm, eps, s->xn, static_cast<int>(s->h_pad),
+                                       s->stream));
   }
 
   // ---- output
@@ -864,10 +885,16 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
       PLAUNCH(kProfOther, 0, 0, hb::last_token_launch(s->cu_seqlens, s->sample_rows, S, s->last_idx, s->stream));
       PLAUNCH(kProfOther, 0, 0, hb::rmsnorm_launch(s->hidden, S, h, s->final_norm, eps, s->xs,
                                 static_cast<int>(s->h_pad), s->last_idx, s->stream));
+      const hb::GemmPlan ph = hb::gemm_plan(s->g_head, S, s->sm_count);
+      hb::GemmSlots hslots{};
       PLAUNCH(S <= 128 ? kProfGemmDecode : kProfGemmPrefill,
               gemm_bytes(s->V, S, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->V, S, s->h, 1),
-              hb::gemm_run(s->g_head, s->in_xs, S, hb::kEpiStoreF32, s->logits,
-                          static_cast<int>(s->V), s->gscratch, s->stream));
+              hb::gemm_launch(s->g_head, s->in_xs, S, ph, hb::kEpiStoreF32, s->logits,
+                              static_cast<int>(s->V), s->slots, &hslots, s->status, s->stream));
+      if (ph.stream_k)
+        PLAUNCH(kProfOther, 0, 0,
+                hb::gemm_finish_launch(hslots, S, hb::kEpiStoreF32, s->logits,
+                                       static_cast<int>(s->V), s->stream));
       PLAUNCH(kProfOther, 0, 0, hb::sample_launch(s->logits, S, static_cast<int>(s->V), static_cast<int>(s->V),
                                s->d_params, s->sample_scratch, s->results, s->status, s->stream));
     }
