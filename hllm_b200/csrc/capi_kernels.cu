@@ -37,6 +37,7 @@ hllm_b200_status cuda_status(cudaError_t e) {
 // use and kept until the process exits.
 struct DeviceScratch {
   float* slots = nullptr;
+  int* segmap = nullptr;
   uint32_t* status = nullptr;
   int sm_count = 0;
 };
@@ -53,6 +54,7 @@ hllm_b200_status scratch_for_device(DeviceScratch* out) {
     e = cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
       e = cudaMalloc(&s.slots, hb::gemm_max_slot_floats(s.sm_count) * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&s.segmap, hb::kGemmMapInts * sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&s.status, 256);
     if (e == cudaSuccess) e = cudaMemset(s.status, 0, 256);
     if (e != cudaSuccess) {
@@ -91,7 +93,8 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
   hb::GemmSlots slots{};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = hb::gemm_launch(gw, gx, static_cast<int>(n), plan, static_cast<int>(epilogue), y,
-                                  static_cast<int>(ldy), sc.slots, &slots, sc.status, s);
+                                  static_cast<int>(ldy), sc.slots, sc.segmap, &slots, sc.status,
+                                  s);
   if (e == cudaSuccess && plan.stream_k)
     e = hb::gemm_finish_launch(slots, static_cast<int>(n), static_cast<int>(epilogue), y,
                                static_cast<int>(ldy), s);

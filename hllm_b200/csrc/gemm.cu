@@ -40,6 +40,8 @@ struct GemmParams {
   void* out;
   int ldo;
   float* slots;
+  int* segmap;
+  int* segcount;
   uint32_t* status;
 };
 
@@ -227,9 +229,21 @@ __global__ void __launch_bounds__(192, 1)
       const int n0 = n_tile * BN;
       const int nvalid = min(BN, p.n - n0);
       float* slot = nullptr;
-      if (p.stream_k)
-        slot = p.slots + (static_cast<size_t>(blockIdx.x) * kGemmSlotsPerCta +
-                          (sg.tile - first_tile)) * NA * BN * 128;
+      if (p.stream_k) {
+        const int slot_id = static_cast<int>(blockIdx.x) * kGemmSlotsPerCta + (sg.tile - first_tile);
+        slot = p.slots + static_cast<size_t>(slot_id) * NA * BN * 128;
+        if (t == 0) {
+          // Record this slot in the tile's segment list (CTA order): CTA c covers
+          // unit u iff U*c/G <= u < U*(c+1)/G, i.e. c = floor(((u+1)G - 1)/U).
+          const long long u0 = static_cast<long long>(sg.tile) * p.kb_count;
+          const long long G = grid;
+          const int c_first = static_cast<int>(((u0 + 1) * G - 1) / p.units);
+          const int c_last = static_cast<int>(((u0 + p.kb_count) * G - 1) / p.units);
+          const int pos = static_cast<int>(blockIdx.x) - c_first;
+          p.segmap[sg.tile * kGemmMaxSegsPerTile + pos] = slot_id;
+          if (pos == 0) p.segcount[sg.tile] = c_last - c_first + 1;
+        }
+      }
       for (int c = 0; c < BN / 16; ++c) {
         if (c * 16 >= nvalid) break;
         float v0[16], v1[16];
@@ -369,6 +383,12 @@ GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override, in
   if (grid_override <= 0) grid = std::min<long long>(grid, std::max<long long>(1, pl.units / 4));
   grid = std::max<long long>(1, std::min<long long>(grid, pl.units));
   pl.stream_k = pl.tiles < 2 * grid;
+  if (pl.stream_k) {
+    // Each tile's segments must fit the consumer's segment list, and the
+    // segment map holds a bounded number of tiles.
+    grid = std::min<long long>(grid, pl.tiles * (kGemmMaxSegsPerTile - 2));
+    if (pl.tiles > kGemmMaxStreamKTiles) pl.stream_k = false;
+  }
   if (!pl.stream_k) grid = std::min<long long>(grid, pl.tiles);
   pl.grid = static_cast<int>(grid);
   return pl;
@@ -385,10 +405,10 @@ size_t gemm_max_slot_floats(int sm_count) {
 }
 
 cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const GemmPlan& pl,
-                        int epilogue, void* out, int ldo, float* slots, GemmSlots* result,
-                        uint32_t* status, cudaStream_t stream) {
+                        int epilogue, void* out, int ldo, float* slots, int* segmap,
+                        GemmSlots* result, uint32_t* status, cudaStream_t stream) {
   if (n <= 0 || n > x.rows_cap || w.k_pad != x.k_pad) return cudaErrorInvalidValue;
-  if (pl.stream_k && (!slots || !result)) return cudaErrorInvalidValue;
+  if (pl.stream_k && (!slots || !segmap || !result)) return cudaErrorInvalidValue;
   if (!pl.stream_k && (epilogue == kEpiSwiGLU) != (w.pair == 2)) return cudaErrorInvalidValue;
   GemmParams p{};
   p.m = w.m;
@@ -403,12 +423,13 @@ cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const Ge
   p.out = out;
   p.ldo = ldo;
   p.slots = slots;
+  p.segmap = segmap;
+  p.segcount = segmap ? segmap + kGemmMaxStreamKTiles * kGemmMaxSegsPerTile : nullptr;
   p.status = status;
   if (pl.stream_k) {
     result->slots = slots;
-    result->units = pl.units;
-    result->grid = pl.grid;
-    result->kb_count = pl.kb_count;
+    result->segmap = p.segmap;
+    result->segcount = p.segcount;
     result->bn = pl.bn;
     result->n_tiles = pl.n_tiles;
     result->pair = w.pair;

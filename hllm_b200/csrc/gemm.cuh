@@ -68,11 +68,18 @@ struct GemmPlan {
 
 // Where a stream-K GEMM left its result: the consumer sums, for element
 // (n, m) of accumulator `acc`, the slots of the CTAs that covered its tile.
+// The GEMM records them per tile: segcount[tile] slots, segmap[tile][k] in
+// CTA order.
+constexpr int kGemmMaxSegsPerTile = 16;
+constexpr int kGemmMaxStreamKTiles = 512;
 struct GemmSlots {
-  const float* slots;  // [grid * 3][pair][bn][128]
-  long long units;
-  int grid, kb_count, bn, n_tiles, pair, m;
+  const float* slots;   // [grid * 3][pair][bn][128]
+  const int* segmap;    // [kGemmMaxStreamKTiles][kGemmMaxSegsPerTile]
+  const int* segcount;  // [kGemmMaxStreamKTiles]
+  int bn, n_tiles, pair, m;
 };
+// Ints of segment-map storage that follows the slots.
+constexpr size_t kGemmMapInts = kGemmMaxStreamKTiles * (kGemmMaxSegsPerTile + 1);
 
 GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override = 0,
                    int grid_override = 0);
@@ -87,8 +94,8 @@ bool gemm_make_input(GemmInput* x, const void* base, int rows_cap, int k_pad, in
 // Runs the plan.  Direct plans apply `epilogue` into out/ldo; stream-K plans
 // write `slots` and fill *result for the consumer.
 cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const GemmPlan& plan,
-                        int epilogue, void* out, int ldo, float* slots, GemmSlots* result,
-                        uint32_t* status, cudaStream_t stream);
+                        int epilogue, void* out, int ldo, float* slots, int* segmap,
+                        GemmSlots* result, uint32_t* status, cudaStream_t stream);
 
 // Generic consumer: out = epilogue(sum of slots) for every (n < rows, m).
 cudaError_t gemm_finish_launch(const GemmSlots& s, int rows, int epilogue, void* out, int ldo,
@@ -102,24 +109,15 @@ __host__ __device__ inline long long gemm_unit_begin(long long units, int grid, 
 #ifdef __CUDACC__
 // Sum of the slots holding element (n, m) of accumulator `acc`, in CTA order.
 __device__ inline float gemm_slot_sum(const GemmSlots& s, int n, int m, int acc) {
-  const int tile = (m / kGemmBlockM) * s.n_tiles + n / s.bn;
-  const long long u0 = static_cast<long long>(tile) * s.kb_count;
-  const long long u1 = u0 + s.kb_count - 1;
-  // CTA ranges are [units*c/grid, units*(c+1)/grid).
-  int c0 = static_cast<int>((u0 * s.grid) / s.units);
-  while (c0 + 1 < s.grid && gemm_unit_begin(s.units, s.grid, c0 + 1) <= u0) ++c0;
-  while (c0 > 0 && gemm_unit_begin(s.units, s.grid, c0) > u0) --c0;
+  const int tile = (m >> 7) * s.n_tiles + n / s.bn;
+  const int count = __ldcg(s.segcount + tile);
+  const int* map = s.segmap + tile * kGemmMaxSegsPerTile;
   const size_t within = static_cast<size_t>(acc) * s.bn * 128 +
-                        static_cast<size_t>(n % s.bn) * 128 + (m % kGemmBlockM);
+                        static_cast<size_t>(n % s.bn) * 128 + (m & 127);
   const size_t slot_floats = static_cast<size_t>(s.pair) * s.bn * 128;
   float sum = 0.f;
-  for (int c = c0; c < s.grid; ++c) {
-    const long long b = gemm_unit_begin(s.units, s.grid, c);
-    if (b > u1) break;
-    const int ordinal = tile - static_cast<int>(b / s.kb_count);
-    sum += __ldcg(s.slots + (static_cast<size_t>(c) * kGemmSlotsPerCta + ordinal) * slot_floats +
-                  within);
-  }
+  for (int k = 0; k < count; ++k)
+    sum += __ldcg(s.slots + static_cast<size_t>(__ldcg(map + k)) * slot_floats + within);
   return sum;
 }
 #endif

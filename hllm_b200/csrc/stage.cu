@@ -168,6 +168,7 @@ struct hllm_b200_stage {
   float *part_o = nullptr, *part_ml = nullptr;
   hb::GemmInput in_xn{}, in_attn{}, in_act{}, in_xs{};
   float* slots = nullptr;  // stream-K GEMM slots, consumed by the next kernel
+  int* segmap = nullptr;   // their per-tile segment lists
 
   // pinned host staging
   // Descriptor uploads go through a ring of pinned buffers so that enqueue-only
@@ -475,6 +476,7 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
   s->part_o = s->alloc<float>(s->max_splits * s->hq * s->dim);
   s->part_ml = s->alloc<float>(s->max_splits * s->hq * 2);
   s->slots = s->alloc<float>(hb::gemm_max_slot_floats(s->sm_count));
+  s->segmap = s->alloc<int>(hb::kGemmMapInts);
   if (!hb::gemm_make_input(&s->in_xn, s->xn, static_cast<int>(T), static_cast<int>(s->h_pad),
                            static_cast<int>(s->h_pad)) ||
       !hb::gemm_make_input(&s->in_attn, s->attn, static_cast<int>(T), static_cast<int>(s->qw_pad),
@@ -796,7 +798,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     hb::GemmSlots qslots{};
     PLAUNCH(gk, gemm_bytes(s->qkvw, T, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->qkvw, T, s->h, 1),
             hb::gemm_launch(L.g_qkv, s->in_xn, T, pq, hb::kEpiStoreF32, s->qkv,
-                            static_cast<int>(s->qkvw), s->slots, &qslots, s->status, s->stream));
+                            static_cast<int>(s->qkvw), s->slots, s->segmap, &qslots, s->status, s->stream));
     hb::QkvPostArgs qa{};
     qa.qkv = s->qkv;
     qa.slots = qslots;
@@ -849,7 +851,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     const hb::GemmPlan po = hb::gemm_plan(L.g_o, T, s->sm_count);
     hb::GemmSlots oslots{};
     PLAUNCH(gk, gemm_bytes(s->h, T, s->qw, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->qw, 1),
-            hb::gemm_launch(L.g_o, s->in_attn, T, po, hb::kEpiResidual, s->hidden, h, s->slots,
+            hb::gemm_launch(L.g_o, s->in_attn, T, po, hb::kEpiResidual, s->hidden, h, s->slots, s->segmap,
                             &oslots, s->status, s->stream));
     PLAUNCH(kProfOther, 0, 0,
             hb::residual_norm_launch(s->hidden, T, h, po.stream_k ? &oslots : nullptr,
@@ -860,7 +862,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     hb::GemmSlots gslots{};
     PLAUNCH(gk, gemm_bytes(s->I, T, s->h, 2, hb::kEpiSwiGLU), gemm_flops(s->I, T, s->h, 2),
             hb::gemm_launch(L.g_gu, s->in_xn, T, pg, hb::kEpiSwiGLU, s->act,
-                            static_cast<int>(s->I_pad), s->slots, &gslots, s->status, s->stream));
+                            static_cast<int>(s->I_pad), s->slots, s->segmap, &gslots, s->status, s->stream));
     if (pg.stream_k)
       PLAUNCH(kProfOther, 0, 0,
               hb::swiglu_launch(gslots, T, s->act, static_cast<int>(s->I_pad), s->stream));
@@ -868,7 +870,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     const hb::GemmPlan pd = hb::gemm_plan(L.g_down, T, s->sm_count);
     hb::GemmSlots dslots{};
     PLAUNCH(gk, gemm_bytes(s->h, T, s->I, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->I, 1),
-            hb::gemm_launch(L.g_down, s->in_act, T, pd, hb::kEpiResidual, s->hidden, h, s->slots,
+            hb::gemm_launch(L.g_down, s->in_act, T, pd, hb::kEpiResidual, s->hidden, h, s->slots, s->segmap,
                             &dslots, s->status, s->stream));
     const float* next_norm = li + 1 < s->n_layers ? s->layers[li + 1].in_norm : nullptr;
     if (pd.stream_k || next_norm)
@@ -890,7 +892,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
       PLAUNCH(S <= 128 ? kProfGemmDecode : kProfGemmPrefill,
               gemm_bytes(s->V, S, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->V, S, s->h, 1),
               hb::gemm_launch(s->g_head, s->in_xs, S, ph, hb::kEpiStoreF32, s->logits,
-                              static_cast<int>(s->V), s->slots, &hslots, s->status, s->stream));
+                              static_cast<int>(s->V), s->slots, s->segmap, &hslots, s->status, s->stream));
       if (ph.stream_k)
         PLAUNCH(kProfOther, 0, 0,
                 hb::gemm_finish_launch(hslots, S, hb::kEpiStoreF32, s->logits,
