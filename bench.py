@@ -211,7 +211,7 @@ def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, cl
     if profile:
         prof = {}
         for kind, name in enumerate(("gemm_decode", "gemm_prefill", "attn_decode", "attn_prefill",
-                                     "other")):
+                                     "misc", "norm", "qkv_rope", "swiglu", "sampler")):
             v = [C.c_double(), C.c_uint64(), C.c_double(), C.c_double()]
             _lib.check(L.hllm_b200_stage_profile_read(stage.handle, kind, C.byref(v[0]),
                                                       C.byref(v[1]), C.byref(v[2]), C.byref(v[3])))
@@ -332,6 +332,12 @@ def ours(args, world, rank, local):
     clocks = ClockSampler(local)
     dev_ms, dev_tokens, launches, _, clock_info = run_device_phase(
         stage, cfg, trace, steps, first_timed, K, clocks=clocks)
+    if args.device_phase_only:
+        print(json.dumps({"device_phase_ms_per_step": round(dev_ms / K, 4),
+                          "tokens_per_s": round(dev_tokens / (dev_ms / 1e3), 1),
+                          "launches_per_step": launches / K}), flush=True)
+        stage.close()
+        return
     # e2e: the public call with host buffers and token feedback
     import copy
     trace2, steps2 = plan_schedule(total_steps)
@@ -359,7 +365,7 @@ def ours(args, world, rank, local):
         return
     hbm, tf_burst, tf_sust, peak_src = peaks()
     # dominant kernel class by device time
-    dom = max(prof, key=lambda k: prof[k]["ms"] if k != "other" else -1)
+    dom = max(prof, key=lambda k: prof[k]["ms"] if (prof[k]["bytes"] or prof[k]["flops"]) else -1)
     p = prof[dom]
     per_launch_s = p["ms"] / 1e3 / max(1, p["launches"])
     intensity = p["flops"] / max(1.0, p["bytes"])
@@ -469,6 +475,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--fast-forward", type=int, default=150)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--device-phase-only", action="store_true",
+                    help="run only the device-resident phase (for profiler launch lists)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -132,7 +132,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, int width,
 // (apply_rope, :214-240), then the K/V append (:264) -- here a scatter into
 // 16-token blocks of the paged pool: element (slot, head, i) lives at
 // ((slot/16 * Hkv + head) * 16 + slot%16) * d + i.
-constexpr int kQkvWarps = 8;
+constexpr int kQkvWarps = 4;
 constexpr int kMaxHeadDim = 256;
 
 __global__ void __launch_bounds__(kQkvWarps * 32)
@@ -147,7 +147,9 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
   if (slot < 0) return;  // the packer has already flagged the missing block
   const float* row = a.qkv + static_cast<size_t>(t) * heads * d;
   float* x = buf[warp];
-  for (int h = warp; h < heads; h += kQkvWarps) {
+  // One warp per head: heads [blockIdx.y * warps, +warps) of token t.
+  for (int h = blockIdx.y * kQkvWarps + warp; h < heads && h < (blockIdx.y + 1) * kQkvWarps;
+       h += kQkvWarps) {
     const bool is_q = h < a.hq, is_k = !is_q && h < a.hq + a.hkv;
     float ss = 0.f;
     for (int i = lane; i < d; i += 32) {
@@ -178,9 +180,19 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
       const int kvh = h - a.hq;
       dst = a.k_cache + ((static_cast<size_t>(slot / 16) * a.hkv + kvh) * 16 + slot % 16) * d;
     }
+    const int ipos = a.positions[t];
+    const bool table = a.rope_table && ipos < a.rope_positions;
     for (int i = lane; i < half; i += 32) {
-      const float angle = pos / a.rope_pow[i];
-      const float c = cosf(angle), s = sinf(angle);
+      float c, s;
+      if (table) {
+        const float2 cs = a.rope_table[static_cast<size_t>(ipos) * half + i];
+        c = cs.x;
+        s = cs.y;
+      } else {
+        const float angle = pos / a.rope_pow[i];
+        c = cosf(angle);
+        s = sinf(angle);
+      }
       const float p0 = x[i], p1 = x[half + i];
       dst[i] = __float2half_rn(p0 * c - p1 * s);
       dst[half + i] = __float2half_rn(p1 * c + p0 * s);
@@ -317,7 +329,10 @@ cudaError_t rmsnorm_launch(const float* x, int rows, int width, const float* w, 
 
 cudaError_t qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream) {
   if (a.dim > kMaxHeadDim || (a.dim & 1)) return cudaErrorInvalidValue;
-  qkv_post_kernel<<<a.tokens, kQkvWarps * 32, 0, stream>>>(a);
+  const int heads = a.hq + 2 * a.hkv;
+  const dim3 grid(static_cast<unsigned>(a.tokens),
+                  static_cast<unsigned>((heads + kQkvWarps - 1) / kQkvWarps));
+  qkv_post_kernel<<<grid, kQkvWarps * 32, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

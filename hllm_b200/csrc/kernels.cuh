@@ -73,6 +73,8 @@ struct QkvPostArgs {
   const float* k_norm;    // [d] or null
   float eps;
   const float* rope_pow;  // [d/2]: theta^(2i/d), computed on the host like the reference
+  const float2* rope_table;  // [positions][d/2] (cos, sin) from the host, or null
+  int rope_positions;
   __half* q_out;          // [T][Hq d]
   __half* k_cache;        // [blocks][Hkv][16][d] of this layer
   __half* v_cache;

@@ -145,6 +145,8 @@ struct hllm_b200_stage {
   __half* kv = nullptr;  // [layers][2][blocks][Hkv][16][d]
   size_t kv_layer_elems = 0;
   float* rope_pow = nullptr;
+  float2* rope_table = nullptr;  // [max positions][d/2] (cos, sin)
+  int rope_positions = 0;
 
   // per-step device tensors
   int32_t* up = nullptr;  // row_slot | row_first | row_count | sample_rows | ids
@@ -205,7 +207,7 @@ struct hllm_b200_stage {
     double bytes, flops;
     cudaEvent_t a, b;
   };
-  static constexpr int kProfKinds = 5;
+  static constexpr int kProfKinds = 9;
   bool profiling = false;
   std::vector<ProfEvent> prof_pending;
   std::vector<cudaEvent_t> event_pool;
@@ -435,6 +437,24 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
   s->rope_pow = s->alloc<float>(pw.size());
   check_cuda(cudaMemcpyAsync(s->rope_pow, pw.data(), pw.size() * sizeof(float),
                              cudaMemcpyHostToDevice, s->stream), "rope upload");
+  // (cos, sin) of position / theta^(2i/d) for every position, from the same
+  // F32 expressions (cpp/src/cpu/llama.cpp:222-231), so that the rotation
+  // matches the reference's values exactly.
+  {
+    const size_t positions = d.maximum_sequence_length, half = s->dim / 2;
+    std::vector<float2> table(positions * half);
+    for (size_t pos = 0; pos < positions; ++pos) {
+      const float position = static_cast<float>(pos);
+      for (size_t i = 0; i < half; ++i) {
+        const float angle = position / pw[i];
+        table[pos * half + i] = make_float2(std::cos(angle), std::sin(angle));
+      }
+    }
+    s->rope_table = s->alloc<float2>(table.size());
+    s->rope_positions = static_cast<int>(positions);
+    check_cuda(cudaMemcpy(s->rope_table, table.data(), table.size() * sizeof(float2),
+                          cudaMemcpyHostToDevice), "rope table upload");
+  }
 
   // ---- step workspaces
   const size_t R = s->R_max, T = s->T_max;
@@ -682,7 +702,8 @@ StepPlan plan_step(hllm_b200_stage* s, const hllm_b200_row* rows, uint32_t n, bo
 // and prefill width, decode attention (split + combine), prefill attention,
 // everything else (norms, q/k epilogue, packer, embedding, sampler, boundary).
 enum ProfKind { kProfGemmDecode = 0, kProfGemmPrefill = 1, kProfAttnDecode = 2,
-                kProfAttnPrefill = 3, kProfOther = 4 };
+                kProfAttnPrefill = 3, kProfOther = 4, kProfNorm = 5, kProfQkv = 6,
+                kProfSwiglu = 7, kProfSample = 8 };
 
 #define PLAUNCH(kind, bytes, flops, expr)               \
   do {                                                  \
@@ -792,7 +813,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     // Layer 0's input norm runs alone; every later one is fused into the
     // previous layer's residual consumer.
     if (li == 0)
-      PLAUNCH(kProfOther, 0, 0, hb::rmsnorm_launch(s->hidden, T, h, L.in_norm, eps, s->xn,
+      PLAUNCH(kProfNorm, 0, 0, hb::rmsnorm_launch(s->hidden, T, h, L.in_norm, eps, s->xn,
                                                    static_cast<int>(s->h_pad), nullptr, s->stream));
     const hb::GemmPlan pq = hb::gemm_plan(L.g_qkv, T, s->sm_count);
     hb::GemmSlots qslots{};
@@ -813,10 +834,12 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     qa.k_norm = L.k_norm;
     qa.eps = eps;
     qa.rope_pow = s->rope_pow;
+    qa.rope_table = s->rope_table;
+    qa.rope_positions = s->rope_positions;
     qa.q_out = s->q;
     qa.k_cache = kc;
     qa.v_cache = vc;
-    PLAUNCH(kProfOther, 0, 0, hb::qkv_post_launch(qa, s->stream));
+    PLAUNCH(kProfQkv, 0, 0, hb::qkv_post_launch(qa, s->stream));
     hb::AttnArgs aa{};
     aa.q = s->q;
     aa.k_cache = kc;
@@ -853,7 +876,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     PLAUNCH(gk, gemm_bytes(s->h, T, s->qw, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->qw, 1),
             hb::gemm_launch(L.g_o, s->in_attn, T, po, hb::kEpiResidual, s->hidden, h, s->slots, s->segmap,
                             &oslots, s->status, s->stream));
-    PLAUNCH(kProfOther, 0, 0,
+    PLAUNCH(kProfNorm, 0, 0,
             hb::residual_norm_launch(s->hidden, T, h, po.stream_k ? &oslots : nullptr,
                                      L.post_norm, eps, s->xn, static_cast<int>(s->h_pad),
                                      s->stream));
@@ -864,7 +887,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
             hb::gemm_launch(L.g_gu, s->in_xn, T, pg, hb::kEpiSwiGLU, s->act,
                             static_cast<int>(s->I_pad), s->slots, s->segmap, &gslots, s->status, s->stream));
     if (pg.stream_k)
-      PLAUNCH(kProfOther, 0, 0,
+      PLAUNCH(kProfSwiglu, 0, 0,
               hb::swiglu_launch(gslots, T, s->act, static_cast<int>(s->I_pad), s->stream));
     // down_proj, then the residual add fused with the next layer's input norm.
     const hb::GemmPlan pd = hb::gemm_plan(L.g_down, T, s->sm_count);
@@ -874,7 +897,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
                             &dslots, s->status, s->stream));
     const float* next_norm = li + 1 < s->n_layers ? s->layers[li + 1].in_norm : nullptr;
     if (pd.stream_k || next_norm)
-      PLAUNCH(kProfOther, 0, 0,
+      PLAUNCH(kProfNorm, 0, 0,
               hb::residual_norm_launch(s->hidden, T, h, pd.stream_k ? &dslots : nullptr,
                                        next_norm, eps, s->xn, static_cast<int>(s->h_pad),
                                        s->stream));
@@ -885,7 +908,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     if (p.samples) {
       const int S = static_cast<int>(p.samples);
       PLAUNCH(kProfOther, 0, 0, hb::last_token_launch(s->cu_seqlens, s->sample_rows, S, s->last_idx, s->stream));
-      PLAUNCH(kProfOther, 0, 0, hb::rmsnorm_launch(s->hidden, S, h, s->final_norm, eps, s->xs,
+      PLAUNCH(kProfNorm, 0, 0, hb::rmsnorm_launch(s->hidden, S, h, s->final_norm, eps, s->xs,
                                 static_cast<int>(s->h_pad), s->last_idx, s->stream));
       const hb::GemmPlan ph = hb::gemm_plan(s->g_head, S, s->sm_count);
       hb::GemmSlots hslots{};
@@ -894,10 +917,10 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
               hb::gemm_launch(s->g_head, s->in_xs, S, ph, hb::kEpiStoreF32, s->logits,
                               static_cast<int>(s->V), s->slots, s->segmap, &hslots, s->status, s->stream));
       if (ph.stream_k)
-        PLAUNCH(kProfOther, 0, 0,
+        PLAUNCH(kProfSwiglu, 0, 0,
                 hb::gemm_finish_launch(hslots, S, hb::kEpiStoreF32, s->logits,
                                        static_cast<int>(s->V), s->stream));
-      PLAUNCH(kProfOther, 0, 0, hb::sample_launch(s->logits, S, static_cast<int>(s->V), static_cast<int>(s->V),
+      PLAUNCH(kProfSample, 0, 0, hb::sample_launch(s->logits, S, static_cast<int>(s->V), static_cast<int>(s->V),
                                s->d_params, s->sample_scratch, s->results, s->status, s->stream));
     }
   } else {

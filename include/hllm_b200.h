@@ -195,7 +195,9 @@ hllm_b200_status hllm_b200_stage_last_transfer(const hllm_b200_stage* stage, uin
  * resets the counters and brackets every later launch with CUDA events on the
  * stage stream; 0 stops.  Kernel classes: 0 projection GEMMs at decode width
  * (<= 128 tokens), 1 projection GEMMs at prefill width, 2 decode attention
- * (split + combine), 3 prefill attention, 4 all other kernels.  profile_read
+ * (split + combine), 3 prefill attention, 4 packer / embedding / boundary,
+ * 5 RMSNorm and residual-add consumers, 6 q/k-norm + RoPE + KV write,
+ * 7 SwiGLU / split-sum consumers, 8 sampler.  profile_read
  * waits for the stream and returns a class's summed device milliseconds,
  * launch count, and algorithmic bytes and FLOPs.  No reference counterpart;
  * the reference times components with a host clock after a device
