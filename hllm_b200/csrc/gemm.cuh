@@ -120,6 +120,40 @@ __device__ inline float gemm_slot_sum(const GemmSlots& s, int n, int m, int acc)
     sum += __ldcg(s.slots + static_cast<size_t>(__ldcg(map + k)) * slot_floats + within);
   return sum;
 }
+
+// The same sum for four consecutive features m..m+3 (m % 4 == 0, one tile):
+// the tile's segment list is read once and the slot loads are issued together
+// before they are added (in CTA order, as gemm_slot_sum does).
+__device__ inline float4 gemm_slot_sum4(const GemmSlots& s, int n, int m, int acc) {
+  const int tile = (m >> 7) * s.n_tiles + n / s.bn;
+  const int count = __ldcg(s.segcount + tile);
+  const int4* map4 = reinterpret_cast<const int4*>(s.segmap + tile * kGemmMaxSegsPerTile);
+  const size_t within = static_cast<size_t>(acc) * s.bn * 128 +
+                        static_cast<size_t>(n % s.bn) * 128 + (m & 127);
+  const size_t slot_floats = static_cast<size_t>(s.pair) * s.bn * 128;
+  float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k0 = 0; k0 < count; k0 += 4) {
+    const int4 ids = __ldcg(map4 + (k0 >> 2));
+    const int id[4] = {ids.x, ids.y, ids.z, ids.w};
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      v[j] = k0 + j < count
+                 ? __ldcg(reinterpret_cast<const float4*>(
+                       s.slots + static_cast<size_t>(id[j]) * slot_floats + within))
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (k0 + j < count) {
+        sum.x += v[j].x;
+        sum.y += v[j].y;
+        sum.z += v[j].z;
+        sum.w += v[j].w;
+      }
+    }
+  }
+  return sum;
+}
 #endif
 
 }  // namespace hb

@@ -137,7 +137,7 @@ constexpr int kMaxHeadDim = 256;
 
 __global__ void __launch_bounds__(kQkvWarps * 32)
     qkv_post_kernel(QkvPostArgs a) {
-  __shared__ float buf[kQkvWarps][kMaxHeadDim];
+  __shared__ __align__(16) float buf[kQkvWarps][kMaxHeadDim];
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int d = a.dim, half = d / 2;
@@ -152,10 +152,11 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
        h += kQkvWarps) {
     const bool is_q = h < a.hq, is_k = !is_q && h < a.hq + a.hkv;
     float ss = 0.f;
-    for (int i = lane; i < d; i += 32) {
-      const float v = a.from_slots ? gemm_slot_sum(a.slots, t, h * d + i, 0) : row[h * d + i];
-      x[i] = v;
-      ss += v * v;
+    for (int i = lane * 4; i < d; i += 128) {  // d % 4 == 0 (checked at stage creation)
+      const float4 v = a.from_slots ? gemm_slot_sum4(a.slots, t, h * d + i, 0)
+                                    : *reinterpret_cast<const float4*>(row + h * d + i);
+      *reinterpret_cast<float4*>(x + i) = v;
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
     ss = warp_sum(ss);
     __syncwarp();
@@ -210,13 +211,29 @@ __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, Gemm
   const int t = blockIdx.x;
   float* xr = hidden + static_cast<size_t>(t) * width;
   float ss = 0.f;
-  for (int c = threadIdx.x; c < width; c += blockDim.x) {
-    float v = xr[c];
-    if (has_slots) {
-      v += gemm_slot_sum(slots, t, c, 0);
-      xr[c] = v;
+  if ((width & 3) == 0) {
+    // A warp covers 128 consecutive features = one GEMM tile row.
+    for (int c = threadIdx.x * 4; c < width; c += blockDim.x * 4) {
+      float4 v = *reinterpret_cast<const float4*>(xr + c);
+      if (has_slots) {
+        const float4 a = gemm_slot_sum4(slots, t, c, 0);
+        v.x += a.x;
+        v.y += a.y;
+        v.z += a.z;
+        v.w += a.w;
+        *reinterpret_cast<float4*>(xr + c) = v;
+      }
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
-    ss += v * v;
+  } else {
+    for (int c = threadIdx.x; c < width; c += blockDim.x) {
+      float v = xr[c];
+      if (has_slots) {
+        v += gemm_slot_sum(slots, t, c, 0);
+        xr[c] = v;
+      }
+      ss += v * v;
+    }
   }
   if (!w) return;
   __shared__ float red[32];
@@ -237,10 +254,23 @@ __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, Gemm
 // cpp/src/cpu/llama.cpp:274-280: (g / (1 + exp(-g))) * u.
 __global__ void swiglu_kernel(GemmSlots slots, __half* __restrict__ act, int ld_act) {
   const int t = blockIdx.y;
+  __half* out = act + static_cast<size_t>(t) * ld_act;
+  if ((slots.m & 3) == 0) {
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) * 4; i < slots.m;
+         i += gridDim.x * blockDim.x * 4) {
+      const float4 g = gemm_slot_sum4(slots, t, i, 0);
+      const float4 u = gemm_slot_sum4(slots, t, i, 1);
+      out[i] = __float2half_rn((g.x / (1.0f + expf(-g.x))) * u.x);
+      out[i + 1] = __float2half_rn((g.y / (1.0f + expf(-g.y))) * u.y);
+      out[i + 2] = __float2half_rn((g.z / (1.0f + expf(-g.z))) * u.z);
+      out[i + 3] = __float2half_rn((g.w / (1.0f + expf(-g.w))) * u.w);
+    }
+    return;
+  }
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < slots.m; i += gridDim.x * blockDim.x) {
     const float g = gemm_slot_sum(slots, t, i, 0);
     const float u = gemm_slot_sum(slots, t, i, 1);
-    act[static_cast<size_t>(t) * ld_act + i] = __float2half_rn((g / (1.0f + expf(-g))) * u);
+    out[i] = __float2half_rn((g / (1.0f + expf(-g))) * u);
   }
 }
 
@@ -351,7 +381,9 @@ cudaError_t residual_norm_launch(float* hidden, int tokens, int width, const Gem
 cudaError_t swiglu_launch(const GemmSlots& slots, int tokens, __half* act, int ld_act,
                           cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
-  const dim3 grid(static_cast<unsigned>((slots.m + 255) / 256), static_cast<unsigned>(tokens));
+  const int per_block = (slots.m & 3) == 0 ? 1024 : 256;
+  const dim3 grid(static_cast<unsigned>((slots.m + per_block - 1) / per_block),
+                  static_cast<unsigned>(tokens));
   swiglu_kernel<<<grid, 256, 0, stream>>>(slots, act, ld_act);
   return cudaGetLastError();
 }
