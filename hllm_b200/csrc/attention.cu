@@ -372,6 +372,19 @@ __global__ void __launch_bounds__(128)
   cp_async_wait<0>();
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
+  const int s0 = a.cu_splits[r];
+  const int ns = a.cu_splits[r + 1] - s0;
+  if (ns == 1) {  // the whole context in one split: normalise and store
+    if (g < G) {
+      const float inv = 1.0f / l;
+      __half* dst = a.out + static_cast<size_t>(t) * a.ld_out + static_cast<size_t>(kvh * G + g) * d;
+#pragma unroll
+      for (int db = 0; db < D / 8; ++db)
+        *reinterpret_cast<__half2*>(dst + db * 8 + (lane & 3) * 2) =
+            __floats2half2_rn(o[db][0] * inv, o[db][1] * inv);
+    }
+    return;
+  }
   if (g < G) {
     const int h = kvh * G + g;
     float* dst = a.part_o + (static_cast<size_t>(split) * a.hq + h) * d;
@@ -380,8 +393,51 @@ __global__ void __launch_bounds__(128)
       *reinterpret_cast<float2*>(dst + db * 8 + (lane & 3) * 2) = make_float2(o[db][0], o[db][1]);
     if ((lane & 3) == 0) {
       float* ml = a.part_ml + (static_cast<size_t>(split) * a.hq + h) * 2;
-      ml[0] = m * 0.6931471805599453f;  // back to the natural-log domain of the combine pass
+      ml[0] = m * 0.6931471805599453f;  // natural-log domain
       ml[1] = l;
+    }
+  }
+  // The last warp to finish a (row, kv head) merges its splits in split order;
+  // no warp waits for another.
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    int* counter = a.counters + static_cast<size_t>(r) * a.hkv + kvh;
+    last = atomicAdd(counter, 1) == ns - 1;
+    if (last) *counter = 0;
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  for (int gg = 0; gg < G; ++gg) {
+    const int h = kvh * G + gg;
+    const float* ml = a.part_ml + (static_cast<size_t>(s0) * a.hq + h) * 2;
+    float mm = -INFINITY;
+    for (int s = lane; s < ns; s += 32) mm = fmaxf(mm, __ldcg(ml + static_cast<size_t>(s) * a.hq * 2));
+    mm = warp_max(mm);
+    float ll = 0.f;
+    for (int s = lane; s < ns; s += 32) {
+      const float* e = ml + static_cast<size_t>(s) * a.hq * 2;
+      ll += __ldcg(e + 1) * expf(__ldcg(e) - mm);
+    }
+    ll = warp_sum(ll);
+    const float inv = 1.0f / ll;
+    const float* po = a.part_o + (static_cast<size_t>(s0) * a.hq + h) * d;
+    for (int i = lane * 4; i < D; i += 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int s = 0; s < ns; ++s) {
+        const float w = expf(__ldcg(ml + static_cast<size_t>(s) * a.hq * 2) - mm);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(po + static_cast<size_t>(s) * a.hq * d + i));
+        acc.x += v.x * w;
+        acc.y += v.y * w;
+        acc.z += v.z * w;
+        acc.w += v.w * w;
+      }
+      __half* dst = a.out + static_cast<size_t>(t) * a.ld_out + static_cast<size_t>(h) * d + i;
+      *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(acc.x * inv, acc.y * inv);
+      *reinterpret_cast<__half2*>(dst + 2) = __floats2half2_rn(acc.z * inv, acc.w * inv);
     }
   }
 }
@@ -716,11 +772,14 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t
     }
     decode_attn_kernel<<<dim3(a.hkv, total_splits), kDecThreads, smem, stream>>>(a);
     e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    decode_combine_kernel<<<dim3(a.rows, a.hq), 128, 0, stream>>>(a);
+    e = cudaGetLastError();
   }
-  if (e != cudaSuccess) return e;
-  decode_combine_kernel<<<dim3(a.rows, a.hq), 128, 0, stream>>>(a);
-  return cudaGetLastError();
+  return e;
 }
+
+int attn_decode_launches(int dim) { return (dim == 64 || dim == 128 || dim == 256) ? 1 : 2; }
 
 cudaError_t attn_prefill_launch(const AttnArgs& a, int total_qtiles, cudaStream_t stream) {
   if (total_qtiles <= 0) return cudaSuccess;

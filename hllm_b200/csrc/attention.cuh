@@ -24,6 +24,7 @@ struct AttnArgs {
   float scale;                 // 1/sqrt(d)
   float* part_o;               // [splits][Hq][d]  unnormalised split outputs
   float* part_ml;              // [splits][Hq][2]  running max, denominator
+  int* counters;               // [rows][Hkv] zero-initialised; returned to zero after use
   __half* out;                 // [T][ld_out]
   int ld_out;
   uint32_t* status;
@@ -32,8 +33,11 @@ struct AttnArgs {
 // Query tokens per prefill tile for a GQA group size (64 query rows per CTA).
 int attn_qtile_tokens(int group);
 
-// Decode rows (one new token): split-K over the context, then a combine pass.
+// Decode rows (one new token): split-K over the context; the splits of a row
+// are merged by the last warp to finish (head sizes 64/128/256) or by a
+// combine pass (other head sizes).
 cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t stream);
+int attn_decode_launches(int dim);
 // Prefill rows (several new tokens): causal tiles on the tensor cores.
 cudaError_t attn_prefill_launch(const AttnArgs& a, int total_qtiles, cudaStream_t stream);
 

@@ -177,7 +177,10 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
     // Split outputs live in a grow-only buffer per device, kept for the process.
     static std::mutex mu;
     static std::map<int, std::pair<float*, size_t>> buffers;
-    const size_t need = static_cast<size_t>(total_splits) * hq * (dim + 2);
+    // split outputs, then one arrival counter per (row, kv head), zeroed on
+    // allocation and returned to zero by the kernel after use
+    const size_t counter_off = static_cast<size_t>(total_splits) * hq * (dim + 2);
+    const size_t need = counter_off + static_cast<size_t>(rows) * hkv;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_status(e);
@@ -192,6 +195,7 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
         }
         buf = {nullptr, 0};
         e = cudaMalloc(&buf.first, need * sizeof(float));
+        if (e == cudaSuccess) e = cudaMemset(buf.first, 0, need * sizeof(float));
         if (e != cudaSuccess) return cuda_status(e);
         buf.second = need;
       }
@@ -199,6 +203,7 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
     }
     a.part_o = base;
     a.part_ml = base + static_cast<size_t>(total_splits) * hq * dim;
+    a.counters = reinterpret_cast<int*>(base + counter_off);
     e = hb::attn_decode_launch(a, static_cast<int>(total_splits), st);
     if (e != cudaSuccess) return cuda_status(e);
   }

@@ -168,6 +168,7 @@ struct hllm_b200_stage {
   float* logits = nullptr;
   double* sample_scratch = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
+  int* attn_counters = nullptr;  // [R_max][Hkv] split arrival counters (self-resetting)
   hb::GemmInput in_xn{}, in_attn{}, in_act{}, in_xs{};
   float* slots = nullptr;  // stream-K GEMM slots, consumed by the next kernel
   int* segmap = nullptr;   // their per-tile segment lists
@@ -495,6 +496,7 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
   }
   s->part_o = s->alloc<float>(s->max_splits * s->hq * s->dim);
   s->part_ml = s->alloc<float>(s->max_splits * s->hq * 2);
+  s->attn_counters = s->alloc<int>(R * s->hkv);
   s->slots = s->alloc<float>(hb::gemm_max_slot_floats(s->sm_count));
   s->segmap = s->alloc<int>(hb::kGemmMapInts);
   if (!hb::gemm_make_input(&s->in_xn, s->xn, static_cast<int>(T), static_cast<int>(s->h_pad),
@@ -861,12 +863,13 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     aa.scale = 1.0f / std::sqrt(static_cast<float>(s->dim));
     aa.part_o = s->part_o;
     aa.part_ml = s->part_ml;
+    aa.counters = s->attn_counters;
     aa.out = s->attn;
     aa.ld_out = static_cast<int>(s->qw_pad);
     aa.status = s->status;
     if (p.total_splits) {
       PLAUNCH(kProfAttnDecode, p.attn_dec_bytes, p.attn_dec_flops, hb::attn_decode_launch(aa, p.total_splits, s->stream));
-      ++s->launches;  // combine pass
+      s->launches += hb::attn_decode_launches(static_cast<int>(s->dim)) - 1;  // combine pass
     }
     if (p.total_qtiles)
       PLAUNCH(kProfAttnPrefill, p.attn_pre_bytes, p.attn_pre_flops, hb::attn_prefill_launch(aa, p.total_qtiles, s->stream));
