@@ -177,10 +177,13 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
     // Split outputs live in a grow-only buffer per device, kept for the process.
     static std::mutex mu;
     static std::map<int, std::pair<float*, size_t>> buffers;
-    // split outputs, then one arrival counter per (row, kv head), zeroed on
-    // allocation and returned to zero by the kernel after use
-    const size_t counter_off = static_cast<size_t>(total_splits) * hq * (dim + 2);
-    const size_t need = counter_off + static_cast<size_t>(rows) * hkv;
+    // A fixed block of arrival counters (one per (row, kv head); zeroed on
+    // allocation and returned to zero by the kernel after use) at the head of
+    // the buffer, then the split outputs.
+    constexpr size_t kCounters = 1 << 16;
+    if (static_cast<size_t>(rows) * hkv > kCounters) return HLLM_B200_INVALID_REQUEST;
+    const size_t counter_off = 0;
+    const size_t need = kCounters + static_cast<size_t>(total_splits) * hq * (dim + 2);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_status(e);
@@ -201,9 +204,9 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
       }
       base = buf.first;
     }
-    a.part_o = base;
-    a.part_ml = base + static_cast<size_t>(total_splits) * hq * dim;
     a.counters = reinterpret_cast<int*>(base + counter_off);
+    a.part_o = base + kCounters;
+    a.part_ml = a.part_o + static_cast<size_t>(total_splits) * hq * dim;
     e = hb::attn_decode_launch(a, static_cast<int>(total_splits), st);
     if (e != cudaSuccess) return cuda_status(e);
   }
