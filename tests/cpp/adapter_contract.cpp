@@ -1,0 +1,159 @@
+// adapter_contract.cpp -- the B200 stage behind hLLM's own runtime types.
+//
+// Built by tests/cpp/Makefile against the reference headers and sources
+// (runtime/stage_backend.hpp, decode_batch.cpp, worker/scheduler.cpp) and
+// libhllm_b200.so; run by tests/test_gpu_adapter.py on a B200.
+//
+//  1. The decode-batch contract of tests/cpp/decode_batch_contract.hpp:8-47 in
+//     the reference: a ragged batch (lengths 7, 2, 4, 1) run through
+//     execute_decode_batch equals serial execute: same tokens, logprobs within
+//     0.02, same generated_index; greedy and seeded sampling.
+//  2. The reference's StageScheduler (cpp/src/worker/scheduler.cpp) driving the
+//     backend from concurrent request threads: every request's tokens equal a
+//     serial run's, and the scheduler formed decode batches of at most 8.
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <memory>
+#include <thread>
+#include <variant>
+#include <vector>
+
+#include "b200_stage_backend.hpp"
+#include "hllm/worker/scheduler.hpp"
+
+using namespace hllm;
+
+namespace {
+int failures = 0;
+#define EXPECT(cond, ...)                        \
+  do {                                           \
+    if (!(cond)) {                               \
+      ++failures;                                \
+      std::printf("FAIL %s:%d ", __FILE__, __LINE__); \
+      std::printf(__VA_ARGS__);                  \
+      std::printf("\n");                         \
+    }                                            \
+  } while (0)
+
+std::unique_ptr<b200::B200StageBackend> make_stage(std::uint64_t seed) {
+  hllm_b200_stage_desc d{};
+  d.hidden_size = 256;
+  d.intermediate_size = 688;
+  d.attention_heads = 4;
+  d.key_value_heads = 2;
+  d.head_dimension = 64;
+  d.maximum_sequence_length = 256;
+  d.rms_norm_epsilon = 1e-6F;
+  d.rope_theta = 1e6F;
+  d.query_key_norm = 1;
+  d.vocabulary_size = 4096;
+  d.layer_start = 0;
+  d.layer_end = 2;
+  d.first = 1;
+  d.final = 1;
+  d.tied_head = 1;
+  d.device_id = 0;
+  d.kv_pool_tokens = 8192;
+  d.max_step_tokens = 512;
+  d.max_step_rows = 64;
+  d.max_sequences = 64;
+  hllm_b200_stage* stage = nullptr;
+  b200::check(hllm_b200_stage_create(&d, &stage));
+  b200::check(hllm_b200_stage_init_synthetic(stage, seed));
+  b200::check(hllm_b200_stage_finalize(stage));
+  return std::make_unique<b200::B200StageBackend>(stage, true, true);
+}
+
+void decode_batch_case(runtime::StageBackend& stage, double temperature) {
+  std::atomic_bool cancelled{false};
+  std::vector<std::unique_ptr<runtime::SequenceState>> reference, batched;
+  const std::vector<std::size_t> lengths{7, 2, 4, 1};
+  std::vector<runtime::SampledToken> expected;
+  for (std::size_t i = 0; i < lengths.size(); ++i) {
+    reference.push_back(stage.allocate_sequence(lengths[i] + 1U));
+    batched.push_back(stage.allocate_sequence(lengths[i] + 1U));
+    for (auto* state : {reference.back().get(), batched.back().get()}) {
+      state->sampling = {temperature, 0.95, 8, i + 42U, true, 3};
+      static_cast<void>(stage.execute(
+          runtime::TokenInput{std::vector<std::uint64_t>(lengths[i], 1U)}, 0U, *state, cancelled));
+    }
+    expected.push_back(std::get<runtime::SampledToken>(
+        stage.execute(runtime::TokenInput{{4U}}, lengths[i], *reference.back(), cancelled)));
+  }
+  std::vector<runtime::DecodeBatchItem> items;
+  for (std::size_t i = 0; i < lengths.size(); ++i)
+    items.push_back({runtime::TokenInput{{4U}}, lengths[i], batched[i].get(), &cancelled});
+  const auto actual = stage.execute_decode_batch(std::move(items));
+  EXPECT(actual.size() == expected.size(), "batch size");
+  for (std::size_t i = 0; i < expected.size() && i < actual.size(); ++i) {
+    const auto& token = std::get<runtime::SampledToken>(actual[i]);
+    EXPECT(token.id == expected[i].id, "token %zu: %llu vs %llu", i,
+           static_cast<unsigned long long>(token.id),
+           static_cast<unsigned long long>(expected[i].id));
+    EXPECT(token.logprob && expected[i].logprob &&
+               std::abs(*token.logprob - *expected[i].logprob) < 0.02,
+           "logprob %zu", i);
+    EXPECT(token.top_logprobs.size() == 3U, "top logprobs %zu", i);
+    EXPECT(batched[i]->generated_index == reference[i]->generated_index, "generated_index %zu", i);
+  }
+}
+
+std::vector<std::uint64_t> run_request(runtime::StageBackend& stage,
+                                       worker::StageScheduler* scheduler,
+                                       const std::vector<std::uint64_t>& prompt, int steps) {
+  std::atomic_bool cancelled{false};
+  auto state = stage.allocate_sequence(prompt.size() + steps);
+  std::vector<std::uint64_t> out;
+  std::vector<std::uint64_t> input = prompt;
+  std::size_t position = 0;
+  const auto deadline = std::chrono::system_clock::now() + std::chrono::minutes(5);
+  for (int s = 0; s < steps; ++s) {
+    runtime::StageOutput result =
+        scheduler ? scheduler->execute(stage, runtime::TokenInput{input}, position, *state,
+                                       cancelled, deadline)
+                  : stage.execute(runtime::TokenInput{input}, position, *state, cancelled);
+    const auto token = std::get<runtime::SampledToken>(result).id;
+    out.push_back(token);
+    position += input.size();
+    input = {token};
+  }
+  return out;
+}
+}  // namespace
+
+int main() {
+  auto stage = make_stage(7);
+  decode_batch_case(*stage, 0.0);
+  decode_batch_case(*stage, 0.8);
+
+  // Concurrent requests through the reference scheduler vs serial execution.
+  const int requests = 6, steps = 10;
+  std::vector<std::vector<std::uint64_t>> prompts;
+  for (int r = 0; r < requests; ++r) {
+    std::vector<std::uint64_t> p;
+    for (int i = 0; i < 5 + 3 * r; ++i) p.push_back(static_cast<std::uint64_t>((r * 977 + i * 31) % 4096));
+    prompts.push_back(p);
+  }
+  std::vector<std::vector<std::uint64_t>> serial;
+  for (int r = 0; r < requests; ++r) serial.push_back(run_request(*stage, nullptr, prompts[r], steps));
+  worker::StageScheduler scheduler;
+  scheduler.configure(8);
+  std::vector<std::vector<std::uint64_t>> concurrent(requests);
+  std::vector<std::thread> threads;
+  for (int r = 0; r < requests; ++r)
+    threads.emplace_back([&, r] { concurrent[r] = run_request(*stage, &scheduler, prompts[r], steps); });
+  for (auto& t : threads) t.join();
+  for (int r = 0; r < requests; ++r)
+    EXPECT(concurrent[r] == serial[r], "request %d tokens differ under the scheduler", r);
+  const auto metrics = scheduler.metrics();
+  EXPECT(metrics.completed_steps == static_cast<std::size_t>(requests * steps), "completed %zu",
+         metrics.completed_steps);
+  EXPECT(metrics.largest_decode_batch <= 8U, "largest batch %zu", metrics.largest_decode_batch);
+  std::printf("decode_batches=%zu largest_decode_batch=%zu completed_steps=%zu\n",
+              metrics.decode_batches, metrics.largest_decode_batch, metrics.completed_steps);
+  std::printf(failures ? "adapter contract: %d failures\n" : "adapter contract: ok\n", failures);
+  return failures ? 1 : 0;
+}
