@@ -1,0 +1,136 @@
+"""Per-operator timing of the executor's kernels through the C ABI.
+
+    python -m hllm_b200.opbench [gemm|attn|all] [--ncu-gemm M,K,N,PAIR,EPI]
+
+Times the projection GEMM at the Qwen3-4B shapes (decode width 16/64 tokens,
+prefill width 575 tokens) and the paged decode attention at configuration-5
+batch sizes (contexts log-uniform in [128, 32768], 16-token pages randomly
+placed in a pool), with CUDA events on the current stream after warm-up.
+Inputs are far larger than L2 for the weight-streaming shapes.  `--ncu-gemm`
+runs three launches of one GEMM shape (for a profiler capture).
+Device memory comes from torch; all compute is libhllm_b200.so.
+"""
+from __future__ import annotations
+
+import math
+import sys
+
+import numpy as np
+
+
+def _torch():
+    import torch
+    if not torch.cuda.is_available():
+        raise SystemExit("opbench needs a CUDA device")
+    return torch
+
+
+def ev_time(fn, iters=20, warm=3):
+    torch = _torch()
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters * 1e3  # microseconds per call
+
+
+def gemm_case(m, k, n, pair=1, epi=0, bn=0, grid=0, iters=20):
+    torch = _torch()
+    from . import _lib
+    L = _lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    rows = m * pair
+    W = (torch.randn(rows, k, device="cuda") * 0.02).half()
+    X = torch.randn(max(n, 1), k, device="cuda").half()
+    outdt = torch.float32 if epi in (0, 2) else torch.float16
+    Y = torch.zeros(n, m, device="cuda", dtype=outdt)
+
+    def fn():
+        _lib.check(L.hllm_b200_gemm(W.data_ptr(), m, k, pair, m if pair == 2 else 0, X.data_ptr(),
+                                    n, epi, Y.data_ptr(), m, bn, grid, stream))
+    us = ev_time(fn, iters)
+    nbytes = rows * k * 2 + n * k * 2 + n * m * (4 if outdt == torch.float32 else 2)
+    flops = 2 * rows * n * k
+    print(f"gemm m={m} pair={pair} k={k} n={n} epi={epi}: {us:8.1f} us  "
+          f"{nbytes / us / 1e3:8.1f} GB/s  {flops / us / 1e6:8.1f} TFLOP/s", flush=True)
+    return us
+
+
+def attn_case(rows_ctx, hq=32, hkv=8, d=128, split=256, iters=10):
+    """Decode attention over rows with the given contexts (one new token each)."""
+    torch = _torch()
+    from . import _lib
+    L = _lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    R = len(rows_ctx)
+    need = [(c + 15) // 16 for c in rows_ctx]
+    nblocks = int(sum(need) * 1.2) + 8
+    perm = np.random.default_rng(0).permutation(nblocks).astype(np.int32)
+    mb = max(need)
+    tables = np.full((R, mb), -1, np.int32)
+    o = 0
+    for r, nb in enumerate(need):
+        tables[r, :nb] = perm[o:o + nb]
+        o += nb
+    kc = (torch.randn(nblocks, hkv, 16, d, device="cuda") / math.sqrt(d)).half()
+    vc = (torch.randn(nblocks, hkv, 16, d, device="cuda") / math.sqrt(d)).half()
+    q = (torch.randn(R, hq * d, device="cuda") / math.sqrt(d)).half()
+    ctx = np.asarray(rows_ctx, np.int32)
+    first = ctx - 1
+    count = np.ones(R, np.int32)
+    cu = np.arange(R + 1, dtype=np.int32)
+    sp = (ctx + split - 1) // split
+    cu_s = np.concatenate([[0], np.cumsum(sp)]).astype(np.int32)
+    cu_q = np.zeros(R + 1, np.int32)
+    dv = [torch.from_numpy(x).cuda() for x in (first, count, cu, ctx, tables, cu_s, cu_q)]
+    out = torch.zeros(R, hq * d, device="cuda").half()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def fn():
+        _lib.check(L.hllm_b200_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                         *[t.data_ptr() for t in dv], R, int(cu_s[-1]), 0, hq,
+                                         hkv, d, mb, split, out.data_ptr(), hq * d,
+                                         status.data_ptr(), stream))
+    us = ev_time(fn, iters)
+    nbytes = sum(rows_ctx) * hkv * d * 2 * 2 + R * hq * d * 4
+    print(f"decode attention B={R} sum_ctx={sum(rows_ctx)} split={split}: {us:8.1f} us  "
+          f"{nbytes / us / 1e3:8.1f} GB/s", flush=True)
+    return us
+
+
+def gemm_suite():
+    # (m, k, n, pair, epilogue): Qwen3-4B QKV, gate/up, down, o, LM head
+    for args in [(6144, 2560, 64, 1, 0), (9728, 2560, 64, 2, 3), (2560, 9728, 64, 1, 2),
+                 (2560, 4096, 64, 1, 2), (151936, 2560, 64, 1, 0), (6144, 2560, 16, 1, 0),
+                 (6144, 2560, 575, 1, 0), (9728, 2560, 575, 2, 3), (2560, 9728, 575, 1, 2),
+                 (2560, 4096, 575, 1, 2)]:
+        gemm_case(*args)
+
+
+def attn_suite():
+    rng = np.random.default_rng(5)
+    for B in (1, 8, 32, 128, 256):
+        ctx = np.exp(rng.uniform(np.log(128), np.log(32768), B)).astype(int).tolist()
+        for split in (128, 512, 2048):
+            attn_case(ctx, split=split)
+
+
+def main(argv):
+    if "--ncu-gemm" in argv:
+        m, k, n, pair, epi = (int(x) for x in argv[argv.index("--ncu-gemm") + 1].split(","))
+        gemm_case(m, k, n, pair, epi, iters=3)
+        return
+    what = argv[1] if len(argv) > 1 else "all"
+    if what in ("gemm", "all"):
+        gemm_suite()
+    if what in ("attn", "all"):
+        attn_suite()
+
+
+if __name__ == "__main__":
+    main(sys.argv)
