@@ -108,6 +108,8 @@ def lib():
         "hllm_b200_stage_read_hidden": (C.c_int, [vp, C.POINTER(C.c_float), u64]),
         "hllm_b200_stage_read_logits": (C.c_int, [vp, C.POINTER(C.c_float), u64]),
         "hllm_b200_gemm": (C.c_int, [vp, u64, u64, u32, u64, vp, u64, u32, vp, u64, u32, u32, vp]),
+        "hllm_b200_gemm_noalloc": (C.c_int, [vp, u64, u64, u32, u64, vp, u64, u32, vp, u64, u32,
+                                             u32, vp]),
         "hllm_b200_rmsnorm": (C.c_int, [vp, u64, u64, vp, f32, vp, u64, vp]),
         "hllm_b200_pack": (C.c_int, [vp, vp, vp, u32, u32, vp, u32, u32, u32] + [vp] * 9 + [vp]),
         "hllm_b200_attention": (C.c_int, [vp] * 10 + [u32] * 8 + [vp, u64, vp, vp]),

@@ -233,6 +233,24 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
                                 uint64_t second_row, const void* x, uint64_t n, uint32_t epilogue,
                                 void* y, uint64_t ldy, uint32_t bn, uint32_t grid, void* stream);
 
+/* The same GEMM without allocating anything.  No counterpart in the reference:
+ * it exists for callers that cannot let a library allocate device memory --
+ * a serving process that fixes its device budget at start-up and admits
+ * requests against it, or a host that owns all of a plugin's device memory.
+ * Its split-K scratch is a static device array of 32 MiB (+68 KiB of segment
+ * lists) that every GPU loading the library holds until the process exits.
+ * Splits that need more partial-sum storage than that are rejected with
+ * HLLM_B200_RESOURCE_EXHAUSTED and a message; plans that need none always run.
+ * The first call on a device, with that device current, resolves the array's
+ * device address (cudaGetSymbolAddress); make that first call before any
+ * stream capture.  All calls on a device share the array: calls whose GPU
+ * work overlaps (e.g. on two streams) race and must not be issued.  Calls no
+ * cudaMalloc/cudaFree. */
+hllm_b200_status hllm_b200_gemm_noalloc(const void* w, uint64_t m, uint64_t k_pad, uint32_t pair,
+                                        uint64_t second_row, const void* x, uint64_t n,
+                                        uint32_t epilogue, void* y, uint64_t ldy, uint32_t bn,
+                                        uint32_t grid, void* stream);
+
 /* RMSNorm of rows of F32 x into F16 out (cpp/src/cpu/llama.cpp:193-212). */
 hllm_b200_status hllm_b200_rmsnorm(const float* x, uint64_t rows, uint64_t width, const float* w,
                                    float eps, uint16_t* out, uint64_t ld_out, void* stream);
