@@ -153,8 +153,12 @@ def make_stage(device: int):
     return stage, cfg
 
 
-def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, clocks=None):
-    """Steps [0, first_timed + K) with device-resident ids; times the last K."""
+def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, clocks=None,
+                     profiler_range=False):
+    """Steps [0, first_timed + K) with device-resident ids; times the last K.
+
+    With profiler_range the timed steps are bracketed by cudaProfilerStart/Stop, so
+    that `ncu --profile-from-start off` lists exactly their launches."""
     import torch
     from hllm_b200 import _lib
     L = _lib.lib()
@@ -186,6 +190,8 @@ def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, cl
             if clocks:
                 clocks.start()
             torch.cuda.synchronize()
+            if profiler_range:
+                torch.cuda.profiler.start()
             start.record(stream)
         for r in admits:
             seqs[r.rid] = stage.allocate_sequence(r.capacity)
@@ -205,6 +211,8 @@ def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, cl
     end.record(stream)
     _lib.check(L.hllm_b200_stage_sync(stage.handle))
     torch.cuda.synchronize()
+    if profiler_range:
+        torch.cuda.profiler.stop()
     ms = start.elapsed_time(end)
     clock_info = clocks.stop() if clocks else None
     prof = None
@@ -331,7 +339,8 @@ def ours(args, world, rank, local):
     # value: device-resident inputs, steps enqueued back to back
     clocks = ClockSampler(local)
     dev_ms, dev_tokens, launches, _, clock_info = run_device_phase(
-        stage, cfg, trace, steps, first_timed, K, clocks=clocks)
+        stage, cfg, trace, steps, first_timed, K, clocks=clocks,
+        profiler_range=args.profiler_range)
     if args.device_phase_only:
         print(json.dumps({"device_phase_ms_per_step": round(dev_ms / K, 4),
                           "tokens_per_s": round(dev_tokens / (dev_ms / 1e3), 1),
@@ -474,6 +483,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--fast-forward", type=int, default=150)
+    ap.add_argument("--profiler-range", action="store_true",
+                    help="bracket the timed device-phase steps with cudaProfilerStart/Stop")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--device-phase-only", action="store_true",
                     help="run only the device-resident phase (for profiler launch lists)")

@@ -9,15 +9,19 @@
 // pages, every query head of a GQA group shares one pass over its KV pages,
 // and no score matrix is stored (online softmax).
 //
-//   decode rows:  split-K over the context.  Each CTA takes one (kv head,
-//                 context split); a single thread streams the split's 16-token
-//                 K and V pages into a shared-memory ring with cp.async.bulk
-//                 (TMA bulk copies, mbarrier completion, bounded waits); a
-//                 combine pass merges the splits.
+//   decode rows:  head sizes 64/128/256 -- the batch's KV pages split evenly
+//                 over one wave of warps (ranges cross row boundaries), QK^T
+//                 and PV on the tensor cores (mma.sync), pieces merged by the
+//                 last warp of each (row, kv head).  Other head sizes -- split-K
+//                 with one CTA per (kv head, context split) streaming 16-token
+//                 pages with cp.async.bulk (mbarrier completion, bounded
+//                 waits), then a combine pass.
 //   prefill rows: causal flash tiles on the tensor cores (mma.sync F16 -> F32),
 //                 64 query rows per CTA = (tokens x heads of one GQA group),
 //                 K/V pages gathered by block table with cp.async.
 #include <math.h>
+
+#include <algorithm>
 
 #include "attention.cuh"
 #include "common.cuh"
@@ -239,93 +243,314 @@ __global__ void __launch_bounds__(kDecThreads)
 }
 
 // ---------------------------------------------------------------- decode (tensor cores)
-// One warp per (decode row, kv head, context split); four independent warps
-// per CTA, no CTA-wide synchronisation.  The G query heads of the kv head are
-// the first G rows of an m16n8k16 tile (rows G..15 are zero), so QK^T and PV
-// run on the tensor cores; K/V pages (16 keys x d) stream through a per-warp
-// cp.async ring in an XOR-swizzled layout that ldmatrix reads without bank
-// conflicts.  Partial (m, l, O) per split go to the combine pass.
-constexpr int kWarpStages = 3;
+// Work is balanced over pages, not rows.  The decode rows' KV pages form one
+// sequence ordered (row, kv head, page); each (row, kv head) is a "stream" of
+// ceil(ctx / 16) pages.  Warp w of W takes the contiguous range
+// [P w / W, P (w + 1) / W) of the P pages, whatever the rows' lengths, so one
+// wave of warps finishes together.  A warp's range may cross streams; for each
+// stream it touches it keeps a piece (m, l, unnormalised O of the G query
+// heads).  A stream inside one warp is normalised and stored at once;
+// otherwise its pieces go to part_o/part_ml at index (stream + warp) -- unique,
+// since both grow along the sequence -- and the last of the stream's warps to
+// arrive merges them in warp order (deterministic).
+//
+// Per warp: the G query heads of the kv head are the first G rows of an
+// m16n8k16 tile (rows G..15 are zero), so QK^T and PV run on the tensor cores.
+// K/V pages (16 keys x d) stream through a per-warp cp.async ring in an
+// XOR-swizzled layout that ldmatrix reads without bank conflicts; a stream's
+// query heads ride in the ring stage of its first page.  The ring runs ahead
+// across stream boundaries, and block-table entries are fetched 32 pages at a
+// time, so no global load sits between one page and the next.
+// Ring depth: three stages (two pages in flight while one is computed); two
+// for d = 256, whose stages would not fit three deep in shared memory.
+template <int D>
+__host__ __device__ constexpr int dec_stages() {
+  return D >= 256 ? 2 : 3;
+}
 
 template <int D>
 __device__ __forceinline__ uint32_t page_off(int row, int chunk) {
   return static_cast<uint32_t>(row * D * 2 + ((chunk ^ (row & 7)) * 16));
 }
 
+// Bytes of one ring stage: K page, V page, the group's query heads.
+__host__ __device__ constexpr uint32_t decode_stage_bytes(int d, int group) {
+  return 2u * 16u * d * 2u + ((static_cast<uint32_t>(group) * d * 2u + 127u) & ~127u);
+}
+
+// Position in the page sequence: row, kv head, page within the stream, and
+// the row's page count, context length and first packed token.
+struct PageCursor {
+  int r, kvh, q;
+  int pages, ctx, t;
+  long long cum;  // pages of the decode rows before r (one kv head)
+};
+
+__device__ __forceinline__ void cursor_load_row(const AttnArgs& a, PageCursor& c) {
+  const int count = __ldg(a.row_count + c.r);
+  c.ctx = __ldg(a.seq_lens + c.r);
+  c.t = __ldg(a.cu_seqlens + c.r);
+  c.pages = count == 1 ? (c.ctx + 15) >> 4 : 0;
+}
+
+__device__ __forceinline__ void cursor_next(const AttnArgs& a, PageCursor& c) {
+  if (++c.q < c.pages) return;
+  c.q = 0;
+  if (++c.kvh < a.hkv) return;
+  c.kvh = 0;
+  c.cum += c.pages;
+  while (++c.r < a.rows) {
+    cursor_load_row(a, c);
+    if (c.pages) return;
+  }
+  c.pages = 0;
+}
+
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Decode pages of rows base + 32k + lane, k < 4 (0 past the end or for prefill
+// rows); all eight loads are issued together.
+__device__ __forceinline__ void load_row_pages(const AttnArgs& a, int base, int lane, int (&pg)[4]) {
+  int cnt[4], len[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = base + 32 * k + lane;
+    cnt[k] = r < a.rows ? __ldg(a.row_count + r) : 0;
+    len[k] = r < a.rows ? __ldg(a.seq_lens + r) : 0;
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) pg[k] = cnt[k] == 1 ? (len[k] + 15) >> 4 : 0;
+}
+
+// Merges the ns pieces of one stream (pieces p0 + s * G + g, s < ns, g < G)
+// in piece order and stores the G normalised head outputs at `out`.
+template <int D>
+__device__ __noinline__ void decode_merge(const AttnArgs& a, size_t p0, int ns, int G,
+                                          __half* out, int lane) {
+  if (G * ns <= 32 && (G & (G - 1)) == 0) {
+    // One (piece, head) per lane: j = s * G + g.  Lanes with equal g are the
+    // lanes j ^ (multiples of G), so xor shuffles reduce per head.
+    const int j = lane;
+    float mj = -INFINITY, lj = 0.f;
+    if (j < G * ns) {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(a.part_ml + (p0 + j) * 2));
+      mj = v.x;
+      lj = v.y;
+    }
+    float M = mj;
+    for (int o = G; o < 32; o <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float wj = j < G * ns ? expf(mj - M) : 0.f;
+    float L = lj * wj;
+    for (int o = G; o < 32; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    // Output float4 f = lane + 32 k of the G x D block.
+    constexpr int kMaxF = (8 * D / 4 + 31) / 32;
+    const int nf4 = G * D / 4;
+    float4 acc[kMaxF];
+#pragma unroll
+    for (int k = 0; k < kMaxF; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
+    for (int s = 0; s < ns; ++s) {
+#pragma unroll
+      for (int k = 0; k < kMaxF; ++k) {
+        const int f = lane + 32 * k;
+        const int gg = min(f * 4 / D, G - 1);
+        const float wt = __shfl_sync(0xffffffffu, wj, s * G + gg);
+        if (f < nf4) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(
+              a.part_o + (p0 + static_cast<size_t>(s) * G + gg) * D + (f * 4) % D));
+          acc[k].x += wt * v.x;
+          acc[k].y += wt * v.y;
+          acc[k].z += wt * v.z;
+          acc[k].w += wt * v.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxF; ++k) {
+      const int f = lane + 32 * k;
+      const int gg = min(f * 4 / D, G - 1);
+      const float inv = 1.0f / __shfl_sync(0xffffffffu, L, gg);
+      if (f < nf4) {
+        __half* dst = out + f * 4;  // head gg, element (f * 4) % D
+        *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(acc[k].x * inv, acc[k].y * inv);
+        *reinterpret_cast<__half2*>(dst + 2) = __floats2half2_rn(acc[k].z * inv, acc[k].w * inv);
+      }
+    }
+    return;
+  }
+  // Many pieces (or a group size that is not a power of two): one head at a time.
+  for (int gg = 0; gg < G; ++gg) {
+    const float* ml = a.part_ml + (p0 + gg) * 2;
+    const size_t mls = static_cast<size_t>(G) * 2;
+    float mm = -INFINITY;
+    for (int s = lane; s < ns; s += 32) mm = fmaxf(mm, __ldcg(ml + s * mls));
+    mm = warp_max(mm);
+    float ll = 0.f;
+    for (int s = lane; s < ns; s += 32) ll += __ldcg(ml + s * mls + 1) * expf(__ldcg(ml + s * mls) - mm);
+    ll = warp_sum(ll);
+    const float inv = 1.0f / ll;
+    const float* po = a.part_o + (p0 + gg) * D;
+    const size_t pos = static_cast<size_t>(G) * D;
+    for (int i0 = lane * 4; i0 < D; i0 += 128) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+      for (int s = 0; s < ns; ++s) {
+        const float wt = expf(__ldcg(ml + s * mls) - mm);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(po + s * pos + i0));
+        acc.x += v.x * wt;
+        acc.y += v.y * wt;
+        acc.z += v.z * wt;
+        acc.w += v.w * wt;
+      }
+      __half* dst = out + gg * D + i0;
+      *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(acc.x * inv, acc.y * inv);
+      *reinterpret_cast<__half2*>(dst + 2) = __floats2half2_rn(acc.z * inv, acc.w * inv);
+    }
+  }
+}
+
 template <int D>
 __global__ void __launch_bounds__(128)
-    decode_attn_mma_kernel(const AttnArgs a, int total_items) {
+    decode_attn_mma_kernel(const AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr uint32_t kPage = 16 * D * 2;  // bytes of one K (or V) page
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int item = blockIdx.x * 4 + warp;
-  if (item >= total_items) return;
-  const int kvh = item % a.hkv;
-  const int split = item / a.hkv;
-  const int r = find_row(a.cu_splits, a.rows, split);
-  if (a.row_count[r] != 1) return;
-  const int G = a.hq / a.hkv;
-  const int d = a.dim;
-  const int ctx = a.seq_lens[r];
-  const int key0 = (split - a.cu_splits[r]) * a.split_tokens;
-  const int key1 = min(ctx, key0 + a.split_tokens);
-  const int kb0 = key0 >> 4;
-  const int npage = ((key1 + 15) >> 4) - kb0;
-  const int t = a.cu_seqlens[r];
-  const int32_t* table = a.block_tables + static_cast<size_t>(r) * a.max_blocks;
-  uint8_t* ring = smem + warp * (kWarpStages * 2 * kPage);
+  const int w = blockIdx.x * 4 + warp;
+  const int hkv = a.hkv;
+  const int G = a.hq / hkv;
+  const uint32_t stage_bytes = decode_stage_bytes(D, G);
 
+  // Total pages P (every warp computes it; the rows' counts are L2-resident).
+  long long total = 0;
+  for (int base = 0; base < a.rows; base += 128) {
+    int pg[4];
+    load_row_pages(a, base, lane, pg);
+    total += warp_sum_int(pg[0] + pg[1] + pg[2] + pg[3]);
+  }
+  total *= hkv;
+  // At most one warp per page, so that every warp in [0, W) owns at least one
+  // page and each stream's pieces come from consecutive warps.
+  const int W = static_cast<int>(min(static_cast<long long>(gridDim.x) * 4, total));
+  if (w >= W) return;
+  const long long p_begin = total * w / W, p_end = total * (w + 1) / W;
+
+  // Locate p_begin: the row whose pages (x hkv) cover it.
+  PageCursor c{};
+  c.r = -1;
+  {
+    long long cum = 0;
+    for (int base = 0; base < a.rows && c.r < 0; base += 128) {
+      int pg[4];
+      load_row_pages(a, base, lane, pg);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        int incl = pg[k];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        const long long lo = (cum + incl - pg[k]) * hkv, hi = (cum + incl) * hkv;
+        const unsigned hit =
+            __ballot_sync(0xffffffffu, pg[k] > 0 && lo <= p_begin && p_begin < hi);
+        if (c.r < 0 && hit) {
+          const int src = __ffs(hit) - 1;
+          c.r = base + 32 * k + src;
+          c.cum = cum + __shfl_sync(0xffffffffu, incl - pg[k], src);
+        }
+        cum += __shfl_sync(0xffffffffu, incl, 31);
+      }
+    }
+    if (c.r < 0) {  // unreachable for consistent row counts
+      if (lane == 0) atomicOr(a.status, kDevBadIndex);
+      return;
+    }
+    cursor_load_row(a, c);
+    const long long off = p_begin - c.cum * hkv;
+    c.kvh = static_cast<int>(off / c.pages);
+    c.q = static_cast<int>(off % c.pages);
+  }
+  PageCursor ic = c;  // issue cursor, runs ahead of c
+  const int n = static_cast<int>(p_end - p_begin);
+  uint8_t* ring = smem + warp * (dec_stages<D>() * stage_bytes);
+
+  // Block-table entries of the issue cursor's row, 32 pages per fetch.
+  int tab_r = -1, tab_q0 = 0, tab_val = -1;
   auto issue = [&](int i) {
-    uint8_t* kd = ring + (i % kWarpStages) * 2 * kPage;
-    const int bid = table[kb0 + i];
+    uint8_t* kd = ring + (i % dec_stages<D>()) * stage_bytes;
+    if (ic.r != tab_r || ic.q < tab_q0 || ic.q >= tab_q0 + 32) {
+      tab_r = ic.r;
+      tab_q0 = ic.q;
+      const int qq = ic.q + lane;
+      tab_val = qq < ic.pages && qq < a.max_blocks
+                    ? __ldg(a.block_tables + static_cast<size_t>(ic.r) * a.max_blocks + qq)
+                    : -1;
+    }
+    const int bid = __shfl_sync(0xffffffffu, tab_val, ic.q - tab_q0);
+    if (i == 0 || ic.q == 0) {
+      // First page of a stream: its query heads ride along.
+      const __half* qs =
+          a.q + static_cast<size_t>(ic.t) * a.hq * D + static_cast<size_t>(ic.kvh) * G * D;
+      const uint32_t qd = smem_u32(kd + 2 * kPage);
+      for (int ch = lane; ch < G * D / 8; ch += 32) cp_async16(qd + ch * 16, qs + ch * 8);
+    }
+    const int kvh = ic.kvh;
+    cursor_next(a, ic);
     if (bid < 0) {
       if (lane == 0) atomicOr(a.status, kDevBadIndex);
       return;
     }
-    const size_t page = (static_cast<size_t>(bid) * a.hkv + kvh) * 16 * D;
+    const size_t page = (static_cast<size_t>(bid) * hkv + kvh) * 16 * D;
     const __half* ks = a.k_cache + page;
     const __half* vs = a.v_cache + page;
     const uint32_t kb = smem_u32(kd), vb = kb + kPage;
     constexpr int kChunks = 16 * D / 8;  // 16-byte chunks per page
 #pragma unroll
-    for (int c = lane; c < kChunks; c += 32) {
-      const int row = c / (D / 8), ch = c % (D / 8);
+    for (int ch16 = lane; ch16 < kChunks; ch16 += 32) {
+      const int row = ch16 / (D / 8), ch = ch16 % (D / 8);
       cp_async16(kb + page_off<D>(row, ch), ks + row * D + ch * 8);
       cp_async16(vb + page_off<D>(row, ch), vs + row * D + ch * 8);
     }
   };
 
-  // Q as A fragments (rows = heads of the group; rows >= G are zero).
   const int g = lane >> 2;
-  uint32_t qa[D / 16][2];
-  {
-    const __half* qrow = a.q + static_cast<size_t>(t) * a.hq * d + static_cast<size_t>(kvh * G + g) * d;
-#pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      const int col = kk * 16 + (lane & 3) * 2;
-      qa[kk][0] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + col) : 0u;
-      qa[kk][1] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + col + 8) : 0u;
-    }
-  }
   const float sl2 = a.scale * kLog2e;
+  uint32_t qa[D / 16][2];
   float o[D / 8][4];
-#pragma unroll
-  for (int i = 0; i < D / 8; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[i][e] = 0.f;
   float m = -INFINITY, l = 0.f;
 
 #pragma unroll
-  for (int i = 0; i < kWarpStages - 1; ++i) {
-    if (i < npage) issue(i);
+  for (int i = 0; i < dec_stages<D>() - 1; ++i) {
+    if (i < n) issue(i);
     cp_async_commit();
   }
-  for (int i = 0; i < npage; ++i) {
-    if (i + kWarpStages - 1 < npage) issue(i + kWarpStages - 1);
+  for (int i = 0; i < n; ++i) {
+    if (i + dec_stages<D>() - 1 < n) issue(i + dec_stages<D>() - 1);
     cp_async_commit();
-    cp_async_wait<kWarpStages - 1>();
+    cp_async_wait<dec_stages<D>() - 1>();
     __syncwarp();
-    const uint32_t kb = smem_u32(ring + (i % kWarpStages) * 2 * kPage), vb = kb + kPage;
+    const uint8_t* stage = ring + (i % dec_stages<D>()) * stage_bytes;
+    if (i == 0 || c.q == 0) {
+      // A new stream: its query heads as A fragments, fresh softmax state.
+      const uint8_t* qrow = stage + 2 * kPage + g * D * 2;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int col = kk * 16 + (lane & 3) * 2;
+        qa[kk][0] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + col * 2) : 0u;
+        qa[kk][1] = g < G ? *reinterpret_cast<const uint32_t*>(qrow + (col + 8) * 2) : 0u;
+      }
+#pragma unroll
+      for (int db = 0; db < D / 8; ++db)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[db][e] = 0.f;
+      m = -INFINITY;
+      l = 0.f;
+    }
+    const uint32_t kb = smem_u32(stage), vb = kb + kPage;
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
@@ -335,14 +560,14 @@ __global__ void __launch_bounds__(128)
       mma16816(s[0], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
       mma16816(s[1], qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
     }
-    const int base = (kb0 + i) * 16;
+    const int base = c.q * 16;
     float mx = m;
 #pragma unroll
     for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int key = base + nb * 8 + (lane & 3) * 2 + e;
-        const float v = (key >= key0 && key < key1) ? s[nb][e] * sl2 : -INFINITY;
+        const float v = key < c.ctx ? s[nb][e] * sl2 : -INFINITY;
         s[nb][e] = v;
         mx = fmaxf(mx, v);
       }
@@ -367,79 +592,55 @@ __global__ void __launch_bounds__(128)
       mma16816(o[db], pa0, 0u, pa2, 0u, b0, b1);
       mma16816(o[db + 1], pa0, 0u, pa2, 0u, b2, b3);
     }
-    __syncwarp();
+    __syncwarp();  // every lane is done with this stage before it is refilled
+    if (c.q == c.pages - 1 || i == n - 1) {
+      // This warp's piece of the stream (c.r, c.kvh) is complete.
+      float lt = l;
+      lt += __shfl_xor_sync(0xffffffffu, lt, 1);
+      lt += __shfl_xor_sync(0xffffffffu, lt, 2);
+      const long long f0 = c.cum * hkv + static_cast<long long>(c.kvh) * c.pages;
+      const int w0 = static_cast<int>(((f0 + 1) * W - 1) / total);
+      const int w1 = static_cast<int>(((f0 + c.pages) * W - 1) / total);
+      __half* out = a.out + static_cast<size_t>(c.t) * a.ld_out + static_cast<size_t>(c.kvh) * G * D;
+      if (w0 == w1) {  // the whole stream in this warp: normalise and store
+        if (g < G) {
+          const float inv = 1.0f / lt;
+#pragma unroll
+          for (int db = 0; db < D / 8; ++db)
+            *reinterpret_cast<__half2*>(out + g * D + db * 8 + (lane & 3) * 2) =
+                __floats2half2_rn(o[db][0] * inv, o[db][1] * inv);
+        }
+      } else {
+        const int stream = c.r * hkv + c.kvh;
+        if (g < G) {
+          const size_t piece = static_cast<size_t>(stream + w) * G + g;
+          float* dst = a.part_o + piece * D;
+#pragma unroll
+          for (int db = 0; db < D / 8; ++db)
+            *reinterpret_cast<float2*>(dst + db * 8 + (lane & 3) * 2) =
+                make_float2(o[db][0], o[db][1]);
+          if ((lane & 3) == 0)
+            *reinterpret_cast<float2*>(a.part_ml + piece * 2) =
+                make_float2(m * 0.6931471805599453f, lt);  // natural-log domain
+        }
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          int* counter = a.counters + stream;
+          last = atomicAdd(counter, 1) == w1 - w0;
+          if (last) *counter = 0;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          decode_merge<D>(a, static_cast<size_t>(stream + w0) * G, w1 - w0 + 1, G, out, lane);
+        }
+      }
+    }
+    cursor_next(a, c);
   }
   cp_async_wait<0>();
-  l += __shfl_xor_sync(0xffffffffu, l, 1);
-  l += __shfl_xor_sync(0xffffffffu, l, 2);
-  const int s0 = a.cu_splits[r];
-  const int ns = a.cu_splits[r + 1] - s0;
-  if (ns == 1) {  // the whole context in one split: normalise and store
-    if (g < G) {
-      const float inv = 1.0f / l;
-      __half* dst = a.out + static_cast<size_t>(t) * a.ld_out + static_cast<size_t>(kvh * G + g) * d;
-#pragma unroll
-      for (int db = 0; db < D / 8; ++db)
-        *reinterpret_cast<__half2*>(dst + db * 8 + (lane & 3) * 2) =
-            __floats2half2_rn(o[db][0] * inv, o[db][1] * inv);
-    }
-    return;
-  }
-  if (g < G) {
-    const int h = kvh * G + g;
-    float* dst = a.part_o + (static_cast<size_t>(split) * a.hq + h) * d;
-#pragma unroll
-    for (int db = 0; db < D / 8; ++db)
-      *reinterpret_cast<float2*>(dst + db * 8 + (lane & 3) * 2) = make_float2(o[db][0], o[db][1]);
-    if ((lane & 3) == 0) {
-      float* ml = a.part_ml + (static_cast<size_t>(split) * a.hq + h) * 2;
-      ml[0] = m * 0.6931471805599453f;  // natural-log domain
-      ml[1] = l;
-    }
-  }
-  // The last warp to finish a (row, kv head) merges its splits in split order;
-  // no warp waits for another.
-  __threadfence();
-  __syncwarp();
-  int last = 0;
-  if (lane == 0) {
-    int* counter = a.counters + static_cast<size_t>(r) * a.hkv + kvh;
-    last = atomicAdd(counter, 1) == ns - 1;
-    if (last) *counter = 0;
-  }
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (!last) return;
-  __threadfence();
-  for (int gg = 0; gg < G; ++gg) {
-    const int h = kvh * G + gg;
-    const float* ml = a.part_ml + (static_cast<size_t>(s0) * a.hq + h) * 2;
-    float mm = -INFINITY;
-    for (int s = lane; s < ns; s += 32) mm = fmaxf(mm, __ldcg(ml + static_cast<size_t>(s) * a.hq * 2));
-    mm = warp_max(mm);
-    float ll = 0.f;
-    for (int s = lane; s < ns; s += 32) {
-      const float* e = ml + static_cast<size_t>(s) * a.hq * 2;
-      ll += __ldcg(e + 1) * expf(__ldcg(e) - mm);
-    }
-    ll = warp_sum(ll);
-    const float inv = 1.0f / ll;
-    const float* po = a.part_o + (static_cast<size_t>(s0) * a.hq + h) * d;
-    for (int i = lane * 4; i < D; i += 128) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-      for (int s = 0; s < ns; ++s) {
-        const float w = expf(__ldcg(ml + static_cast<size_t>(s) * a.hq * 2) - mm);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(po + static_cast<size_t>(s) * a.hq * d + i));
-        acc.x += v.x * w;
-        acc.y += v.y * w;
-        acc.z += v.z * w;
-        acc.w += v.w * w;
-      }
-      __half* dst = a.out + static_cast<size_t>(t) * a.ld_out + static_cast<size_t>(h) * d + i;
-      *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(acc.x * inv, acc.y * inv);
-      *reinterpret_cast<__half2*>(dst + 2) = __floats2half2_rn(acc.z * inv, acc.w * inv);
-    }
-  }
 }
 
 // One CTA per (decode row, query head): merge the row's splits.
@@ -728,24 +929,62 @@ cudaError_t launch_prefill(const AttnArgs& a, int total_qtiles, cudaStream_t str
 }
 
 template <int D>
-cudaError_t launch_decode_mma(const AttnArgs& a, int total_splits, cudaStream_t stream) {
-  constexpr size_t kSmem = 4 * kWarpStages * 2 * (16 * D * 2);
+size_t decode_mma_smem(int group) {
+  return static_cast<size_t>(4) * dec_stages<D>() * decode_stage_bytes(D, group);
+}
+
+// Sets the kernel's shared-memory limit once and returns its resident CTAs per
+// SM for a GQA group size (1..kMaxGroup), 0 on failure.
+template <int D>
+int decode_mma_setup(int group) {
   static bool configured = false;
+  static int per_sm[kMaxGroup + 1] = {};
+  if (group < 1 || group > kMaxGroup) return 0;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_attn_mma_kernel<D>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmem));
-    if (e != cudaSuccess) return e;
+    if (cudaFuncSetAttribute(decode_attn_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(decode_mma_smem<D>(kMaxGroup))) != cudaSuccess)
+      return 0;
     configured = true;
   }
-  const int items = total_splits * a.hkv;
-  decode_attn_mma_kernel<D><<<(items + 3) / 4, 128, kSmem, stream>>>(a, items);
+  if (per_sm[group] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_attn_mma_kernel<D>, 128,
+                                                      decode_mma_smem<D>(group)) != cudaSuccess)
+      return 0;
+    per_sm[group] = n > 0 ? n : 1;
+  }
+  return per_sm[group];
+}
+
+template <int D>
+cudaError_t launch_decode_mma(const AttnArgs& a, cudaStream_t stream) {
+  const int group = a.hq / a.hkv;
+  if (a.decode_ctas <= 0 || decode_mma_setup<D>(group) == 0) return cudaErrorInvalidValue;
+  decode_attn_mma_kernel<D><<<a.decode_ctas, 128, decode_mma_smem<D>(group), stream>>>(a);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 int attn_qtile_tokens(int group) { return 64 / group; }
+
+bool attn_decode_balanced(int dim) { return dim == 64 || dim == 128 || dim == 256; }
+
+int attn_decode_ctas(int dim, int group, long long pages, int sm_count) {
+  if (!attn_decode_balanced(dim) || pages <= 0) return 0;
+  const int per_sm = dim == 64 ? decode_mma_setup<64>(group)
+                     : dim == 128 ? decode_mma_setup<128>(group)
+                                  : decode_mma_setup<256>(group);
+  if (per_sm == 0) return 0;
+  // One wave of resident CTAs, but at least ~8 pages per warp.
+  const long long want = (pages + 31) / 32;
+  return static_cast<int>(std::max<long long>(1, std::min<long long>(want, 1LL * per_sm * sm_count)));
+}
+
+size_t attn_decode_part_floats(int rows, int hq, int hkv, int dim, int ctas) {
+  const size_t pieces = static_cast<size_t>(rows) * hkv + 4 * static_cast<size_t>(ctas);
+  return pieces * static_cast<size_t>(hq / hkv) * static_cast<size_t>(dim + 2);
+}
 
 cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t stream) {
   if (total_splits <= 0) return cudaSuccess;
@@ -754,10 +993,10 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t
       a.split_tokens % 16 != 0)
     return cudaErrorInvalidValue;
   cudaError_t e;
-  if (a.dim == 64 || a.dim == 128 || a.dim == 256) {
-    e = a.dim == 64    ? launch_decode_mma<64>(a, total_splits, stream)
-        : a.dim == 128 ? launch_decode_mma<128>(a, total_splits, stream)
-                       : launch_decode_mma<256>(a, total_splits, stream);
+  if (attn_decode_balanced(a.dim)) {
+    e = a.dim == 64    ? launch_decode_mma<64>(a, stream)
+        : a.dim == 128 ? launch_decode_mma<128>(a, stream)
+                       : launch_decode_mma<256>(a, stream);
   } else {
     // Other head sizes (e.g. the tiny fixtures): one CTA per (kv head, split).
     const size_t smem = kDecStages * 2 * 16 * a.dim * 2 +
@@ -779,7 +1018,7 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t
   return e;
 }
 
-int attn_decode_launches(int dim) { return (dim == 64 || dim == 128 || dim == 256) ? 1 : 2; }
+int attn_decode_launches(int dim) { return attn_decode_balanced(dim) ? 1 : 2; }
 
 cudaError_t attn_prefill_launch(const AttnArgs& a, int total_qtiles, cudaStream_t stream) {
   if (total_qtiles <= 0) return cudaSuccess;

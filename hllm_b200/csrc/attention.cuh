@@ -22,8 +22,10 @@ struct AttnArgs {
   int split_tokens;            // keys per decode split (multiple of 16)
   int qtile_tokens;            // query tokens per prefill tile
   float scale;                 // 1/sqrt(d)
-  float* part_o;               // [splits][Hq][d]  unnormalised split outputs
-  float* part_ml;              // [splits][Hq][2]  running max, denominator
+  int decode_ctas;             // balanced decode grid (attn_decode_ctas), head sizes 64/128/256
+  float* part_o;               // partial outputs: [splits][Hq][d] (combine path) or
+                               // [pieces][Hq/Hkv][d] (balanced path)
+  float* part_ml;              // matching running max, denominator pairs
   int* counters;               // [rows][Hkv] zero-initialised; returned to zero after use
   __half* out;                 // [T][ld_out]
   int ld_out;
@@ -33,11 +35,21 @@ struct AttnArgs {
 // Query tokens per prefill tile for a GQA group size (64 query rows per CTA).
 int attn_qtile_tokens(int group);
 
-// Decode rows (one new token): split-K over the context; the splits of a row
-// are merged by the last warp to finish (head sizes 64/128/256) or by a
-// combine pass (other head sizes).
+// Decode rows (one new token).  Head sizes 64/128/256: the decode rows' KV
+// pages are split evenly over 4 * decode_ctas warps regardless of row
+// lengths, and the pieces of a (row, kv head) are merged by its last warp to
+// finish (split_tokens/cu_splits unused).  Other head sizes: split-K over
+// split_tokens-key splits, one CTA per (kv head, split), then a combine pass.
 cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t stream);
 int attn_decode_launches(int dim);
+bool attn_decode_balanced(int dim);
+// CTAs of the balanced decode pass (GQA group size `group` = Hq/Hkv) for
+// `pages` = sum over decode rows of
+// ceil(ctx / 16) x Hkv: one wave of resident CTAs at most, about 8 pages per
+// warp at least; 0 when the head size takes the combine path.
+int attn_decode_ctas(int dim, int group, long long pages, int sm_count);
+// Floats of part_o + part_ml that the balanced pass needs for `rows` rows.
+size_t attn_decode_part_floats(int rows, int hq, int hkv, int dim, int ctas);
 // Prefill rows (several new tokens): causal tiles on the tensor cores.
 cudaError_t attn_prefill_launch(const AttnArgs& a, int total_qtiles, cudaStream_t stream);
 

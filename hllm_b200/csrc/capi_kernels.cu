@@ -4,6 +4,7 @@
 // executor launches.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -183,10 +184,22 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
     constexpr size_t kCounters = 1 << 16;
     if (static_cast<size_t>(rows) * hkv > kCounters) return HLLM_B200_INVALID_REQUEST;
     const size_t counter_off = 0;
-    const size_t need = kCounters + static_cast<size_t>(total_splits) * hq * (dim + 2);
-    int dev = 0;
+    int dev = 0, sm_count = 0;
     cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return cuda_status(e);
+    // The balanced pass (head sizes 64/128/256) sizes its grid from the pages
+    // the splits cover (an upper bound of the decode rows' pages).
+    const long long pages = static_cast<long long>(total_splits) *
+                            ((split_tokens + 15) / 16) * static_cast<long long>(hkv);
+    a.decode_ctas = hb::attn_decode_ctas(static_cast<int>(dim), static_cast<int>(hq / hkv), pages,
+                                         sm_count);
+    const size_t part_floats =
+        std::max(static_cast<size_t>(total_splits) * hq * (dim + 2),
+                 hb::attn_decode_part_floats(static_cast<int>(rows), static_cast<int>(hq),
+                                             static_cast<int>(hkv), static_cast<int>(dim),
+                                             a.decode_ctas));
+    const size_t need = kCounters + part_floats;
     float* base = nullptr;
     {
       std::scoped_lock lock(mu);
@@ -206,7 +219,8 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
     }
     a.counters = reinterpret_cast<int*>(base + counter_off);
     a.part_o = base + kCounters;
-    a.part_ml = a.part_o + static_cast<size_t>(total_splits) * hq * dim;
+    // part_ml after the larger of the two layouts' part_o extents.
+    a.part_ml = a.part_o + part_floats / (dim + 2) * dim;
     e = hb::attn_decode_launch(a, static_cast<int>(total_splits), st);
     if (e != cudaSuccess) return cuda_status(e);
   }

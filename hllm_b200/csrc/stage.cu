@@ -494,8 +494,16 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
     s->logits = s->alloc<float>(R * s->V);
     s->sample_scratch = s->alloc<double>(R * s->V);
   }
-  s->part_o = s->alloc<float>(s->max_splits * s->hq * s->dim);
-  s->part_ml = s->alloc<float>(s->max_splits * s->hq * 2);
+  {
+    // Partial decode outputs: split-K splits (combine path) or the balanced
+    // pass's pieces, whichever needs more.
+    const int max_ctas = hb::attn_decode_ctas(static_cast<int>(s->dim), static_cast<int>(s->hq / s->hkv),
+                                              1LL << 40, s->sm_count);
+    const size_t pieces = R * s->hkv + 4 * static_cast<size_t>(max_ctas);
+    const size_t group = s->hq / s->hkv;
+    s->part_o = s->alloc<float>(std::max(s->max_splits * s->hq, pieces * group) * s->dim);
+    s->part_ml = s->alloc<float>(std::max(s->max_splits * s->hq, pieces * group) * 2);
+  }
   s->attn_counters = s->alloc<int>(R * s->hkv);
   s->slots = s->alloc<float>(hb::gemm_max_slot_floats(s->sm_count));
   s->segmap = s->alloc<int>(hb::kGemmMapInts);
@@ -606,6 +614,7 @@ struct StepPlan {
   int total_splits = 0;
   int total_qtiles = 0;
   int qtile_tokens = 0;
+  int decode_ctas = 0;     // balanced decode attention grid
   double attn_dec_bytes = 0, attn_dec_flops = 0;  // algorithmic, per layer
   double attn_pre_bytes = 0, attn_pre_flops = 0;
 };
@@ -624,7 +633,7 @@ StepPlan plan_step(hllm_b200_stage* s, const hllm_b200_row* rows, uint32_t n, bo
   StepPlan p;
   p.rows = n;
   std::set<const hllm_b200_seq*> seen;
-  uint64_t decode_keys = 0;
+  uint64_t decode_keys = 0, decode_pages = 0;
   int decode_rows = 0;
   for (uint32_t i = 0; i < n; ++i) {
     const auto& r = rows[i];
@@ -652,6 +661,7 @@ StepPlan plan_step(hllm_b200_stage* s, const hllm_b200_row* rows, uint32_t n, bo
     p.tokens += r.tokens;
     if (r.tokens == 1) {
       decode_keys += r.first_position + 1;
+      decode_pages += (r.first_position + 1 + hb::kBlockTokens - 1) / hb::kBlockTokens;
       ++decode_rows;
     }
   }
@@ -670,6 +680,8 @@ StepPlan plan_step(hllm_b200_stage* s, const hllm_b200_row* rows, uint32_t n, bo
   while (count_splits(split) > s->max_splits) split *= 2;
   p.split_tokens = static_cast<int>(std::min<uint64_t>(split, 1u << 30));
   p.total_splits = static_cast<int>(count_splits(split));
+  p.decode_ctas = hb::attn_decode_ctas(static_cast<int>(s->dim), static_cast<int>(s->hq / s->hkv),
+                                       static_cast<long long>(decode_pages * s->hkv), s->sm_count);
   p.qtile_tokens = hb::attn_qtile_tokens(static_cast<int>(s->hq / s->hkv));
   for (uint32_t i = 0; i < n; ++i)
     if (rows[i].tokens > 1)
@@ -860,6 +872,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     aa.max_blocks = static_cast<int>(s->max_blocks);
     aa.split_tokens = p.split_tokens;
     aa.qtile_tokens = p.qtile_tokens;
+    aa.decode_ctas = p.decode_ctas;
     aa.scale = 1.0f / std::sqrt(static_cast<float>(s->dim));
     aa.part_o = s->part_o;
     aa.part_ml = s->part_ml;
