@@ -82,6 +82,7 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 __global__ void __launch_bounds__(kDecThreads)
     decode_attn_kernel(const AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  griddep_enter();
   const int d = a.dim;
   const int G = a.hq / a.hkv;
   const int kvh = blockIdx.x;
@@ -478,8 +479,18 @@ __global__ void __launch_bounds__(128)
   const int n = static_cast<int>(p_end - p_begin);
   uint8_t* ring = smem + warp * (dec_stages<D>() * stage_bytes);
 
-  // Block-table entries of the issue cursor's row, 32 pages per fetch.
-  int tab_r = -1, tab_q0 = 0, tab_val = -1;
+  // Block-table entries of the issue cursor's row, 32 pages per fetch.  The
+  // first fetch, like everything above, reads only the packer's tables, so it
+  // runs before the wait for the previous kernel (which writes q and the
+  // current token's K/V).
+  int tab_r = ic.r, tab_q0 = ic.q, tab_val = -1;
+  {
+    const int qq = ic.q + lane;
+    tab_val = qq < ic.pages && qq < a.max_blocks
+                  ? __ldg(a.block_tables + static_cast<size_t>(ic.r) * a.max_blocks + qq)
+                  : -1;
+  }
+  griddep_enter();
   auto issue = [&](int i) {
     uint8_t* kd = ring + (i % dec_stages<D>()) * stage_bytes;
     if (ic.r != tab_r || ic.q < tab_q0 || ic.q >= tab_q0 + 32) {
@@ -645,6 +656,7 @@ __global__ void __launch_bounds__(128)
 
 // One CTA per (decode row, query head): merge the row's splits.
 __global__ void decode_combine_kernel(const AttnArgs a) {
+  griddep_enter();
   const int r = blockIdx.x, h = blockIdx.y;
   if (a.row_count[r] != 1) return;
   const int s0 = a.cu_splits[r], ns = a.cu_splits[r + 1] - s0;
@@ -738,6 +750,7 @@ __global__ void __launch_bounds__(128)
     prefill_attn_kernel(const AttnArgs a) {
   using S = PrefillShape<DP, KT>;
   extern __shared__ __align__(128) uint8_t smem[];
+  griddep_enter();
   uint8_t* qs = smem;
   uint8_t* ks[2] = {smem + S::kQBytes, smem + S::kQBytes + S::kKvBytes};
   uint8_t* vs[2] = {smem + S::kQBytes + 2 * S::kKvBytes, smem + S::kQBytes + 3 * S::kKvBytes};
@@ -924,8 +937,8 @@ cudaError_t launch_prefill(const AttnArgs& a, int total_qtiles, cudaStream_t str
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  prefill_attn_kernel<DP, KT><<<dim3(a.hkv, total_qtiles), 128, S::kSmem, stream>>>(a);
-  return cudaGetLastError();
+  return launch_dependent(prefill_attn_kernel<DP, KT>, dim3(a.hkv, total_qtiles), dim3(128),
+                          S::kSmem, stream, a);
 }
 
 template <int D>
@@ -960,8 +973,8 @@ template <int D>
 cudaError_t launch_decode_mma(const AttnArgs& a, cudaStream_t stream) {
   const int group = a.hq / a.hkv;
   if (a.decode_ctas <= 0 || decode_mma_setup<D>(group) == 0) return cudaErrorInvalidValue;
-  decode_attn_mma_kernel<D><<<a.decode_ctas, 128, decode_mma_smem<D>(group), stream>>>(a);
-  return cudaGetLastError();
+  return launch_dependent(decode_attn_mma_kernel<D>, dim3(a.decode_ctas), dim3(128),
+                          decode_mma_smem<D>(group), stream, a);
 }
 
 }  // namespace
@@ -1009,11 +1022,10 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t
       if (e != cudaSuccess) return e;
       configured = true;
     }
-    decode_attn_kernel<<<dim3(a.hkv, total_splits), kDecThreads, smem, stream>>>(a);
-    e = cudaGetLastError();
+    e = launch_dependent(decode_attn_kernel, dim3(a.hkv, total_splits), dim3(kDecThreads), smem,
+                         stream, a);
     if (e != cudaSuccess) return e;
-    decode_combine_kernel<<<dim3(a.rows, a.hq), 128, 0, stream>>>(a);
-    e = cudaGetLastError();
+    e = launch_dependent(decode_combine_kernel, dim3(a.rows, a.hq), dim3(128), 0, stream, a);
   }
   return e;
 }

@@ -37,6 +37,49 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Step kernels after the packer are launched with programmatic stream
+// serialisation: a kernel may start while its predecessor in the stream still
+// runs.  Each kernel
+//   1. does only work that touches data fixed since the packer finished
+//      (weights, packed batch tables) and its own shared memory,
+//   2. calls griddep_wait(), which returns once the predecessor grid has
+//      completed and its writes are visible,
+//   3. calls griddep_launch_dependents(), letting the next kernel's CTAs be
+//      scheduled (so at most one kernel waits behind the running one),
+// then reads its inputs.  The packer launches without the attribute and never
+// triggers, so every later kernel starts after it completed.  Without the
+// attribute both instructions are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_enter() {
+  griddep_wait();
+  griddep_launch_dependents();
+}
+
+// Whether launches use programmatic stream serialisation (on unless the
+// environment sets HLLM_B200_PDL=0).
+bool pdl_enabled();
+
+// Launches `kernel` on `stream` with programmatic stream serialisation.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)

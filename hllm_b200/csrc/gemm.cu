@@ -159,6 +159,26 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
+      auto load_weights = [&](uint8_t* st, uint64_t* bar, int kb, int m_tile) {
+        tma_load_2d_hint(st, &map_a, bar, kb * kGemmBlockK, m_tile * kGemmBlockM, pol_w);
+        if (NA == 2)
+          tma_load_2d_hint(st + S::kABytes, &map_a, bar, kb * kGemmBlockK,
+                           p.second_row + m_tile * kGemmBlockM, pol_w);
+      };
+      // The weight tiles of the first STAGES K blocks go out before the wait
+      // for the previous kernel: weights are fixed, only the token tiles are
+      // that kernel's output.  (First use of each stage: no empty-wait.)
+      uint32_t pre = 0;
+      {
+        long long cursor = ub;
+        Segment sg;
+        for (int j = 0; pre < STAGES && next_segment(p, cursor, ue, j, sg); ++j)
+          for (int kb = sg.kb0; kb < sg.kb1 && pre < STAGES; ++kb, ++pre) {
+            mbar_arrive_expect_tx(&full[pre], S::kStageBytes);
+            load_weights(smem + pre * S::kStageBytes, &full[pre], kb, sg.tile / p.n_tiles);
+          }
+      }
+      griddep_enter();
       uint32_t it = 0;
       long long cursor = ub;
       Segment sg;
@@ -167,13 +187,12 @@ __global__ void __launch_bounds__(192, 1)
         for (int kb = sg.kb0; kb < sg.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
-          if (!mbar_wait(&empty[s], ph ^ 1u, p.status)) goto producer_done;
-          mbar_arrive_expect_tx(&full[s], S::kStageBytes);
           uint8_t* st = smem + s * S::kStageBytes;
-          tma_load_2d_hint(st, &map_a, &full[s], kb * kGemmBlockK, m_tile * kGemmBlockM, pol_w);
-          if (NA == 2)
-            tma_load_2d_hint(st + S::kABytes, &map_a, &full[s], kb * kGemmBlockK,
-                             p.second_row + m_tile * kGemmBlockM, pol_w);
+          if (it >= pre) {
+            if (!mbar_wait(&empty[s], ph ^ 1u, p.status)) goto producer_done;
+            mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+            load_weights(st, &full[s], kb, m_tile);
+          }
           tma_load_2d_hint(st + NA * S::kABytes, &map_b, &full[s], kb * kGemmBlockK,
                            n_tile * BN, pol_x);
         }
@@ -214,6 +233,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // Epilogue: thread t owns TMEM lane t = output feature m_tile*128 + t.
+    griddep_enter();  // it reads (residual) and writes buffers of earlier kernels
     const int t = threadIdx.x;
     long long cursor = ub;
     const int first_tile = static_cast<int>(ub / (p.kb_count > 0 ? p.kb_count : 1));
@@ -275,6 +295,7 @@ __global__ void __launch_bounds__(192, 1)
 
 // ---------------------------------------------------------------- generic consumer
 __global__ void gemm_finish_kernel(const GemmSlots s, int rows, int epilogue, void* out, int ldo) {
+  griddep_enter();
   const int n = blockIdx.y;
   if (n >= rows) return;
   for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < s.m; m += gridDim.x * blockDim.x) {
@@ -332,8 +353,8 @@ cudaError_t launch(const GemmWeight& w, const GemmInput& x, int bn_index, const 
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  gemm_tc_kernel<BN, NA><<<grid, 192, S::kSmemBytes, stream>>>(w.map, x.maps[bn_index], p);
-  return cudaGetLastError();
+  return launch_dependent(gemm_tc_kernel<BN, NA>, dim3(grid), dim3(192), S::kSmemBytes, stream,
+                          w.map, x.maps[bn_index], p);
 }
 
 }  // namespace
@@ -458,8 +479,8 @@ cudaError_t gemm_finish_launch(const GemmSlots& s, int rows, int epilogue, void*
                                cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const dim3 grid(static_cast<unsigned>((s.m + 255) / 256), static_cast<unsigned>(rows));
-  gemm_finish_kernel<<<grid, 256, 0, stream>>>(s, rows, epilogue, out, ldo);
-  return cudaGetLastError();
+  return launch_dependent(gemm_finish_kernel, grid, dim3(256), 0, stream, s, rows, epilogue, out,
+                          ldo);
 }
 
 }  // namespace hb

@@ -1,5 +1,7 @@
 // kernels.cu -- packer, embedding, norms, q/k-norm + RoPE + paged-KV write,
 // boundary conversion and synthetic initialisation for the stage executor.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -66,6 +68,7 @@ __global__ void pack_kernel(StepTensors s, const int32_t* __restrict__ slot_bloc
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const __half* __restrict__ emb,
                              int vocab, int hidden, int ld, float* __restrict__ out,
                              uint32_t* status) {
+  griddep_enter();
   const int t = blockIdx.x;
   const int id = ids[t];
   if (id < 0 || id >= vocab) {
@@ -79,6 +82,7 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const __half* __re
 
 __global__ void boundary_in_kernel(const __half* __restrict__ in, size_t n,
                                    float* __restrict__ out, uint32_t* status) {
+  griddep_enter();
   bool bad = false;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -91,6 +95,7 @@ __global__ void boundary_in_kernel(const __half* __restrict__ in, size_t n,
 
 __global__ void boundary_out_kernel(const float* __restrict__ in, size_t n,
                                     __half* __restrict__ out, uint32_t* status) {
+  griddep_enter();
   bool bad = false;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -106,6 +111,7 @@ __global__ void boundary_out_kernel(const float* __restrict__ in, size_t n,
 __global__ void rmsnorm_kernel(const float* __restrict__ x, int width,
                                const float* __restrict__ w, float eps, __half* __restrict__ out,
                                int ld_out, const int32_t* __restrict__ row_index) {
+  griddep_enter();
   const int r = blockIdx.x;
   const int src = row_index ? row_index[r] : r;
   const float* xr = x + static_cast<size_t>(src) * width;
@@ -137,6 +143,7 @@ constexpr int kMaxHeadDim = 256;
 
 __global__ void __launch_bounds__(kQkvWarps * 32)
     qkv_post_kernel(QkvPostArgs a) {
+  griddep_enter();
   __shared__ __align__(16) float buf[kQkvWarps][kMaxHeadDim];
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -208,6 +215,7 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
 __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, GemmSlots slots,
                                      int has_slots, const float* __restrict__ w, float eps,
                                      __half* __restrict__ out, int ld_out) {
+  griddep_enter();
   const int t = blockIdx.x;
   float* xr = hidden + static_cast<size_t>(t) * width;
   float ss = 0.f;
@@ -253,6 +261,7 @@ __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, Gemm
 
 // cpp/src/cpu/llama.cpp:274-280: (g / (1 + exp(-g))) * u.
 __global__ void swiglu_kernel(GemmSlots slots, __half* __restrict__ act, int ld_act) {
+  griddep_enter();
   const int t = blockIdx.y;
   __half* out = act + static_cast<size_t>(t) * ld_act;
   if ((slots.m & 3) == 0) {
@@ -275,6 +284,7 @@ __global__ void swiglu_kernel(GemmSlots slots, __half* __restrict__ act, int ld_
 }
 
 __global__ void last_token_kernel(const int32_t* cu, const int32_t* rows, int count, int32_t* idx) {
+  griddep_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < count) idx[i] = cu[rows[i] + 1] - 1;
 }
@@ -319,6 +329,14 @@ int grid_for(size_t n, int threads) {
 
 }  // namespace
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("HLLM_B200_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 cudaError_t pack_launch(const StepTensors& s, const int32_t* slot_blocks, uint32_t* status,
                         cudaStream_t stream) {
   if (s.rows <= 0) return cudaErrorInvalidValue;
@@ -329,23 +347,22 @@ cudaError_t pack_launch(const StepTensors& s, const int32_t* slot_blocks, uint32
 cudaError_t embed_launch(const int32_t* ids, int tokens, const __half* embedding, int vocab,
                          int hidden, int ld_embedding, float* out, uint32_t* status,
                          cudaStream_t stream) {
-  embed_kernel<<<tokens, 256, 0, stream>>>(ids, embedding, vocab, hidden, ld_embedding, out,
-                                           status);
-  return cudaGetLastError();
+  return launch_dependent(embed_kernel, dim3(tokens), dim3(256), 0, stream, ids, embedding, vocab,
+                          hidden, ld_embedding, out, status);
 }
 
 cudaError_t boundary_in_launch(const __half* in, int tokens, int hidden, float* out,
                                uint32_t* status, cudaStream_t stream) {
   const size_t n = static_cast<size_t>(tokens) * hidden;
-  boundary_in_kernel<<<grid_for(n, 256), 256, 0, stream>>>(in, n, out, status);
-  return cudaGetLastError();
+  return launch_dependent(boundary_in_kernel, dim3(grid_for(n, 256)), dim3(256), 0, stream, in, n,
+                          out, status);
 }
 
 cudaError_t boundary_out_launch(const float* hidden, int tokens, int width, __half* out,
                                 uint32_t* status, cudaStream_t stream) {
   const size_t n = static_cast<size_t>(tokens) * width;
-  boundary_out_kernel<<<grid_for(n, 256), 256, 0, stream>>>(hidden, n, out, status);
-  return cudaGetLastError();
+  return launch_dependent(boundary_out_kernel, dim3(grid_for(n, 256)), dim3(256), 0, stream, hidden,
+                          n, out, status);
 }
 
 cudaError_t rmsnorm_launch(const float* x, int rows, int width, const float* w, float eps,
@@ -353,8 +370,8 @@ cudaError_t rmsnorm_launch(const float* x, int rows, int width, const float* w, 
                            cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   const int threads = width >= 1024 ? 512 : (width >= 256 ? 256 : 64);
-  rmsnorm_kernel<<<rows, threads, 0, stream>>>(x, width, w, eps, out, ld_out, row_index);
-  return cudaGetLastError();
+  return launch_dependent(rmsnorm_kernel, dim3(rows), dim3(threads), 0, stream, x, width, w, eps,
+                          out, ld_out, row_index);
 }
 
 cudaError_t qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream) {
@@ -362,8 +379,7 @@ cudaError_t qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream) {
   const int heads = a.hq + 2 * a.hkv;
   const dim3 grid(static_cast<unsigned>(a.tokens),
                   static_cast<unsigned>((heads + kQkvWarps - 1) / kQkvWarps));
-  qkv_post_kernel<<<grid, kQkvWarps * 32, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_dependent(qkv_post_kernel, grid, dim3(kQkvWarps * 32), 0, stream, a);
 }
 
 cudaError_t residual_norm_launch(float* hidden, int tokens, int width, const GemmSlots* slots,
@@ -373,9 +389,8 @@ cudaError_t residual_norm_launch(float* hidden, int tokens, int width, const Gem
   GemmSlots s{};
   if (slots) s = *slots;
   const int threads = width >= 1024 ? 512 : (width >= 256 ? 256 : 64);
-  residual_norm_kernel<<<tokens, threads, 0, stream>>>(hidden, width, s, slots ? 1 : 0, norm,
-                                                       eps, out, ld_out);
-  return cudaGetLastError();
+  return launch_dependent(residual_norm_kernel, dim3(tokens), dim3(threads), 0, stream, hidden,
+                          width, s, slots ? 1 : 0, norm, eps, out, ld_out);
 }
 
 cudaError_t swiglu_launch(const GemmSlots& slots, int tokens, __half* act, int ld_act,
@@ -384,15 +399,14 @@ cudaError_t swiglu_launch(const GemmSlots& slots, int tokens, __half* act, int l
   const int per_block = (slots.m & 3) == 0 ? 1024 : 256;
   const dim3 grid(static_cast<unsigned>((slots.m + per_block - 1) / per_block),
                   static_cast<unsigned>(tokens));
-  swiglu_kernel<<<grid, 256, 0, stream>>>(slots, act, ld_act);
-  return cudaGetLastError();
+  return launch_dependent(swiglu_kernel, grid, dim3(256), 0, stream, slots, act, ld_act);
 }
 
 cudaError_t last_token_launch(const int32_t* cu_seqlens, const int32_t* sample_rows, int count,
                               int32_t* idx, cudaStream_t stream) {
   if (count <= 0) return cudaSuccess;
-  last_token_kernel<<<(count + 127) / 128, 128, 0, stream>>>(cu_seqlens, sample_rows, count, idx);
-  return cudaGetLastError();
+  return launch_dependent(last_token_kernel, dim3((count + 127) / 128), dim3(128), 0, stream,
+                          cu_seqlens, sample_rows, count, idx);
 }
 
 cudaError_t synth_matrix_launch(uint64_t seed, uint64_t tag, int rows, int cols, int ld,

@@ -168,6 +168,7 @@ __global__ void __launch_bounds__(kThreads)
     sample_kernel(const float* __restrict__ logits, int vocab, int ld,
                   const SampleParams* __restrict__ params, double* __restrict__ scratch,
                   SampleResult* __restrict__ out, uint32_t* status) {
+  griddep_enter();
   __shared__ SelectShared sel;
   __shared__ double dsh[32];
   __shared__ uint64_t ush[32];
@@ -265,8 +266,8 @@ cudaError_t sample_launch(const float* logits, int rows, int vocab, int ld,
                           const SampleParams* params, double* scratch, SampleResult* out,
                           uint32_t* status, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  sample_kernel<<<rows, kThreads, 0, stream>>>(logits, vocab, ld, params, scratch, out, status);
-  return cudaGetLastError();
+  return launch_dependent(sample_kernel, dim3(rows), dim3(kThreads), 0, stream, logits, vocab, ld,
+                          params, scratch, out, status);
 }
 
 }  // namespace hb
