@@ -26,9 +26,12 @@ Arms and numbers:
             from the reference sources; the C restatement when absent) on the
             host: each step is one decode token through one Qwen3-4B layer,
             extrapolated to the model (36 layers + LM head share).
-Multi-GPU (torchrun, N > 1): every rank runs the workload on its own GPU
-(replicas; no collective in the data path); value = all ranks' tokens / max
-time over ranks.
+Multi-GPU (torchrun, N > 1): an N-stage pipeline, one rank per GPU.  Rank r
+owns a contiguous layer range (split by streamed bytes, hllm_b200.pipeline);
+F16 boundaries go rank to rank with NCCL send/recv; N micro-batches of 64
+concurrent requests each (independent traces) keep every stage busy, so the
+global batch is 64 N (weak scaling).  A timed tick is one micro-batch step on
+every rank; value = tokens completed by the last stage / max time over ranks.
 """
 from __future__ import annotations
 
@@ -138,19 +141,41 @@ def prompt_ids(rid: int, n: int, vocab: int) -> np.ndarray:
 
 
 # ---------------------------------------------------------------------------- our arm
-def make_stage(device: int):
+def make_stage(device: int, layer_start=0, layer_end=None, first=True, final=True,
+               microbatches=1):
+    """The Qwen3-4B stage for layers [layer_start, layer_end) with KV room for
+    `microbatches` x 64 concurrent requests."""
     from hllm_b200 import B200Stage, ModelConfig
     from hllm_b200.workload import QWEN3_4B as Q
     cfg = ModelConfig(Q["hidden_size"], Q["intermediate_size"], Q["attention_heads"],
                       Q["key_value_heads"], Q["head_dimension"], Q["maximum_sequence_length"],
                       Q["rms_norm_epsilon"], Q["rope_theta"], Q["query_key_norm"],
                       Q["vocabulary_size"], Q["layers"], Q["tied"])
-    stage = B200Stage(cfg, 0, Q["layers"], first=True, final=True, device=device,
-                      kv_pool_tokens=MAX_ACTIVE * Q["maximum_sequence_length"] + 4096,
+    end = Q["layers"] if layer_end is None else layer_end
+    stage = B200Stage(cfg, layer_start, end, first=first, final=final, device=device,
+                      kv_pool_tokens=microbatches * (MAX_ACTIVE * Q["maximum_sequence_length"]
+                                                     + 4096),
                       max_step_tokens=MAX_ACTIVE + CHUNK + 64, max_step_rows=MAX_ACTIVE + 16,
-                      max_sequences=MAX_ACTIVE + 16)
+                      max_sequences=microbatches * (MAX_ACTIVE + 16))
     stage.init_synthetic(SEED)
     return stage, cfg
+
+
+KERNEL_CLASSES = ("gemm_decode", "gemm_prefill", "attn_decode", "attn_prefill", "misc", "norm",
+                  "qkv_rope", "swiglu", "sampler")
+
+
+def read_profile(stage):
+    """Per-class totals of the stage's launch profile (ms, launches, bytes, flops)."""
+    from hllm_b200 import _lib
+    L = _lib.lib()
+    prof = {}
+    for kind, name in enumerate(KERNEL_CLASSES):
+        v = [C.c_double(), C.c_uint64(), C.c_double(), C.c_double()]
+        _lib.check(L.hllm_b200_stage_profile_read(stage.handle, kind, C.byref(v[0]),
+                                                  C.byref(v[1]), C.byref(v[2]), C.byref(v[3])))
+        prof[name] = dict(ms=v[0].value, launches=v[1].value, bytes=v[2].value, flops=v[3].value)
+    return prof
 
 
 def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, clocks=None,
@@ -217,14 +242,7 @@ def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, cl
     clock_info = clocks.stop() if clocks else None
     prof = None
     if profile:
-        prof = {}
-        for kind, name in enumerate(("gemm_decode", "gemm_prefill", "attn_decode", "attn_prefill",
-                                     "misc", "norm", "qkv_rope", "swiglu", "sampler")):
-            v = [C.c_double(), C.c_uint64(), C.c_double(), C.c_double()]
-            _lib.check(L.hllm_b200_stage_profile_read(stage.handle, kind, C.byref(v[0]),
-                                                      C.byref(v[1]), C.byref(v[2]), C.byref(v[3])))
-            prof[name] = dict(ms=v[0].value, launches=v[1].value, bytes=v[2].value,
-                              flops=v[3].value)
+        prof = read_profile(stage)
         _lib.check(L.hllm_b200_stage_profile(stage.handle, 0))
     for s in seqs.values():
         stage.release(s)
@@ -323,13 +341,10 @@ def host_cores():
 
 
 def ours(args, world, rank, local):
-    import torch
     if world > 1:
-        import datetime
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        ours_pipeline(args, world, rank, local)
+        return
+    import torch
     torch.cuda.set_device(local)
     W, K, F = args.warmup, args.steps, args.fast_forward
     total_steps = F + W + K
@@ -348,30 +363,31 @@ def ours(args, world, rank, local):
         stage.close()
         return
     # e2e: the public call with host buffers and token feedback
-    import copy
     trace2, steps2 = plan_schedule(total_steps)
     e2e_ms, e2e_tokens, generated, h2d, d2h, ttft = run_host_phase(stage, cfg, trace2, steps2,
                                                                     first_timed, K)
     # profile pass (events around every launch) for the roofline
     trace3, steps3 = plan_schedule(total_steps)
     _, _, _, prof, _ = run_device_phase(stage, cfg, trace3, steps3, first_timed, K, profile=True)
-    del copy
-    times = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device="cuda")
-    toks = torch.tensor([dev_tokens, e2e_tokens], dtype=torch.float64, device="cuda")
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-        dist.all_reduce(toks, op=dist.ReduceOp.SUM)
-    dev_ms, e2e_ms = times.tolist()
-    all_dev_tokens, all_e2e_tokens = toks.tolist()
-    if rank != 0:
-        stage.close()
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-            dist.destroy_process_group()
-        return
+    stage.close()
+    cpu = None
+    if not args.no_cpu_baseline:
+        tps, t_layer, t_head, kind, _, _ = cpu_reference_sample()
+        cpu = {"value": round(tps, 5), "unit": "tokens/s", "cores": 1, "kind": kind,
+               "sample": (f"3 decode tokens through one Qwen3-4B layer (median {t_layer:.3f} s) "
+                          f"+ one LM-head row ({t_head:.3f} s), -O2 -ffp-contract=off, one "
+                          f"thread (the reference CPU stage is single-threaded); extrapolated "
+                          f"as 36 layers + {GEN_FRACTION:.3f} LM-head rows per token"),
+               "host_cores": host_cores()}
+    emit_line(args, 1, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d, d2h, ttft,
+              generated, prof, clock_info, cpu, parallelism="single stage")
+
+
+def emit_line(args, world, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d_step, d2h_step,
+              ttft, generated, prof, clock_info, cpu, parallelism):
+    """Prints the benchmark's JSON line (rank 0)."""
+    K = args.steps
+    steps_timed = K * world  # micro-batch steps completed in the timed region
     hbm, tf_burst, tf_sust, peak_src = peaks()
     # dominant kernel class by device time
     dom = max(prof, key=lambda k: prof[k]["ms"] if (prof[k]["bytes"] or prof[k]["flops"]) else -1)
@@ -390,48 +406,282 @@ def ours(args, world, rank, local):
     roof.update({"kernel": dom, "peak_source": f"{peak_src} (MEASURED_PEAKS.json)"
                  if peak_src == "measured" else "fallback", "traffic": None,
                  "launches": p["launches"], "avg_launch_us": round(per_launch_s * 1e6, 2)})
-    kernels = {k: {"ms": round(v["ms"], 3), "share": round(v["ms"] / max(1e-9, sum(
-        x["ms"] for x in prof.values())), 4), "launches": v["launches"],
-        "gbs": round(v["bytes"] / max(1e-12, v["ms"] / 1e3) / 1e9, 1) if v["bytes"] else None,
-        "tflops": round(v["flops"] / max(1e-12, v["ms"] / 1e3) / 1e12, 1) if v["flops"] else None}
-        for k, v in prof.items()}
-    value = all_dev_tokens / (dev_ms / 1e3)
-    e2e_value = all_e2e_tokens / (e2e_ms / 1e3)
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        tps, t_layer, t_head, kind, _, _ = cpu_reference_sample()
-        cpu = {"value": round(tps, 5), "unit": "tokens/s", "cores": 1, "kind": kind,
-               "sample": (f"3 decode tokens through one Qwen3-4B layer (median {t_layer:.3f} s) "
-                          f"+ one LM-head row ({t_head:.3f} s), -O2 -ffp-contract=off, one "
-                          f"thread (the reference CPU stage is single-threaded); extrapolated "
-                          f"as 36 layers + {GEN_FRACTION:.3f} LM-head rows per token"),
-               "host_cores": host_cores()}
+    total_ms = sum(x["ms"] for x in prof.values())
+    kernels = {k: {"ms": round(v["ms"], 3), "share": round(v["ms"] / max(1e-9, total_ms), 4),
+                   "launches": v["launches"],
+                   "gbs": round(v["bytes"] / max(1e-12, v["ms"] / 1e3) / 1e9, 1) if v["bytes"] else None,
+                   "tflops": round(v["flops"] / max(1e-12, v["ms"] / 1e3) / 1e12, 1) if v["flops"] else None}
+               for k, v in prof.items()}
+    value = dev_tokens / (dev_ms / 1e3)
+    e2e_value = e2e_tokens / (e2e_ms / 1e3)
+    config = {"workload": "configuration 3: Qwen3-4B, 64 concurrent requests, prompts "
+                          "lognormal(512, 1.0) in [32, 4096], outputs U[64, 512], 512-token "
+                          "chunks mixed into decode batches, greedy",
+              "model": "Qwen3-4B-architecture random init (seeded), F16 weights, F32 accumulate",
+              "global_batch": MAX_ACTIVE * world, "seq_len": 4608,
+              "parallelism": parallelism,
+              "fast_forward_steps": args.fast_forward,
+              "l2": "inputs larger than L2: 8.0 GB of weights and the KV cache stream every step"}
+    if world > 1:
+        config["microbatches"] = world
+        config["timed_microbatch_steps"] = steps_timed
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
-        "steps": K, "warmup": W, "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "configuration 3: Qwen3-4B, 64 concurrent requests, prompts "
-                               "lognormal(512, 1.0) in [32, 4096], outputs U[64, 512], 512-token "
-                               "chunks mixed into decode batches, greedy",
-                   "model": "Qwen3-4B-architecture random init (seeded), F16 weights, F32 accumulate",
-                   "global_batch": MAX_ACTIVE * world, "seq_len": 4608,
-                   "parallelism": "single stage" if world == 1 else f"replicas x{world}",
-                   "fast_forward_steps": F,
-                   "l2": "inputs larger than L2: 8.0 GB of weights and the KV cache stream every step"},
+        "steps": K, "warmup": args.warmup, "ms_per_step": round(dev_ms / steps_timed, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic", "config": config,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                "ms_per_step": round(e2e_ms / K, 4)},
+                "h2d_bytes_per_step": int(h2d_step), "d2h_bytes_per_step": int(d2h_step),
+                "ms_per_step": round(e2e_ms / steps_timed, 4)},
         "ttft_p50_ms": round(statistics.median(ttft), 3) if ttft else None,
-        "output_tokens_per_s_e2e": round(generated * world / (e2e_ms / 1e3), 1),
+        "output_tokens_per_s_e2e": round(generated / (e2e_ms / 1e3), 1),
         "roofline": roof, "kernels": kernels, "cpu_baseline": cpu, "clocks": clock_info,
-        "gpu_launches": launches,
+        "gpu_launches": int(launches),
     }
     print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- pipeline (N > 1)
+def qwen_stage_bytes():
+    """F16 bytes one Qwen3-4B layer and the LM head stream per step."""
+    from hllm_b200.workload import QWEN3_4B as Q
+    h, i, d = Q["hidden_size"], Q["intermediate_size"], Q["head_dimension"]
+    q, kv = Q["attention_heads"] * d, Q["key_value_heads"] * d
+    layer = 2.0 * (h * (q + 2 * kv) + q * h + 2 * i * h + i * h)
+    return layer, 2.0 * Q["vocabulary_size"] * h
+
+
+def pipeline_ranges(world: int):
+    from hllm_b200.pipeline import partition_layers
+    from hllm_b200.workload import QWEN3_4B as Q
+    layer, head = qwen_stage_bytes()
+    return partition_layers(Q["layers"], world, layer, head)
+
+
+def run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, host_mode,
+                       profile=False, clocks=None):
+    """All ticks of the micro-batch schedule on this rank; times ticks [T0, T1).
+
+    host_mode False (value): rank 0 reads pre-uploaded token ids (synthetic ids
+    for decode rows), boundaries go rank to rank over NCCL, nothing returns to
+    the host.  host_mode True (e2e): rank 0 copies each step's ids from pinned
+    host memory (decode rows: the tokens the last rank sampled one tick
+    earlier, sent back over gloo), and the last rank reads its sampled tokens
+    back to the host every step.  Returns this rank's (ms, tokens completed on
+    the last rank, launches, h2d, d2h, prof, clocks, ttft samples, generated)."""
+    import torch
+    import torch.distributed as dist
+    from hllm_b200 import _lib
+    from hllm_b200.pipeline import Schedule, device_view, run_ticks
+    L = _lib.lib()
+    V, H = cfg.vocabulary_size, cfg.hidden_size
+    S = F + W + K + 1
+    sched = Schedule(world, S)
+    T0 = world * (F + W) + world - 1
+    T1 = T0 + world * K
+    first, final = rank == 0, rank == world - 1
+    stream = torch.cuda.ExternalStream(L.hllm_b200_stage_stream(stage.handle))
+    max_tokens = MAX_ACTIVE + CHUNK + 64
+    base = None
+    offsets = {}
+    if first and not host_mode:
+        chunks, off = [], 0
+        for m in range(world):
+            for j in range(S):
+                offsets[(m, j)] = off
+                for rid, fpos, count, sample, decode in plans[m][j][1]:
+                    if decode:
+                        ids = np.asarray([(rid * 7919 + fpos) % V], np.int32)
+                    else:
+                        ids = prompt_ids(rid, traces[m][rid].prompt_len, V)[fpos:fpos + count]
+                    chunks.append(np.asarray(ids, np.int32))
+                    off += count
+        all_ids = torch.from_numpy(np.concatenate(chunks)).cuda()
+        base = all_ids.data_ptr()
+    if first and host_mode:
+        ids_dev = torch.empty(max_tokens, dtype=torch.int32, device="cuda")
+    boundary = None if final else device_view(L.hllm_b200_stage_boundary(stage.handle),
+                                              (max_tokens, H))
+    seqs = [dict() for _ in range(world)]
+    last_tok = {}
+    admit_wall, first_wall = {}, {}
+    acc = dict(tokens=0, launches=0, h2d=0, d2h=0, generated=0)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    greedy = _lib.Sampling(0.0, 1.0, 0, 0, 0, 0)
+
+    def tick(t, m, j):
+        admits, rows, fin = plans[m][j]
+        n_tok = sum(r[2] for r in rows)
+        ptr = None
+        if not first:
+            ptr = links.recv_activation(n_tok)  # posted before any synchronisation
+        if t == T0:
+            torch.cuda.synchronize()
+            dist.barrier()
+            if profile:
+                _lib.check(L.hllm_b200_stage_profile(stage.handle, 1))
+            if clocks:
+                clocks.start()
+            start.record(stream)
+        now = time.time()
+        for r in admits:
+            seqs[m][r.rid] = stage.allocate_sequence(r.capacity)
+            admit_wall[(m, r.rid)] = now
+        arr = (_lib.Row * len(rows))()
+        for k, (rid, fpos, count, sample, decode) in enumerate(rows):
+            arr[k].sequence = seqs[m][rid].handle
+            arr[k].first_position = fpos
+            arr[k].tokens = count
+            arr[k].sample = int(sample)
+            arr[k].sampling = greedy
+        h2d = 0
+        if first:
+            if not host_mode:
+                ptr = base + 4 * offsets[(m, j)]
+            else:
+                if j > 0:
+                    prev = [r[0] for r in plans[m][j - 1][1] if r[3]]
+                    if prev:
+                        for rid, tok in zip(prev, links.recv_tokens(len(prev))):
+                            last_tok[(m, rid)] = int(tok)
+                ids = []
+                for rid, fpos, count, sample, decode in rows:
+                    if decode:
+                        ids.append(np.asarray([last_tok[(m, rid)]], np.int32))
+                    else:
+                        ids.append(prompt_ids(rid, traces[m][rid].prompt_len, V)[fpos:fpos + count]
+                                   .astype(np.int32))
+                # a pinned copy per step: the caching host allocator keeps it
+                # until the asynchronous upload has run
+                ids_host = torch.from_numpy(np.concatenate(ids)).pin_memory()
+                with torch.cuda.stream(stream):
+                    ids_dev[:n_tok].copy_(ids_host, non_blocking=True)
+                ptr = ids_dev.data_ptr()
+                h2d += 4 * n_tok
+        _lib.check(L.hllm_b200_step_async(stage.handle, arr, len(rows), ptr))
+        a, b = C.c_uint64(), C.c_uint64()
+        _lib.check(L.hllm_b200_stage_last_transfer(stage.handle, C.byref(a), C.byref(b)))
+        h2d += a.value
+        d2h = b.value
+        if not final:
+            links.send_activation(boundary, n_tok)
+        elif host_mode:
+            _lib.check(L.hllm_b200_stage_sync(stage.handle))
+            samp = [r for r in rows if r[3]]
+            if samp:
+                out = (_lib.Sampled * len(samp))()
+                _lib.check(L.hllm_b200_stage_results(stage.handle, out, len(samp)))
+                d2h += 104 * len(samp)
+                toks = np.asarray([out[k].token_id for k in range(len(samp))], np.int64)
+                now = time.time()
+                for (rid, fpos, count, sample, decode), tok in zip(samp, toks):
+                    if not decode and (m, rid) not in first_wall:
+                        first_wall[(m, rid)] = (now, T0 <= t < T1)
+                if j + 1 < S:
+                    links.send_tokens(toks)
+                if T0 <= t < T1:
+                    acc["generated"] += len(samp)
+        if T0 <= t < T1:
+            if final:
+                acc["tokens"] += n_tok
+            acc["launches"] += int(L.hllm_b200_stage_last_launches(stage.handle))
+            acc["h2d"] += h2d
+            acc["d2h"] += d2h
+        if t == T1 - 1:
+            end.record(stream)
+        for rid in fin:
+            stage.release(seqs[m].pop(rid))
+
+    run_ticks(sched, rank, tick)
+    links.drain()
+    _lib.check(L.hllm_b200_stage_sync(stage.handle))
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    clock_info = clocks.stop() if clocks else None
+    prof = None
+    if profile:
+        prof = read_profile(stage)
+        _lib.check(L.hllm_b200_stage_profile(stage.handle, 0))
+    for d in seqs:
+        for s in d.values():
+            stage.release(s)
+    ttft = []
+    if host_mode and (first or final):
+        # admission wall times live on rank 0, first tokens on the last rank
+        obj = [admit_wall if first else None]
+        dist.broadcast_object_list(obj, src=0, group=links.token_group)
+        if final:
+            for key, (tw, timed) in first_wall.items():
+                if timed and key in obj[0]:
+                    ttft.append((tw - obj[0][key]) * 1e3)
+    return (ms, acc["tokens"], acc["launches"], acc["h2d"], acc["d2h"], prof, clock_info, ttft,
+            acc["generated"])
+
+
+def ours_pipeline(args, world, rank, local):
+    """N > 1: the stage executor as an N-stage pipeline, one rank per GPU."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from hllm_b200 import _lib
+    from hllm_b200.pipeline import DeviceLinks
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    token_group = dist.new_group([0, world - 1], backend="gloo")
+    W, K, F = args.warmup, args.steps, args.fast_forward
+    S = F + W + K + 1
+    ranges = pipeline_ranges(world)
+    lo, hi = ranges[rank]
+    stage, cfg = make_stage(local, lo, hi, rank == 0, rank == world - 1, microbatches=world)
+    L = _lib.lib()
+    stream = torch.cuda.ExternalStream(L.hllm_b200_stage_stream(stage.handle))
+    links = DeviceLinks(rank, world, stream, MAX_ACTIVE + CHUNK + 64, cfg.hidden_size,
+                        token_group=token_group)
+
+    def fresh_plans():
+        traces, plans = [], []
+        for m in range(world):
+            tr, st = plan_schedule(S, seed=SEED + m)
+            traces.append(tr)
+            plans.append(st)
+        return traces, plans
+
+    traces, plans = fresh_plans()
+    clocks = ClockSampler(local) if rank == 0 else None
+    dev = run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, False,
+                             clocks=clocks)
+    traces, plans = fresh_plans()
+    e2e = run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, True)
+    traces, plans = fresh_plans()
+    prof = run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, False,
+                              profile=True)[5]
+    # times: max over ranks; tokens: completed on the last rank; launches: sum
+    t = torch.tensor([dev[0], e2e[0]], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    n = torch.tensor([dev[1], e2e[1], dev[2], e2e[3], e2e[4], e2e[8]], dtype=torch.float64,
+                     device="cuda")
+    dist.all_reduce(n, op=dist.ReduceOp.SUM)
+    profs = [None] * world
+    dist.all_gather_object(profs, prof)
+    ttfts = [None] * world
+    dist.all_gather_object(ttfts, e2e[7])
+    dev_ms, e2e_ms = t.tolist()
+    dev_tokens, e2e_tokens, launches, h2d, d2h, generated = n.tolist()
     stage.close()
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.destroy_process_group()
+    if rank == 0:
+        merged = {}
+        for p in profs:
+            for k, v in p.items():
+                m = merged.setdefault(k, dict(ms=0.0, launches=0, bytes=0.0, flops=0.0))
+                for f in m:
+                    m[f] += v[f]
+        ttft = [x for lst in ttfts for x in lst]
+        emit_line(args, world, dev_ms, dev_tokens, e2e_ms, e2e_tokens, int(launches),
+                  h2d / (world * K), d2h / (world * K), ttft, generated, merged, dev[6], None,
+                  parallelism=f"pipeline x{world}, layers {ranges}")
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def reference(args, world, rank):

@@ -103,6 +103,7 @@ def lib():
         "hllm_b200_stage_stream": (vp, [vp]),
         "hllm_b200_stage_device": (i32, [vp]),
         "hllm_b200_stage_last_launches": (u32, [vp]),
+        "hllm_b200_stage_boundary": (vp, [vp]),
         "hllm_b200_stage_last_transfer": (C.c_int, [vp, C.POINTER(u64), C.POINTER(u64)]),
         "hllm_b200_seq_read_kv": (C.c_int, [vp, vp, u64, u32, C.POINTER(C.c_uint16)]),
         "hllm_b200_stage_read_hidden": (C.c_int, [vp, C.POINTER(C.c_float), u64]),

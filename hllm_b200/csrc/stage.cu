@@ -1264,6 +1264,10 @@ uint32_t hllm_b200_stage_last_launches(const hllm_b200_stage* stage) {
   return stage ? stage->launches : 0;
 }
 
+const void* hllm_b200_stage_boundary(const hllm_b200_stage* stage) {
+  return stage && !stage->desc.final ? static_cast<const void*>(stage->bout) : nullptr;
+}
+
 hllm_b200_status hllm_b200_stage_last_transfer(const hllm_b200_stage* stage, uint64_t* h2d_bytes,
                                                uint64_t* d2h_bytes) {
   return guarded([&] {

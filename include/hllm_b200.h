@@ -187,6 +187,12 @@ void* hllm_b200_stage_stream(hllm_b200_stage* stage);
 int32_t hllm_b200_stage_device(const hllm_b200_stage* stage);
 /* Kernel launches of the last step (for launch accounting). */
 uint32_t hllm_b200_stage_last_launches(const hllm_b200_stage* stage);
+/* Device address of the stage's F16 boundary output, [tokens][hidden] of the
+ * last step (non-final stages), valid until the next step is enqueued; work
+ * that reads it must be ordered after the step on the stage stream.  No
+ * reference counterpart: pipeline ranks send it to the next stage's GPU
+ * device to device instead of through the host. */
+const void* hllm_b200_stage_boundary(const hllm_b200_stage* stage);
 /* Host->device and device->host bytes the last step copied. */
 hllm_b200_status hllm_b200_stage_last_transfer(const hllm_b200_stage* stage, uint64_t* h2d_bytes,
                                                uint64_t* d2h_bytes);
