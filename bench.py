@@ -624,11 +624,11 @@ def ours_pipeline(args, world, rank, local):
     import torch
     import torch.distributed as dist
     from hllm_b200 import _lib
-    from hllm_b200.pipeline import DeviceLinks
+    from hllm_b200.pipeline import DeviceLinks, make_groups
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", local))
-    token_group = dist.new_group([0, world - 1], backend="gloo")
+    pair_groups, token_group = make_groups(world)
     W, K, F = args.warmup, args.steps, args.fast_forward
     S = F + W + K + 1
     ranges = pipeline_ranges(world)
@@ -637,7 +637,7 @@ def ours_pipeline(args, world, rank, local):
     L = _lib.lib()
     stream = torch.cuda.ExternalStream(L.hllm_b200_stage_stream(stage.handle))
     links = DeviceLinks(rank, world, stream, MAX_ACTIVE + CHUNK + 64, cfg.hidden_size,
-                        token_group=token_group)
+                        token_group=token_group, pair_groups=pair_groups)
 
     def fresh_plans():
         traces, plans = [], []

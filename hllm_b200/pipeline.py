@@ -31,7 +31,7 @@ from typing import Callable, List, Optional, Sequence, Tuple
 import numpy as np
 
 __all__ = ["partition_layers", "Schedule", "run_ticks", "HostLinks", "DeviceLinks",
-           "device_view", "stage_bytes"]
+           "device_view", "stage_bytes", "make_groups"]
 
 
 def partition_layers(n_layers: int, n_stages: int, layer_bytes: float,
@@ -161,6 +161,16 @@ class HostLinks:
         return buf.numpy()
 
 
+def make_groups(world: int):
+    """The pipeline's process groups, created collectively by every rank:
+    (NCCL group of each neighbour pair (r, r + 1), gloo group {0, N - 1} for
+    the sampled tokens)."""
+    import torch.distributed as dist
+    pairs = [dist.new_group([r, r + 1]) for r in range(world - 1)]
+    tokens = dist.new_group(sorted({0, world - 1}), backend="gloo")
+    return pairs, tokens
+
+
 class _CudaArray:
     def __init__(self, ptr: int, shape, typestr: str):
         self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
@@ -187,11 +197,15 @@ class DeviceLinks:
     copy ran."""
 
     def __init__(self, rank: int, world: int, stream, max_tokens: int, hidden: int,
-                 token_group=None):
+                 token_group=None, pair_groups=None):
         import torch
         self.rank, self.world, self.stream = rank, world, stream
         self.hidden = hidden
         self.token_group = token_group
+        # one NCCL communicator per neighbour pair, so that a rank's receive from
+        # rank - 1 and its send to rank + 1 do not serialise on one communicator
+        self.recv_group = pair_groups[rank - 1] if pair_groups and rank > 0 else None
+        self.send_group = pair_groups[rank] if pair_groups and rank < world - 1 else None
         dev = torch.device("cuda", torch.cuda.current_device())
         self.recv_buf = torch.empty((max_tokens, hidden), dtype=torch.float16, device=dev)
         self.send_bufs = [torch.empty((max_tokens, hidden), dtype=torch.float16, device=dev)
@@ -204,7 +218,7 @@ class DeviceLinks:
         import torch
         import torch.distributed as dist
         with torch.cuda.stream(self.stream):
-            dist.recv(self.recv_buf[:tokens], src=self.rank - 1)
+            dist.recv(self.recv_buf[:tokens], src=self.rank - 1, group=self.recv_group)
         return self.recv_buf.data_ptr()
 
     def send_activation(self, boundary, tokens: int) -> None:
@@ -216,7 +230,8 @@ class DeviceLinks:
             if self.send_work[k] is not None:
                 self.send_work[k].wait()
             self.send_bufs[k][:tokens].copy_(boundary[:tokens])
-            self.send_work[k] = dist.isend(self.send_bufs[k][:tokens], dst=self.rank + 1)
+            self.send_work[k] = dist.isend(self.send_bufs[k][:tokens], dst=self.rank + 1,
+                                           group=self.send_group)
 
     def drain(self) -> None:
         """Waits for the sends still in flight (boundaries: on the stage stream)."""

@@ -30,7 +30,7 @@ def main(out_path):
     import torch.distributed as dist
     import oracle
     from hllm_b200 import B200Stage, ModelConfig, _lib
-    from hllm_b200.pipeline import DeviceLinks, Schedule, device_view, run_ticks
+    from hllm_b200.pipeline import DeviceLinks, Schedule, device_view, make_groups, run_ticks
     from tests.golden.make_golden import C1, C1_SEED
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -39,7 +39,7 @@ def main(out_path):
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", local))
-    token_group = dist.new_group([0, 1], backend="gloo")
+    pair_groups, token_group = make_groups(world)
     L = _lib.lib()
     g = np.load(os.path.join(ROOT, "tests", "golden", "tiny_llama_pipeline.npz"))
     lens = g["prompt_lengths"]
@@ -55,7 +55,8 @@ def main(out_path):
                       kv_pool_tokens=4096, max_step_tokens=128, max_step_rows=8, max_sequences=8)
     stage.init_synthetic(C1_SEED)
     stream = torch.cuda.ExternalStream(L.hllm_b200_stage_stream(stage.handle))
-    links = DeviceLinks(rank, world, stream, 128, cfg.hidden_size, token_group=token_group)
+    links = DeviceLinks(rank, world, stream, 128, cfg.hidden_size, token_group=token_group,
+                        pair_groups=pair_groups)
     boundary = None if rank == 1 else device_view(L.hllm_b200_stage_boundary(stage.handle),
                                                   (128, cfg.hidden_size))
     mbs = [[0, 2], [1, 3]]
