@@ -712,12 +712,18 @@ __device__ __forceinline__ uint32_t tile_off(int row, int c) {
   return static_cast<uint32_t>(row * DP * 2 + sc * 16);
 }
 
+constexpr int kPreRows = 128;    // query rows per CTA = tokens x heads of one GQA group
+constexpr int kPreThreads = 256; // 8 warps, 16 query rows each
+
 template <int DP, int KT>
 struct PrefillShape {
-  static constexpr int kRows = 64;
+  static constexpr int kRows = kPreRows;
   static constexpr uint32_t kQBytes = kRows * DP * 2;
   static constexpr uint32_t kKvBytes = KT * DP * 2;
-  static constexpr uint32_t kSmem = kQBytes + 4 * kKvBytes;  // Q + 2 x (K, V)
+  static constexpr uint32_t kSmem = kQBytes + 4 * kKvBytes;  // Q + 2 x (K, V); block table after
+  static constexpr int kMinBlocks = DP <= 128 ? 2 : 1;      // resident CTAs per SM aimed for
+  static constexpr int kChunks = DP / 8;                     // 16-byte chunks per row
+  static constexpr int kLoads = KT * kChunks / kPreThreads;  // K (or V) chunks per thread
 };
 
 // Loads `rows` rows of a [*][d] F16 source into a swizzled [rows][DP] tile;
@@ -745,200 +751,343 @@ __device__ __forceinline__ void load_tile(uint8_t* tile, int rows, int d, RowSrc
   }
 }
 
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Causal flash attention over one (kv head, query tile, key split): 128 query
+// rows = (tokens x heads of one GQA group), 8 warps of 16 rows, key tiles
+// [kt0, kt1) of the row's context.  With one split the tile is normalised and
+// stored; with several, each split stores its unnormalised rows and (m, l) and
+// the last split to arrive merges them in split order (deterministic).
+// Per-tile work is kept to the MMAs where possible: the causal mask only on
+// tiles that reach past the first query's position, the output rescale only
+// when some row's running maximum moved, the softmax scale folded into one
+// FMA before ex2, and each thread's copy slots fixed for the whole loop.
 template <int DP, int KT>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kPreThreads, PrefillShape<DP, KT>::kMinBlocks)
     prefill_attn_kernel(const AttnArgs a) {
   using S = PrefillShape<DP, KT>;
   extern __shared__ __align__(128) uint8_t smem[];
-  griddep_enter();
   uint8_t* qs = smem;
   uint8_t* ks[2] = {smem + S::kQBytes, smem + S::kQBytes + S::kKvBytes};
   uint8_t* vs[2] = {smem + S::kQBytes + 2 * S::kKvBytes, smem + S::kQBytes + 3 * S::kKvBytes};
+  int32_t* stab = reinterpret_cast<int32_t*>(smem + S::kSmem);
 
   const int d = a.dim;
   const int G = a.hq / a.hkv;
   const int QT = a.qtile_tokens;
   const int kvh = blockIdx.x;
   const int tile = blockIdx.y;
+  const int split = blockIdx.z, nsplit = gridDim.z;
+  // The packer's tables are complete before this kernel starts.
   const int r = find_row(a.cu_qtiles, a.rows, tile);
   const int count = a.row_count[r];
   if (count <= 1) return;
   const int tok0 = (tile - a.cu_qtiles[r]) * QT;  // first local token of this tile
   const int first = a.row_first[r];
-  const int t_base = a.cu_seqlens[r];
   const int ntok = min(QT, count - tok0);
   const int ctx_hi = first + tok0 + ntok;  // keys [0, ctx_hi)
-  const int32_t* table = a.block_tables + static_cast<size_t>(r) * a.max_blocks;
-
-  // Q tile: query row qr = (token qr / G, head qr % G of this group).
-  load_tile<DP>(qs, S::kRows, d, [&](int qr) -> const __half* {
-    const int tl = qr / G, g = qr % G;
-    if (tl >= ntok) return nullptr;
-    return a.q + static_cast<size_t>(t_base + tok0 + tl) * a.hq * d + (kvh * G + g) * d;
-  });
-  auto kv_src = [&](const __half* cache, int key) -> const __half* {
-    if (key >= ctx_hi) return nullptr;
-    const int bid = table[key >> 4];
-    if (bid < 0) return nullptr;
-    return cache + ((static_cast<size_t>(bid) * a.hkv + kvh) * 16 + (key & 15)) * d;
-  };
   const int n_kt = (ctx_hi + KT - 1) / KT;
-  load_tile<DP>(ks[0], KT, d, [&](int i) { return kv_src(a.k_cache, i); });
-  load_tile<DP>(vs[0], KT, d, [&](int i) { return kv_src(a.v_cache, i); });
-  cp_async_commit();
+  const int kt0 = n_kt * split / nsplit, kt1 = n_kt * (split + 1) / nsplit;
+  // This split's block-table entries (pages [pg0, pg1)) into shared memory.
+  const int pg0 = kt0 * KT / 16;
+  const int pg1 = min(min((kt1 * KT + 15) / 16, (ctx_hi + 15) / 16), a.max_blocks);
+  {
+    const int32_t* table = a.block_tables + static_cast<size_t>(r) * a.max_blocks;
+    for (int p = pg0 + threadIdx.x; p < pg1; p += blockDim.x) stab[p - pg0] = table[p];
+  }
+  griddep_enter();
+  const int t_base = a.cu_seqlens[r];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = warp * 16 + (lane >> 2), row1 = row0 + 8;
-  const int pos0 = first + tok0 + row0 / G, pos1 = first + tok0 + row1 / G;
-  const float sl2 = a.scale * kLog2e;
-
   float o[DP / 8][4];
 #pragma unroll
   for (int i = 0; i < DP / 8; ++i)
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[i][e] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  const uint32_t q_base = smem_u32(qs);
 
-  for (int kt = 0; kt < n_kt; ++kt) {
-    const int buf = kt & 1;
-    if (kt + 1 < n_kt) {
-      load_tile<DP>(ks[buf ^ 1], KT, d, [&](int i) { return kv_src(a.k_cache, (kt + 1) * KT + i); });
-      load_tile<DP>(vs[buf ^ 1], KT, d, [&](int i) { return kv_src(a.v_cache, (kt + 1) * KT + i); });
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const uint32_t k_base = smem_u32(ks[buf]);
-    const uint32_t v_base = smem_u32(vs[buf]);
+  if (kt0 < kt1) {
+    // Q tile: query row qr = (token qr / G, head qr % G of this group).
+    load_tile<DP>(qs, S::kRows, d, [&](int qr) -> const __half* {
+      const int tl = qr / G, g = qr % G;
+      if (tl >= ntok) return nullptr;
+      return a.q + static_cast<size_t>(t_base + tok0 + tl) * a.hq * d + (kvh * G + g) * d;
+    });
+    __syncthreads();  // the block table in shared memory
+    // Copy slots: chunk c of rows row_j = tid / kChunks + j * (threads / kChunks).
+    const bool fast = d == DP && S::kLoads >= 1;
+    const int cslot = threadIdx.x % S::kChunks;
+    const int rslot = threadIdx.x / S::kChunks;
+    auto load_kv = [&](int kt, int buf) {
+      if (fast) {
+        const uint32_t kb = smem_u32(ks[buf]), vb = smem_u32(vs[buf]);
+#pragma unroll
+        for (int j = 0; j < S::kLoads; ++j) {
+          const int row = rslot + j * (kPreThreads / S::kChunks);
+          const int key = kt * KT + row;
+          const int pg = key >> 4;
+          const int bid = (key < ctx_hi && pg < pg1) ? stab[pg - pg0] : -1;
+          const uint32_t off = tile_off<DP>(row, cslot);
+          if (bid >= 0) {
+            const size_t src = ((static_cast<size_t>(bid) * a.hkv + kvh) * 16 + (key & 15)) * DP +
+                               cslot * 8;
+            cp_async16(kb + off, a.k_cache + src);
+            cp_async16(vb + off, a.v_cache + src);
+          } else {  // past the context (or a missing block): zeros, never NaN
+            *reinterpret_cast<uint4*>(ks[buf] + off) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(vs[buf] + off) = make_uint4(0, 0, 0, 0);
+          }
+        }
+      } else {
+        auto kv_src = [&](const __half* cache, int key) -> const __half* {
+          if (key >= ctx_hi || (key >> 4) >= pg1) return nullptr;
+          const int bid = stab[(key >> 4) - pg0];
+          if (bid < 0) return nullptr;
+          return cache + ((static_cast<size_t>(bid) * a.hkv + kvh) * 16 + (key & 15)) * d;
+        };
+        load_tile<DP>(ks[buf], KT, d, [&](int i) { return kv_src(a.k_cache, kt * KT + i); });
+        load_tile<DP>(vs[buf], KT, d, [&](int i) { return kv_src(a.v_cache, kt * KT + i); });
+      }
+    };
+    load_kv(kt0, 0);
+    cp_async_commit();
 
-    float s[KT / 8][4];
-#pragma unroll
-    for (int i = 0; i < KT / 8; ++i)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) s[i][e] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < DP / 16; ++kk) {
-      uint32_t a0, a1, a2, a3;
-      {
-        const int rr = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int c = kk * 2 + (lane >> 4);
-        ldsm_x4(q_base + tile_off<DP>(rr, c), a0, a1, a2, a3);
+    const int pos0 = first + tok0 + row0 / G, pos1 = first + tok0 + row1 / G;
+    const int pos_min = first + tok0;  // the tile's first query position
+    const float sl2 = a.scale * kLog2e;
+    const uint32_t q_base = smem_u32(qs);
+
+    for (int kt = kt0; kt < kt1; ++kt) {
+      const int buf = (kt - kt0) & 1;
+      if (kt + 1 < kt1) {
+        load_kv(kt + 1, buf ^ 1);
+        cp_async_commit();
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
       }
+      __syncthreads();
+      const uint32_t k_base = smem_u32(ks[buf]);
+      const uint32_t v_base = smem_u32(vs[buf]);
+
+      float s[KT / 8][4];
 #pragma unroll
-      for (int nb = 0; nb < KT / 8; nb += 2) {
-        uint32_t b0, b1, b2, b3;
-        const int key = nb * 8 + (lane & 7) + (lane >> 4) * 8;
-        const int c = kk * 2 + ((lane >> 3) & 1);
-        ldsm_x4(k_base + tile_off<DP>(key, c), b0, b1, b2, b3);
-        mma16816(s[nb], a0, a1, a2, a3, b0, b1);
-        mma16816(s[nb + 1], a0, a1, a2, a3, b2, b3);
+      for (int i = 0; i < KT / 8; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[i][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < DP / 16; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        {
+          const int rr = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int c = kk * 2 + (lane >> 4);
+          ldsm_x4(q_base + tile_off<DP>(rr, c), a0, a1, a2, a3);
+        }
+#pragma unroll
+        for (int nb = 0; nb < KT / 8; nb += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int key = nb * 8 + (lane & 7) + (lane >> 4) * 8;
+          const int c = kk * 2 + ((lane >> 3) & 1);
+          ldsm_x4(k_base + tile_off<DP>(key, c), b0, b1, b2, b3);
+          mma16816(s[nb], a0, a1, a2, a3, b0, b1);
+          mma16816(s[nb + 1], a0, a1, a2, a3, b2, b3);
+        }
       }
-    }
-    // Scale, causal mask, online softmax (base-2 exponent of scale*log2(e)*s).
-    float mx0 = m0, mx1 = m1;
+      // Causal mask, only where the tile reaches past the first query.
+      if (kt * KT + KT - 1 > pos_min || kt * KT + KT > ctx_hi) {
 #pragma unroll
-    for (int nb = 0; nb < KT / 8; ++nb) {
+        for (int nb = 0; nb < KT / 8; ++nb)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = kt * KT + nb * 8 + (lane & 3) * 2 + (e & 1);
-        const int pos = e < 2 ? pos0 : pos1;
-        const float v = (key <= pos && key < ctx_hi) ? s[nb][e] * sl2 : -INFINITY;
-        s[nb][e] = v;
-        if (e < 2) mx0 = fmaxf(mx0, v); else mx1 = fmaxf(mx1, v);
+          for (int e = 0; e < 4; ++e) {
+            const int key = kt * KT + nb * 8 + (lane & 3) * 2 + (e & 1);
+            const int pos = e < 2 ? pos0 : pos1;
+            if (key > pos || key >= ctx_hi) s[nb][e] = -INFINITY;
+          }
       }
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    // A query row always sees key 0 in the first tile, so the maxima are finite
-    // from the first tile on; padded rows (beyond the tile's tokens) are masked
-    // like their last valid token and never stored.
-    const float al0 = exp2f(m0 - mx0), al1 = exp2f(m1 - mx1);
-    m0 = mx0;
-    m1 = mx1;
-    float rs0 = 0.f, rs1 = 0.f;
+      // Online softmax in base 2: p = 2^(s * scale * log2 e - m).
+      float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-    for (int nb = 0; nb < KT / 8; ++nb) {
-      s[nb][0] = exp2f(s[nb][0] - m0);
-      s[nb][1] = exp2f(s[nb][1] - m0);
-      s[nb][2] = exp2f(s[nb][2] - m1);
-      s[nb][3] = exp2f(s[nb][3] - m1);
-      rs0 += s[nb][0] + s[nb][1];
-      rs1 += s[nb][2] + s[nb][3];
-    }
-    l0 = l0 * al0 + rs0;
-    l1 = l1 * al1 + rs1;
-#pragma unroll
-    for (int i = 0; i < DP / 8; ++i) {
-      o[i][0] *= al0;
-      o[i][1] *= al0;
-      o[i][2] *= al1;
-      o[i][3] *= al1;
-    }
-    // O += P V.
-#pragma unroll
-    for (int k2 = 0; k2 < KT / 16; ++k2) {
-      const uint32_t p0 = pack_half2(s[2 * k2][0], s[2 * k2][1]);
-      const uint32_t p1 = pack_half2(s[2 * k2][2], s[2 * k2][3]);
-      const uint32_t p2 = pack_half2(s[2 * k2 + 1][0], s[2 * k2 + 1][1]);
-      const uint32_t p3 = pack_half2(s[2 * k2 + 1][2], s[2 * k2 + 1][3]);
-#pragma unroll
-      for (int db = 0; db < DP / 8; db += 2) {
-        uint32_t b0, b1, b2, b3;
-        const int key = k2 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int c = db + (lane >> 4);
-        ldsm_x4_t(v_base + tile_off<DP>(key, c), b0, b1, b2, b3);
-        mma16816(o[db], p0, p1, p2, p3, b0, b1);
-        mma16816(o[db + 1], p0, p1, p2, p3, b2, b3);
+      for (int nb = 0; nb < KT / 8; ++nb) {
+        mx0 = fmaxf(mx0, fmaxf(s[nb][0], s[nb][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[nb][2], s[nb][3]));
       }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float n0 = fmaxf(m0, mx0 * sl2), n1 = fmaxf(m1, mx1 * sl2);
+      // A split that starts after a row's position sees no key of that row
+      // yet: its maximum stays -inf and the reference point 0 keeps every
+      // exponential at exactly 0 (no inf - inf).
+      const float r0 = n0 == -INFINITY ? 0.f : n0, r1 = n1 == -INFINITY ? 0.f : n1;
+      const float al0 = ex2_approx(m0 - r0), al1 = ex2_approx(m1 - r1);
+      m0 = n0;
+      m1 = n1;
+      float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+      for (int nb = 0; nb < KT / 8; ++nb) {
+        s[nb][0] = ex2_approx(fmaf(s[nb][0], sl2, -r0));
+        s[nb][1] = ex2_approx(fmaf(s[nb][1], sl2, -r0));
+        s[nb][2] = ex2_approx(fmaf(s[nb][2], sl2, -r1));
+        s[nb][3] = ex2_approx(fmaf(s[nb][3], sl2, -r1));
+        rs0 += s[nb][0] + s[nb][1];
+        rs1 += s[nb][2] + s[nb][3];
+      }
+      l0 = l0 * al0 + rs0;
+      l1 = l1 * al1 + rs1;
+      if (!__all_sync(0xffffffffu, al0 == 1.f && al1 == 1.f)) {
+#pragma unroll
+        for (int i = 0; i < DP / 8; ++i) {
+          o[i][0] *= al0;
+          o[i][1] *= al0;
+          o[i][2] *= al1;
+          o[i][3] *= al1;
+        }
+      }
+      // O += P V.
+#pragma unroll
+      for (int k2 = 0; k2 < KT / 16; ++k2) {
+        const uint32_t p0 = pack_half2(s[2 * k2][0], s[2 * k2][1]);
+        const uint32_t p1 = pack_half2(s[2 * k2][2], s[2 * k2][3]);
+        const uint32_t p2 = pack_half2(s[2 * k2 + 1][0], s[2 * k2 + 1][1]);
+        const uint32_t p3 = pack_half2(s[2 * k2 + 1][2], s[2 * k2 + 1][3]);
+#pragma unroll
+        for (int db = 0; db < DP / 8; db += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int key = k2 * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int c = db + (lane >> 4);
+          ldsm_x4_t(v_base + tile_off<DP>(key, c), b0, b1, b2, b3);
+          mma16816(o[db], p0, p1, p2, p3, b0, b1);
+          mma16816(o[db + 1], p0, p1, p2, p3, b2, b3);
+        }
+      }
+      __syncthreads();
     }
-    __syncthreads();
   }
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
   const int tl0 = row0 / G, g0 = row0 % G, tl1 = row1 / G, g1 = row1 % G;
-  __half* out0 = tl0 < ntok ? a.out + static_cast<size_t>(t_base + tok0 + tl0) * a.ld_out +
-                                  (kvh * G + g0) * d
-                            : nullptr;
-  __half* out1 = tl1 < ntok ? a.out + static_cast<size_t>(t_base + tok0 + tl1) * a.ld_out +
-                                  (kvh * G + g1) * d
-                            : nullptr;
+  if (nsplit == 1) {
+    const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+    __half* out0 = tl0 < ntok ? a.out + static_cast<size_t>(t_base + tok0 + tl0) * a.ld_out +
+                                    (kvh * G + g0) * d
+                              : nullptr;
+    __half* out1 = tl1 < ntok ? a.out + static_cast<size_t>(t_base + tok0 + tl1) * a.ld_out +
+                                    (kvh * G + g1) * d
+                              : nullptr;
+#pragma unroll
+    for (int db = 0; db < DP / 8; ++db) {
+      const int dim = db * 8 + (lane & 3) * 2;
+      if (dim < d) {
+        if (out0) {
+          out0[dim] = __float2half_rn(o[db][0] * inv0);
+          if (dim + 1 < d) out0[dim + 1] = __float2half_rn(o[db][1] * inv0);
+        }
+        if (out1) {
+          out1[dim] = __float2half_rn(o[db][2] * inv1);
+          if (dim + 1 < d) out1[dim + 1] = __float2half_rn(o[db][3] * inv1);
+        }
+      }
+    }
+    return;
+  }
+  // Several splits: store this split's rows [64][DP] and (m, l) [64][2].
+  const size_t cell = static_cast<size_t>(tile) * a.hkv + kvh;
+  constexpr size_t kPiece = static_cast<size_t>(S::kRows) * (DP + 2);
+  float* piece = a.pre_part + (cell * nsplit + split) * kPiece;
 #pragma unroll
   for (int db = 0; db < DP / 8; ++db) {
     const int dim = db * 8 + (lane & 3) * 2;
-    if (dim < d) {
-      if (out0) {
-        out0[dim] = __float2half_rn(o[db][0] * inv0);
-        if (dim + 1 < d) out0[dim + 1] = __float2half_rn(o[db][1] * inv0);
-      }
-      if (out1) {
-        out1[dim] = __float2half_rn(o[db][2] * inv1);
-        if (dim + 1 < d) out1[dim + 1] = __float2half_rn(o[db][3] * inv1);
-      }
-    }
+    *reinterpret_cast<float2*>(piece + row0 * DP + dim) = make_float2(o[db][0], o[db][1]);
+    *reinterpret_cast<float2*>(piece + row1 * DP + dim) = make_float2(o[db][2], o[db][3]);
   }
+  if ((lane & 3) == 0) {
+    float* ml = piece + S::kRows * DP;
+    *reinterpret_cast<float2*>(ml + row0 * 2) = make_float2(m0, l0);
+    *reinterpret_cast<float2*>(ml + row1 * 2) = make_float2(m1, l1);
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    int* counter = a.pre_counters + cell;
+    const int last = atomicAdd(counter, 1) == nsplit - 1;
+    if (last) *counter = 0;
+    s_last = last;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // Merge the splits of this tile in split order.
+  const float* pieces = a.pre_part + cell * nsplit * kPiece;
+  for (int idx = threadIdx.x; idx < S::kRows * (DP / 4); idx += blockDim.x) {
+    const int row = idx / (DP / 4), c4 = (idx % (DP / 4)) * 4;
+    const int tl = row / G, g = row % G;
+    if (tl >= ntok || c4 >= d) continue;
+    float M = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp)
+      M = fmaxf(M, __ldcg(pieces + sp * kPiece + S::kRows * DP + row * 2));
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float* p = pieces + sp * kPiece;
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p + S::kRows * DP + row * 2));
+      const float w = exp2f(ml.x - M);  // 0 for a split with no key of this row
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(p + row * DP + c4));
+      L += ml.y * w;
+      acc.x += v.x * w;
+      acc.y += v.y * w;
+      acc.z += v.z * w;
+      acc.w += v.w * w;
+    }
+    const float inv = 1.0f / L;
+    __half* dst = a.out + static_cast<size_t>(t_base + tok0 + tl) * a.ld_out + (kvh * G + g) * d + c4;
+    const float vals[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      if (c4 + e < d) dst[e] = __float2half_rn(vals[e]);
+  }
+}
+
+template <int DP, int KT>
+int prefill_setup(size_t table_bytes) {
+  using S = PrefillShape<DP, KT>;
+  static int per_sm = 0;
+  static size_t configured_bytes = 0;
+  const size_t smem = S::kSmem + table_bytes;
+  if (smem > configured_bytes) {
+    if (cudaFuncSetAttribute(prefill_attn_kernel<DP, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return 0;
+    configured_bytes = smem;
+    per_sm = 0;
+  }
+  if (per_sm == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, prefill_attn_kernel<DP, KT>, kPreThreads, smem) !=
+        cudaSuccess)
+      return 0;
+    per_sm = n > 0 ? n : 1;
+  }
+  return per_sm;
 }
 
 template <int DP, int KT>
 cudaError_t launch_prefill(const AttnArgs& a, int total_qtiles, cudaStream_t stream) {
   using S = PrefillShape<DP, KT>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<DP, KT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(S::kSmem));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  return launch_dependent(prefill_attn_kernel<DP, KT>, dim3(a.hkv, total_qtiles), dim3(128),
-                          S::kSmem, stream, a);
+  const size_t table = prefill_table_bytes(a);
+  if (prefill_setup<DP, KT>(table) == 0) return cudaErrorInvalidValue;
+  const int splits = a.prefill_splits > 0 ? a.prefill_splits : 1;
+  if (splits > 1 && (!a.pre_part || !a.pre_counters)) return cudaErrorInvalidValue;
+  return launch_dependent(prefill_attn_kernel<DP, KT>, dim3(a.hkv, total_qtiles, splits),
+                          dim3(kPreThreads), S::kSmem + table, stream, a);
 }
 
 template <int D>
@@ -979,7 +1128,7 @@ cudaError_t launch_decode_mma(const AttnArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
-int attn_qtile_tokens(int group) { return 64 / group; }
+int attn_qtile_tokens(int group) { return kPreRows / group; }
 
 bool attn_decode_balanced(int dim) { return dim == 64 || dim == 128 || dim == 256; }
 
@@ -1035,12 +1184,40 @@ int attn_decode_launches(int dim) { return attn_decode_balanced(dim) ? 1 : 2; }
 cudaError_t attn_prefill_launch(const AttnArgs& a, int total_qtiles, cudaStream_t stream) {
   if (total_qtiles <= 0) return cudaSuccess;
   const int G = a.hq / a.hkv;
-  if (64 % G != 0 && G > 64) return cudaErrorInvalidValue;
+  if (G > kPreRows) return cudaErrorInvalidValue;
+  if (a.prefill_splits > kPrefillMaxSplits) return cudaErrorInvalidValue;
   if (a.dim <= 16) return launch_prefill<16, 64>(a, total_qtiles, stream);
   if (a.dim <= 64) return launch_prefill<64, 64>(a, total_qtiles, stream);
   if (a.dim <= 128) return launch_prefill<128, 64>(a, total_qtiles, stream);
   if (a.dim <= 256) return launch_prefill<256, 32>(a, total_qtiles, stream);
   return cudaErrorInvalidValue;
+}
+
+size_t prefill_table_bytes(const AttnArgs& a) {
+  return (static_cast<size_t>(a.max_blocks) * 4 + 15) & ~static_cast<size_t>(15);
+}
+
+int attn_prefill_padded_dim(int dim) {
+  return dim <= 16 ? 16 : dim <= 64 ? 64 : dim <= 128 ? 128 : 256;
+}
+
+int attn_prefill_splits(int dim, int hkv, int total_qtiles, int sm_count, size_t table_bytes) {
+  if (total_qtiles <= 0 || dim > 256) return 1;
+  const int per_sm = dim <= 16    ? prefill_setup<16, 64>(table_bytes)
+                     : dim <= 64  ? prefill_setup<64, 64>(table_bytes)
+                     : dim <= 128 ? prefill_setup<128, 64>(table_bytes)
+                                  : prefill_setup<256, 32>(table_bytes);
+  const long long base = static_cast<long long>(hkv) * total_qtiles;
+  const long long resident = static_cast<long long>(per_sm > 0 ? per_sm : 1) * sm_count;
+  // Whole waves only: as many splits as still fit in one wave of resident CTAs.
+  const long long s = resident / std::max<long long>(1, base);
+  return static_cast<int>(std::max<long long>(1, std::min<long long>(s, kPrefillMaxSplits)));
+}
+
+size_t attn_prefill_part_floats(int dim, int hkv, int total_qtiles, int splits) {
+  if (splits <= 1) return 0;
+  const size_t dp = static_cast<size_t>(attn_prefill_padded_dim(dim));
+  return static_cast<size_t>(total_qtiles) * hkv * splits * kPreRows * (dp + 2);
 }
 
 }  // namespace hb

@@ -27,6 +27,9 @@ struct AttnArgs {
                                // [pieces][Hq/Hkv][d] (balanced path)
   float* part_ml;              // matching running max, denominator pairs
   int* counters;               // [rows][Hkv] zero-initialised; returned to zero after use
+  int prefill_splits;          // key splits per prefill tile (attn_prefill_splits), >= 1
+  float* pre_part;             // [qtiles][Hkv][splits] x 64 rows x (DP + 2): split rows, (m, l)
+  int* pre_counters;           // [qtiles][Hkv] zero-initialised; returned to zero after use
   __half* out;                 // [T][ld_out]
   int ld_out;
   uint32_t* status;
@@ -50,7 +53,14 @@ bool attn_decode_balanced(int dim);
 int attn_decode_ctas(int dim, int group, long long pages, int sm_count);
 // Floats of part_o + part_ml that the balanced pass needs for `rows` rows.
 size_t attn_decode_part_floats(int rows, int hq, int hkv, int dim, int ctas);
-// Prefill rows (several new tokens): causal tiles on the tensor cores.
+// Prefill rows (several new tokens): causal tiles on the tensor cores, each
+// tile's keys split over prefill_splits CTAs whose results the last one merges.
+constexpr int kPrefillMaxSplits = 4;
 cudaError_t attn_prefill_launch(const AttnArgs& a, int total_qtiles, cudaStream_t stream);
+// Key splits that keep one wave of resident CTAs busy (1..kPrefillMaxSplits);
+// table_bytes = prefill_table_bytes of the launch (max_blocks x 4, rounded to 16).
+int attn_prefill_splits(int dim, int hkv, int total_qtiles, int sm_count, size_t table_bytes);
+size_t attn_prefill_part_floats(int dim, int hkv, int total_qtiles, int splits);
+size_t prefill_table_bytes(const AttnArgs& a);
 
 }  // namespace hb

@@ -174,32 +174,44 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
   a.ld_out = static_cast<int>(ld_out);
   a.status = status;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0, sm_count = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  // Decode: the balanced pass (head sizes 64/128/256) sizes its grid from the
+  // pages the splits cover (an upper bound of the decode rows' pages).
+  size_t part_floats = 0;
   if (total_splits) {
-    // Split outputs live in a grow-only buffer per device, kept for the process.
-    static std::mutex mu;
-    static std::map<int, std::pair<float*, size_t>> buffers;
-    // A fixed block of arrival counters (one per (row, kv head); zeroed on
-    // allocation and returned to zero by the kernel after use) at the head of
-    // the buffer, then the split outputs.
-    constexpr size_t kCounters = 1 << 16;
-    if (static_cast<size_t>(rows) * hkv > kCounters) return HLLM_B200_INVALID_REQUEST;
-    const size_t counter_off = 0;
-    int dev = 0, sm_count = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return cuda_status(e);
-    // The balanced pass (head sizes 64/128/256) sizes its grid from the pages
-    // the splits cover (an upper bound of the decode rows' pages).
     const long long pages = static_cast<long long>(total_splits) *
                             ((split_tokens + 15) / 16) * static_cast<long long>(hkv);
     a.decode_ctas = hb::attn_decode_ctas(static_cast<int>(dim), static_cast<int>(hq / hkv), pages,
                                          sm_count);
-    const size_t part_floats =
-        std::max(static_cast<size_t>(total_splits) * hq * (dim + 2),
-                 hb::attn_decode_part_floats(static_cast<int>(rows), static_cast<int>(hq),
-                                             static_cast<int>(hkv), static_cast<int>(dim),
-                                             a.decode_ctas));
-    const size_t need = kCounters + part_floats;
+    part_floats = std::max(static_cast<size_t>(total_splits) * hq * (dim + 2),
+                           hb::attn_decode_part_floats(static_cast<int>(rows), static_cast<int>(hq),
+                                                       static_cast<int>(hkv),
+                                                       static_cast<int>(dim), a.decode_ctas));
+  }
+  // Prefill: key splits per tile, merged by the last split of each tile.
+  a.prefill_splits = total_qtiles ? hb::attn_prefill_splits(static_cast<int>(dim),
+                                                            static_cast<int>(hkv),
+                                                            static_cast<int>(total_qtiles),
+                                                            sm_count, hb::prefill_table_bytes(a))
+                                  : 1;
+  const size_t pre_floats = hb::attn_prefill_part_floats(
+      static_cast<int>(dim), static_cast<int>(hkv), static_cast<int>(total_qtiles), a.prefill_splits);
+  if (part_floats || pre_floats) {
+    // Split outputs live in a grow-only buffer per device, kept for the
+    // process: a fixed block of arrival counters at its head (decode: one per
+    // (row, kv head) in the first half; prefill: one per (tile, kv head) in the
+    // second half; zeroed on allocation and returned to zero by the kernels),
+    // then the decode pieces, then the prefill pieces.
+    static std::mutex mu;
+    static std::map<int, std::pair<float*, size_t>> buffers;
+    constexpr size_t kCounters = 1 << 16;
+    if (static_cast<size_t>(rows) * hkv > kCounters / 2 ||
+        static_cast<size_t>(total_qtiles) * hkv > kCounters / 2)
+      return HLLM_B200_INVALID_REQUEST;
+    const size_t need = kCounters + part_floats + pre_floats;
     float* base = nullptr;
     {
       std::scoped_lock lock(mu);
@@ -217,10 +229,14 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
       }
       base = buf.first;
     }
-    a.counters = reinterpret_cast<int*>(base + counter_off);
+    a.counters = reinterpret_cast<int*>(base);
+    a.pre_counters = reinterpret_cast<int*>(base) + kCounters / 2;
     a.part_o = base + kCounters;
-    // part_ml after the larger of the two layouts' part_o extents.
+    // part_ml after the larger of the two decode layouts' part_o extents.
     a.part_ml = a.part_o + part_floats / (dim + 2) * dim;
+    a.pre_part = base + kCounters + part_floats;
+  }
+  if (total_splits) {
     e = hb::attn_decode_launch(a, static_cast<int>(total_splits), st);
     if (e != cudaSuccess) return cuda_status(e);
   }

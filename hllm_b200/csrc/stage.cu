@@ -169,6 +169,9 @@ struct hllm_b200_stage {
   double* sample_scratch = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
   int* attn_counters = nullptr;  // [R_max][Hkv] split arrival counters (self-resetting)
+  float* pre_part = nullptr;     // prefill key-split pieces
+  int* pre_counters = nullptr;   // [max qtiles][Hkv] split arrival counters (self-resetting)
+  int max_qtiles = 0;
   hb::GemmInput in_xn{}, in_attn{}, in_act{}, in_xs{};
   float* slots = nullptr;  // stream-K GEMM slots, consumed by the next kernel
   int* segmap = nullptr;   // their per-tile segment lists
@@ -505,6 +508,15 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
     s->part_ml = s->alloc<float>(std::max(s->max_splits * s->hq, pieces * group) * 2);
   }
   s->attn_counters = s->alloc<int>(R * s->hkv);
+  {
+    // Prefill tiles: at most one partial tile per row beyond T / qtile_tokens.
+    const int qt = hb::attn_qtile_tokens(static_cast<int>(s->hq / s->hkv));
+    s->max_qtiles = static_cast<int>((T + qt - 1) / qt + R);
+    s->pre_part = s->alloc<float>(std::max<size_t>(
+        1, hb::attn_prefill_part_floats(static_cast<int>(s->dim), static_cast<int>(s->hkv),
+                                        s->max_qtiles, hb::kPrefillMaxSplits)));
+    s->pre_counters = s->alloc<int>(static_cast<size_t>(s->max_qtiles) * s->hkv);
+  }
   s->slots = s->alloc<float>(hb::gemm_max_slot_floats(s->sm_count));
   s->segmap = s->alloc<int>(hb::kGemmMapInts);
   if (!hb::gemm_make_input(&s->in_xn, s->xn, static_cast<int>(T), static_cast<int>(s->h_pad),
@@ -615,6 +627,7 @@ struct StepPlan {
   int total_qtiles = 0;
   int qtile_tokens = 0;
   int decode_ctas = 0;     // balanced decode attention grid
+  int prefill_splits = 1;  // key splits per prefill tile
   double attn_dec_bytes = 0, attn_dec_flops = 0;  // algorithmic, per layer
   double attn_pre_bytes = 0, attn_pre_flops = 0;
 };
@@ -686,6 +699,14 @@ StepPlan plan_step(hllm_b200_stage* s, const hllm_b200_row* rows, uint32_t n, bo
   for (uint32_t i = 0; i < n; ++i)
     if (rows[i].tokens > 1)
       p.total_qtiles += static_cast<int>((rows[i].tokens + p.qtile_tokens - 1) / p.qtile_tokens);
+  if (p.total_qtiles > s->max_qtiles) fail(HLLM_B200_INTERNAL, "prefill tiles exceed the workspace");
+  {
+    hb::AttnArgs probe{};
+    probe.max_blocks = static_cast<int>(s->max_blocks);
+    p.prefill_splits = hb::attn_prefill_splits(static_cast<int>(s->dim), static_cast<int>(s->hkv),
+                                               p.total_qtiles, s->sm_count,
+                                               hb::prefill_table_bytes(probe));
+  }
   // Algorithmic attention work per layer: K and V of every context position
   // read once per kv head, q read and output written once; causal FLOPs
   // 4 * Hq * d per (query, key) pair.
@@ -873,6 +894,9 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     aa.split_tokens = p.split_tokens;
     aa.qtile_tokens = p.qtile_tokens;
     aa.decode_ctas = p.decode_ctas;
+    aa.prefill_splits = p.prefill_splits;
+    aa.pre_part = s->pre_part;
+    aa.pre_counters = s->pre_counters;
     aa.scale = 1.0f / std::sqrt(static_cast<float>(s->dim));
     aa.part_o = s->part_o;
     aa.part_ml = s->part_ml;

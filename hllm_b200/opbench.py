@@ -1,13 +1,15 @@
 """Per-operator timing of the executor's kernels through the C ABI.
 
-    python -m hllm_b200.opbench [gemm|attn|all] [--ncu-gemm M,K,N,PAIR,EPI]
+    python -m hllm_b200.opbench [gemm|attn|prefill|all] [--ncu-gemm M,K,N,PAIR,EPI]
+                                 [--ncu-attn ROWS] [--ncu-prefill FIRST,COUNT]
 
 Times the projection GEMM at the Qwen3-4B shapes (decode width 16/64 tokens,
 prefill width 575 tokens) and the paged decode attention at configuration-5
 batch sizes (contexts log-uniform in [128, 32768], 16-token pages randomly
 placed in a pool), with CUDA events on the current stream after warm-up.
 Inputs are far larger than L2 for the weight-streaming shapes.  `--ncu-gemm`
-runs three launches of one GEMM shape (for a profiler capture).
+runs three launches of one GEMM shape and `--ncu-attn` three of the decode
+attention over ROWS configuration-3-like contexts (for profiler captures).
 Device memory comes from torch; all compute is libhllm_b200.so.
 """
 from __future__ import annotations
@@ -103,6 +105,47 @@ def attn_case(rows_ctx, hq=32, hkv=8, d=128, split=256, iters=10):
     return us
 
 
+def prefill_case(first, count, rows=1, hq=32, hkv=8, d=128, iters=10):
+    """Prefill attention of `rows` chunks of `count` tokens at positions
+    [first, first + count) (causal over first + count keys each)."""
+    torch = _torch()
+    from . import _lib
+    L = _lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    ctx = first + count
+    need = (ctx + 15) // 16
+    nblocks = int(need * rows * 1.2) + 8
+    perm = np.random.default_rng(1).permutation(nblocks).astype(np.int32)
+    tables = perm[:need * rows].reshape(rows, need).copy()
+    kc = (torch.randn(nblocks, hkv, 16, d, device="cuda") / math.sqrt(d)).half()
+    vc = torch.randn(nblocks, hkv, 16, d, device="cuda").half()
+    T = rows * count
+    q = torch.randn(T, hq * d, device="cuda").half()
+    qt = int(L.hllm_b200_attention_qtile_tokens(hq // hkv))
+    tiles = (count + qt - 1) // qt
+    first_a = np.full(rows, first, np.int32)
+    count_a = np.full(rows, count, np.int32)
+    cu = (np.arange(rows + 1) * count).astype(np.int32)
+    lens = np.full(rows, ctx, np.int32)
+    cu_s = np.zeros(rows + 1, np.int32)
+    cu_q = (np.arange(rows + 1) * tiles).astype(np.int32)
+    dv = [torch.from_numpy(x).cuda() for x in (first_a, count_a, cu, lens, tables, cu_s, cu_q)]
+    out = torch.zeros(T, hq * d, device="cuda").half()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def fn():
+        _lib.check(L.hllm_b200_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                         *[t.data_ptr() for t in dv], rows, 0, rows * tiles, hq,
+                                         hkv, d, need, 16, out.data_ptr(), hq * d,
+                                         status.data_ptr(), stream))
+    us = ev_time(fn, iters)
+    pairs = rows * (count * first + count * (count + 1) / 2)
+    flops = 4.0 * hq * d * pairs
+    print(f"prefill attention rows={rows} first={first} count={count}: {us:8.1f} us  "
+          f"{flops / us / 1e6:8.1f} TFLOP/s", flush=True)
+    return us
+
+
 def gemm_suite():
     # (m, k, n, pair, epilogue): Qwen3-4B QKV, gate/up, down, o, LM head
     for args in [(6144, 2560, 64, 1, 0), (9728, 2560, 64, 2, 3), (2560, 9728, 64, 1, 2),
@@ -110,6 +153,11 @@ def gemm_suite():
                  (6144, 2560, 575, 1, 0), (9728, 2560, 575, 2, 3), (2560, 9728, 575, 1, 2),
                  (2560, 4096, 575, 1, 2)]:
         gemm_case(*args)
+
+
+def prefill_suite():
+    for first, count in ((0, 512), (512, 512), (2048, 512), (3584, 512), (1000, 100)):
+        prefill_case(first, count)
 
 
 def attn_suite():
@@ -120,7 +168,23 @@ def attn_suite():
             attn_case(ctx, split=split)
 
 
+def steady_decode_contexts(rows=64, seed=3):
+    """Decode contexts like configuration 3's steady state: prompt
+    log-normal(median 512, sigma 1) in [32, 4096] plus U[1, 512] generated."""
+    rng = np.random.default_rng(seed)
+    prompt = np.clip(np.exp(rng.normal(math.log(512), 1.0, rows)), 32, 4096)
+    return (prompt + rng.integers(1, 513, rows)).astype(int).tolist()
+
+
 def main(argv):
+    if "--ncu-prefill" in argv:
+        first, count = (int(x) for x in argv[argv.index("--ncu-prefill") + 1].split(","))
+        prefill_case(first, count, iters=3)
+        return
+    if "--ncu-attn" in argv:
+        rows = int(argv[argv.index("--ncu-attn") + 1])
+        attn_case(steady_decode_contexts(rows), iters=3)
+        return
     if "--ncu-gemm" in argv:
         m, k, n, pair, epi = (int(x) for x in argv[argv.index("--ncu-gemm") + 1].split(","))
         gemm_case(m, k, n, pair, epi, iters=3)
@@ -130,6 +194,8 @@ def main(argv):
         gemm_suite()
     if what in ("attn", "all"):
         attn_suite()
+    if what in ("prefill", "all"):
+        prefill_suite()
 
 
 if __name__ == "__main__":
