@@ -164,6 +164,15 @@ def make_stage(device: int, layer_start=0, layer_end=None, first=True, final=Tru
 KERNEL_CLASSES = ("gemm_decode", "gemm_prefill", "attn_decode", "attn_prefill", "misc", "norm",
                   "qkv_rope", "swiglu", "sampler")
 
+# DRAM bytes per launch relative to the algorithmic bytes, from ncu captures of
+# a smaller case of the same kernel (committed summaries under profiles/);
+# traffic = algorithmic bytes per launch x ratio (traffic grows with the units).
+TRAFFIC_RATIO = {
+    "attn_decode": (279.5 / 271.7, "profiles/attention_decode_64rows.md"),
+    "gemm_decode": (21.54 / 22.8, "profiles/gemm_o_proj_decode64.md"),
+    "gemm_prefill": (106.24 / 113.7, "profiles/gemm_gate_up_prefill575.md"),
+}
+
 
 def read_profile(stage):
     """Per-class totals of the stage's launch profile (ms, launches, bytes, flops)."""
@@ -403,8 +412,14 @@ def emit_line(args, world, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d
         achieved = p["bytes"] / max(1, p["launches"]) / per_launch_s / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4)}
+    traffic, traffic_src = None, None
+    if dom in TRAFFIC_RATIO and p["bytes"]:
+        ratio, traffic_src = TRAFFIC_RATIO[dom]
+        traffic = round(p["bytes"] / max(1, p["launches"]) * ratio / 1e6, 2)
     roof.update({"kernel": dom, "peak_source": f"{peak_src} (MEASURED_PEAKS.json)"
-                 if peak_src == "measured" else "fallback", "traffic": None,
+                 if peak_src == "measured" else "fallback (MEASURED_PEAKS.json absent)",
+                 "traffic": traffic, "traffic_unit": "MB per launch",
+                 "traffic_source": traffic_src,
                  "launches": p["launches"], "avg_launch_us": round(per_launch_s * 1e6, 2)})
     total_ms = sum(x["ms"] for x in prof.values())
     kernels = {k: {"ms": round(v["ms"], 3), "share": round(v["ms"] / max(1e-9, total_ms), 4),
