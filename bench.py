@@ -55,6 +55,7 @@ SEED = 20261201
 MAX_ACTIVE = 64
 CHUNK = 512
 GEN_FRACTION = 288.0 / 1128.0  # generated share of processed tokens in the trace (sets LM-head work)
+PIPELINE_LIMIT_S = 480.0  # wall-clock limit of a multi-GPU (pipeline) run
 
 
 def peaks():
@@ -83,7 +84,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.device), "-lms", "200"], stdout=subprocess.PIPE,
+                 "-i", str(self.device), "-lms", "50"], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
         except FileNotFoundError:
@@ -641,6 +642,16 @@ def ours_pipeline(args, world, rank, local):
     from hllm_b200 import _lib
     from hllm_b200.pipeline import DeviceLinks, make_groups
     torch.cuda.set_device(local)
+    # A stalled pipeline must end the run, not hold N GPUs: every rank exits
+    # with an error after PIPELINE_LIMIT_S seconds (a normal run takes a few
+    # minutes at 8 GPUs).
+    def stalled():
+        print(json.dumps({"error": f"pipeline run on rank {rank} exceeded {PIPELINE_LIMIT_S} s"}),
+              file=sys.stderr, flush=True)
+        os._exit(3)
+    watchdog = threading.Timer(PIPELINE_LIMIT_S, stalled)
+    watchdog.daemon = True
+    watchdog.start()
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", local))
     pair_groups, token_group = make_groups(world)
@@ -697,6 +708,7 @@ def ours_pipeline(args, world, rank, local):
                   parallelism=f"pipeline x{world}, layers {ranges}")
     dist.barrier()
     dist.destroy_process_group()
+    watchdog.cancel()
 
 
 def reference(args, world, rank):

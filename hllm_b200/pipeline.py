@@ -161,14 +161,19 @@ class HostLinks:
         return buf.numpy()
 
 
-def make_groups(world: int):
+def make_groups(world: int, pairs: bool = False, timeout_s: float = 120.0):
     """The pipeline's process groups, created collectively by every rank:
-    (NCCL group of each neighbour pair (r, r + 1), gloo group {0, N - 1} for
-    the sampled tokens)."""
+    (NCCL group of each neighbour pair (r, r + 1) when `pairs`, else None, so
+    that boundaries use the default group; gloo group {0, N - 1} for the
+    sampled tokens, with a `timeout_s` limit on each exchange).  The boundary
+    sends and receives run on the default group unless pairs are asked for:
+    that is the configuration exercised on two GPUs."""
+    import datetime
     import torch.distributed as dist
-    pairs = [dist.new_group([r, r + 1]) for r in range(world - 1)]
-    tokens = dist.new_group(sorted({0, world - 1}), backend="gloo")
-    return pairs, tokens
+    pair_groups = [dist.new_group([r, r + 1]) for r in range(world - 1)] if pairs else None
+    tokens = dist.new_group(sorted({0, world - 1}), backend="gloo",
+                            timeout=datetime.timedelta(seconds=timeout_s))
+    return pair_groups, tokens
 
 
 class _CudaArray:
@@ -202,8 +207,7 @@ class DeviceLinks:
         self.rank, self.world, self.stream = rank, world, stream
         self.hidden = hidden
         self.token_group = token_group
-        # one NCCL communicator per neighbour pair, so that a rank's receive from
-        # rank - 1 and its send to rank + 1 do not serialise on one communicator
+        # optional NCCL communicator per neighbour pair (else the default group)
         self.recv_group = pair_groups[rank - 1] if pair_groups and rank > 0 else None
         self.send_group = pair_groups[rank] if pair_groups and rank < world - 1 else None
         dev = torch.device("cuda", torch.cuda.current_device())
