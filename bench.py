@@ -55,7 +55,7 @@ SEED = 20261201
 MAX_ACTIVE = 64
 CHUNK = 512
 GEN_FRACTION = 288.0 / 1128.0  # generated share of processed tokens in the trace (sets LM-head work)
-PIPELINE_LIMIT_S = 480.0  # wall-clock limit of a multi-GPU (pipeline) run
+PIPELINE_LIMIT_S = 300.0  # wall-clock limit of a multi-GPU (pipeline) run
 
 
 def peaks():
