@@ -102,15 +102,16 @@ def _rank_main(rank, world, port, out_q):
                     [last[r] for r in reqs])
                 for r, tok in zip(reqs, fed):
                     last[r] = int(tok)
-            rows = [list(prompts[r]) if j == 0 else [last[r]] for r in reqs]
+            # every rank knows the rows' lengths; only rank 0 needs the ids
+            lens = [len(prompts[r]) if j == 0 else 1 for r in reqs]
             if rank == 0:
-                hs = [model.embed(ids) for ids in rows]
+                hs = [model.embed(list(prompts[r]) if j == 0 else [last[r]]) for r in reqs]
             else:
-                bits = links.recv_activation(sum(len(x) for x in rows))
+                bits = links.recv_activation(sum(lens))
                 hs, o = [], 0
-                for ids in rows:
-                    hs.append(oracle.f16_decode(bits[o:o + len(ids)]))
-                    o += len(ids)
+                for n in lens:
+                    hs.append(oracle.f16_decode(bits[o:o + n]))
+                    o += n
             outs = []
             for r, h in zip(reqs, hs):
                 outs.append(model.forward(h, pos[r], seqs[r]))
@@ -133,14 +134,37 @@ def _rank_main(rank, world, port, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.timeout(300)
-def test_two_rank_pipeline_over_gloo_matches_the_reference_two_stage_run():
+def _in_process_tokens(world, steps=32):
+    """The same pipeline run stage after stage in one process (F16 boundary
+    between consecutive stages), request by request."""
+    import oracle
+    from tests.golden.make_golden import C1, C1_SEED, c1_workload
+    weights = oracle.synth_weights(C1, C1_SEED)
+    models = [oracle.OracleModel(C1, weights, lo, hi)
+              for lo, hi in partition_layers(C1.layers, world, 1.0)]
+    prompts = c1_workload()
+    tokens = np.zeros((len(prompts), steps), np.int64)
+    for r, prompt in enumerate(prompts):
+        seqs = [m.new_sequence(len(prompt) + steps) for m in models]
+        inp, pos = list(prompt), 0
+        for j in range(steps):
+            h = models[0].embed(inp)
+            for k, (m, sq) in enumerate(zip(models, seqs)):
+                if k:
+                    h = oracle.f16_round(h)
+                h = m.forward(h, pos, sq)
+            tokens[r, j] = oracle.greedy(models[-1].logits(h[-1:]))
+            pos += len(inp)
+            inp = [int(tokens[r, j])]
+    return tokens
+
+
+def _run_ranks(world):
     import multiprocessing as mp
-    g = np.load(os.path.join(GOLD, "tiny_llama_pipeline.npz"))
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -151,4 +175,17 @@ def test_two_rank_pipeline_over_gloo_matches_the_reference_two_stage_run():
             if p.is_alive():
                 p.kill()
     assert all(p.exitcode == 0 for p in procs)
-    np.testing.assert_array_equal(tokens, g["tokens"])
+    return tokens
+
+
+@pytest.mark.timeout(300)
+def test_three_rank_pipeline_over_gloo_matches_the_in_process_run():
+    """A middle rank receives from rank 0 and sends to rank 2 on every tick;
+    three micro-batches (requests {0, 3}, {1}, {2}) follow the schedule."""
+    np.testing.assert_array_equal(_run_ranks(3), _in_process_tokens(3))
+
+
+@pytest.mark.timeout(300)
+def test_two_rank_pipeline_over_gloo_matches_the_reference_two_stage_run():
+    g = np.load(os.path.join(GOLD, "tiny_llama_pipeline.npz"))
+    np.testing.assert_array_equal(_run_ranks(2), g["tokens"])
