@@ -55,6 +55,12 @@ class Row(C.Structure):
                 ("sample", C.c_uint32), ("sampling", Sampling), ("generated_index", C.c_uint64)]
 
 
+class BoundaryIdentity(C.Structure):
+    _fields_ = [("deployment_id", C.c_char_p), ("deployment_version", C.c_uint64),
+                ("request_id", C.c_char_p), ("maximum_tokens", C.c_uint64),
+                ("hidden_size", C.c_uint64)]
+
+
 class Sampled(C.Structure):
     _fields_ = [("token_id", C.c_uint64), ("logprob", C.c_double), ("has_logprob", C.c_uint32),
                 ("n_top", C.c_uint32), ("top_ids", C.c_uint64 * 5),
@@ -105,6 +111,13 @@ def lib():
         "hllm_b200_stage_last_launches": (u32, [vp]),
         "hllm_b200_stage_boundary": (vp, [vp]),
         "hllm_b200_stage_last_transfer": (C.c_int, [vp, C.POINTER(u64), C.POINTER(u64)]),
+        "hllm_b200_envelope_encode": (C.c_int, [C.POINTER(BoundaryIdentity), u64, u64, u32, vp,
+                                                u64, u64, u64, vp, u64, C.POINTER(u64)]),
+        "hllm_b200_envelope_decode": (C.c_int, [vp, u64, C.POINTER(BoundaryIdentity), u64, u64,
+                                                u32, C.POINTER(u64), C.POINTER(u64)]),
+        "hllm_b200_stage_envelope": (C.c_int, [vp, u64, u64, C.POINTER(BoundaryIdentity), u64,
+                                               u64, u32, vp, u64, C.POINTER(u64)]),
+        "hllm_b200_stage_envelope_wait": (C.c_int, [vp]),
         "hllm_b200_seq_read_kv": (C.c_int, [vp, vp, u64, u32, C.POINTER(C.c_uint16)]),
         "hllm_b200_stage_read_hidden": (C.c_int, [vp, C.POINTER(C.c_float), u64]),
         "hllm_b200_stage_read_logits": (C.c_int, [vp, C.POINTER(C.c_float), u64]),

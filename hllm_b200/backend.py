@@ -134,6 +134,23 @@ class B200Stage:
         self._lock = threading.Lock()
 
     # ------------------------------------------------------------ lifetime
+    def encode_boundary(self, first_token: int, tokens: int, identity, sequence: int,
+                        position: int, prefill: bool = False) -> bytes:
+        """The serialized StageMessage (worker::encode_tensor,
+        cpp/src/worker/boundary_codec.cpp:68-108) of boundary rows
+        [first_token, first_token + tokens) of this non-final stage's last
+        step, built from device memory (hllm_b200_stage_envelope, then
+        hllm_b200_stage_envelope_wait).  `identity` is a wire.BoundaryIdentity."""
+        ident = identity.c()
+        n = C.c_uint64()
+        args = (self._h, first_token, tokens, C.byref(ident), sequence, position, int(prefill))
+        with self._lock:
+            check(lib().hllm_b200_stage_envelope(*args, None, 0, C.byref(n)))
+            out = C.create_string_buffer(n.value)
+            check(lib().hllm_b200_stage_envelope(*args, out, n.value, C.byref(n)))
+            check(lib().hllm_b200_stage_envelope_wait(self._h))
+        return out.raw[:n.value]
+
     def close(self):
         if self._h:
             lib().hllm_b200_stage_destroy(self._h)

@@ -31,6 +31,7 @@
 
 #include "attention.cuh"
 #include "common.cuh"
+#include "envelope.cuh"
 #include "gemm.cuh"
 #include "hllm_b200.h"
 #include "kernels.cuh"
@@ -189,6 +190,13 @@ struct hllm_b200_stage {
   int32_t* h_slot_rows = nullptr;             // pinned [max_seqs][max_blocks] block-list staging
   std::vector<cudaEvent_t> slot_copy_done;    // per slot: its last staging copy has run
   __half* h_act = nullptr;  // boundary in/out staging [T_max][h]
+  // Envelope copies (hllm_b200_stage_envelope): boundary rows go device->host
+  // on their own stream after the step that wrote them; a later step's
+  // boundary write waits for env_done.  Payloads are checked at the next wait.
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t step_done = nullptr, env_done = nullptr;
+  bool env_pending = false;
+  std::vector<std::pair<const uint8_t*, uint64_t>> env_payloads;
 
   std::map<std::string, Target> targets;
   std::set<std::string> loaded;
@@ -220,6 +228,12 @@ struct hllm_b200_stage {
   cudaEvent_t prof_open = nullptr;
 
   ~hllm_b200_stage() {
+    if (copy_stream) {
+      cudaStreamSynchronize(copy_stream);
+      cudaStreamDestroy(copy_stream);
+    }
+    if (step_done) cudaEventDestroy(step_done);
+    if (env_done) cudaEventDestroy(env_done);
     if (stream) {
       cudaStreamSynchronize(stream);
       cudaStreamDestroy(stream);
@@ -964,6 +978,8 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
                                s->d_params, s->sample_scratch, s->results, s->status, s->stream));
     }
   } else {
+    if (s->env_pending)  // an envelope copy may still be reading the boundary buffer
+      check_cuda(cudaStreamWaitEvent(s->stream, s->env_done, 0), "envelope order");
     PLAUNCH(kProfOther, 0, 0, hb::boundary_out_launch(s->hidden, T, h, s->bout, s->status, s->stream));
   }
   s->last_samples = p.samples;
@@ -1290,6 +1306,70 @@ uint32_t hllm_b200_stage_last_launches(const hllm_b200_stage* stage) {
 
 const void* hllm_b200_stage_boundary(const hllm_b200_stage* stage) {
   return stage && !stage->desc.final ? static_cast<const void*>(stage->bout) : nullptr;
+}
+
+hllm_b200_status hllm_b200_stage_envelope(hllm_b200_stage* stage, uint64_t first_token,
+                                          uint64_t tokens,
+                                          const hllm_b200_boundary_identity* identity,
+                                          uint64_t sequence, uint64_t position, uint32_t prefill,
+                                          uint8_t* out, uint64_t capacity, uint64_t* written) {
+  return guarded([&] {
+    if (!stage || !identity || !identity->deployment_id || !identity->request_id || !written)
+      fail(HLLM_B200_INVALID_REQUEST, "null argument");
+    std::scoped_lock lock(stage->mutex);
+    if (stage->desc.final) fail(HLLM_B200_INVALID_REQUEST, "a final stage has no boundary output");
+    if (tokens == 0 || first_token > stage->last_tokens || tokens > stage->last_tokens - first_token)
+      fail(HLLM_B200_INVALID_REQUEST, "rows outside the last step's boundary");
+    hb::EnvelopeIdentity id;
+    id.deployment_id = identity->deployment_id;
+    id.deployment_version = identity->deployment_version;
+    id.request_id = identity->request_id;
+    id.maximum_tokens = identity->maximum_tokens;
+    id.hidden_size = identity->hidden_size;
+    const uint64_t bytes = tokens * stage->h * sizeof(__half);
+    hb::EnvelopeLayout layout;
+    std::string why;
+    const hllm_b200_status st = hb::envelope_plan(id, sequence, position, prefill != 0, bytes,
+                                                  tokens, stage->h, &layout, &why);
+    if (st != HLLM_B200_OK) fail(st, why);
+    *written = layout.total;
+    if (!out) return;  // size query
+    if (capacity < layout.total) fail(HLLM_B200_INVALID_REQUEST, "output buffer too small");
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    if (!stage->copy_stream) {
+      check_cuda(cudaStreamCreateWithFlags(&stage->copy_stream, cudaStreamNonBlocking),
+                 "cudaStreamCreate");
+      check_cuda(cudaEventCreateWithFlags(&stage->step_done, cudaEventDisableTiming),
+                 "cudaEventCreate");
+      check_cuda(cudaEventCreateWithFlags(&stage->env_done, cudaEventDisableTiming),
+                 "cudaEventCreate");
+    }
+    hb::envelope_write_frame(id, sequence, position, prefill != 0, tokens, stage->h, out);
+    check_cuda(cudaEventRecord(stage->step_done, stage->stream), "envelope order");
+    check_cuda(cudaStreamWaitEvent(stage->copy_stream, stage->step_done, 0), "envelope order");
+    check_cuda(cudaMemcpyAsync(out + layout.payload_offset, stage->bout + first_token * stage->h,
+                               bytes, cudaMemcpyDeviceToHost, stage->copy_stream),
+               "envelope copy");
+    check_cuda(cudaEventRecord(stage->env_done, stage->copy_stream), "envelope order");
+    stage->env_pending = true;
+    stage->env_payloads.emplace_back(out + layout.payload_offset, bytes);
+  });
+}
+
+hllm_b200_status hllm_b200_stage_envelope_wait(hllm_b200_stage* stage) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    std::scoped_lock lock(stage->mutex);
+    if (!stage->env_pending) return;
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    check_cuda(cudaEventSynchronize(stage->env_done), "envelope copy");
+    std::vector<std::pair<const uint8_t*, uint64_t>> payloads;
+    payloads.swap(stage->env_payloads);
+    stage->env_pending = false;
+    for (const auto& [p, n] : payloads)
+      if (!hb::f16_payload_finite(p, n))  // cpp/src/worker/boundary_codec.cpp:96-100
+        fail(HLLM_B200_INTERNAL, "backend returned a non-finite boundary activation");
+  });
 }
 
 hllm_b200_status hllm_b200_stage_last_transfer(const hllm_b200_stage* stage, uint64_t* h2d_bytes,

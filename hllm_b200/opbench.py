@@ -1,6 +1,6 @@
 """Per-operator timing of the executor's kernels through the C ABI.
 
-    python -m hllm_b200.opbench [gemm|attn|prefill|all] [--ncu-gemm M,K,N,PAIR,EPI]
+    python -m hllm_b200.opbench [gemm|attn|prefill|envelope|all] [--ncu-gemm M,K,N,PAIR,EPI]
                                  [--ncu-attn ROWS] [--ncu-prefill FIRST,COUNT]
 
 Times the projection GEMM at the Qwen3-4B shapes (decode width 16/64 tokens,
@@ -10,6 +10,8 @@ placed in a pool), with CUDA events on the current stream after warm-up.
 Inputs are far larger than L2 for the weight-streaming shapes.  `--ncu-gemm`
 runs three launches of one GEMM shape and `--ncu-attn` three of the decode
 attention over ROWS configuration-3-like contexts (for profiler captures).
+`envelope` times the boundary wire codec (host encode/decode, and the
+envelope built from device memory when a GPU is present).
 Device memory comes from torch; all compute is libhllm_b200.so.
 """
 from __future__ import annotations
@@ -176,6 +178,65 @@ def steady_decode_contexts(rows=64, seed=3):
     return (prompt + rng.integers(1, 513, rows)).astype(int).tolist()
 
 
+def envelope_suite(tokens=512, width=2560, iters=200):
+    """The boundary wire codec at a 512-token Qwen3-4B chunk (2.6 MB of F16):
+    host encode and decode through the C ABI (no GPU needed), then, on a GPU,
+    the envelope built from a non-final stage's device boundary
+    (hllm_b200_stage_envelope + _wait) into pinned memory."""
+    import ctypes as C
+    import time
+    from . import _lib
+    L = _lib.lib()
+    ident = _lib.BoundaryIdentity(b"qwen3-4b-plan", 3, b"request-000001", 4608, width)
+    x = (np.random.default_rng(0).standard_normal(tokens * width)).astype("<f2")
+    n = C.c_uint64()
+    args = (C.byref(ident), 0, 0, 1, x.ctypes.data, x.nbytes, tokens, width)
+    _lib.check(L.hllm_b200_envelope_encode(*args, None, 0, C.byref(n)))
+    out = np.empty(n.value, np.uint8)
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        _lib.check(L.hllm_b200_envelope_encode(*args, out.ctypes.data, n.value, C.byref(n)))
+    enc = (time.perf_counter() - t0) / iters
+    off, tok = C.c_uint64(), C.c_uint64()
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        _lib.check(L.hllm_b200_envelope_decode(out.ctypes.data, n.value, C.byref(ident), 0, 0, 1,
+                                               C.byref(off), C.byref(tok)))
+    dec = (time.perf_counter() - t0) / iters
+    print(f"envelope host  {tokens}x{width}: encode {enc * 1e6:8.1f} us "
+          f"({x.nbytes / enc / 1e9:6.1f} GB/s), decode {dec * 1e6:8.1f} us "
+          f"({x.nbytes / dec / 1e9:6.1f} GB/s), message {n.value} bytes", flush=True)
+    try:
+        import torch
+        if not torch.cuda.is_available():
+            return
+    except ImportError:
+        return
+    from .backend import B200Stage, DecodeBatchItem, ModelConfig, TokenInput
+    cfg = ModelConfig(width, 9728, 32, 8, 128, 4608, 1e-6, 1e6, True, 151936, 36, True)
+    stage = B200Stage(cfg, 0, 1, first=True, final=False, kv_pool_tokens=8192,
+                      max_step_tokens=tokens + 64, max_step_rows=80, max_sequences=80)
+    stage.init_synthetic(1)
+    ids = [int(v) for v in np.random.default_rng(2).integers(0, 151936, tokens)]
+    seq = stage.allocate_sequence(tokens + 8)
+    stage.execute_mixed_batch([DecodeBatchItem(TokenInput(ids), 0, seq)])
+    pinned = torch.empty(n.value, dtype=torch.uint8, pin_memory=True)
+    dev_args = (stage.handle, 0, tokens, C.byref(ident), 0, 0, 1)
+    for _ in range(3):
+        _lib.check(L.hllm_b200_stage_envelope(*dev_args, pinned.data_ptr(), n.value, C.byref(n)))
+        _lib.check(L.hllm_b200_stage_envelope_wait(stage.handle))
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        _lib.check(L.hllm_b200_stage_envelope(*dev_args, pinned.data_ptr(), n.value, C.byref(n)))
+        _lib.check(L.hllm_b200_stage_envelope_wait(stage.handle))
+    devt = (time.perf_counter() - t0) / iters
+    assert bytes(pinned[:16].numpy()) == bytes(out[:16])  # same frame as the host encoding
+    print(f"envelope device {tokens}x{width}: stage_envelope+wait {devt * 1e6:8.1f} us "
+          f"({x.nbytes / devt / 1e9:6.1f} GB/s device->host into the message)", flush=True)
+    stage.release(seq)
+    stage.close()
+
+
 def main(argv):
     if "--ncu-prefill" in argv:
         first, count = (int(x) for x in argv[argv.index("--ncu-prefill") + 1].split(","))
@@ -196,6 +257,8 @@ def main(argv):
         attn_suite()
     if what in ("prefill", "all"):
         prefill_suite()
+    if what in ("envelope", "all"):
+        envelope_suite()
 
 
 if __name__ == "__main__":

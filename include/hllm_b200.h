@@ -193,6 +193,68 @@ uint32_t hllm_b200_stage_last_launches(const hllm_b200_stage* stage);
  * reference counterpart: pipeline ranks send it to the next stage's GPU
  * device to device instead of through the host. */
 const void* hllm_b200_stage_boundary(const hllm_b200_stage* stage);
+/* ------------------------------------------------------------------------
+ * The F16 boundary on the wire between workers: a serialized
+ * hllm.v1.StageMessage whose `tensor` member is a TensorEnvelope
+ * (proto/execution.proto:48-65, 115-123).  The bytes are the reference
+ * worker's own: encode produces what worker::encode_tensor serializes, decode
+ * accepts what worker::decode_tensor accepts, with its checks and messages. */
+
+/* worker::BoundaryIdentity (cpp/include/hllm/worker/boundary_codec.hpp:7-13):
+ * the active sequence's deployment and request, its token budget and the
+ * model width.  Strings are NUL-terminated UTF-8. */
+typedef struct hllm_b200_boundary_identity {
+  const char* deployment_id;
+  uint64_t deployment_version;
+  const char* request_id;
+  uint64_t maximum_tokens;
+  uint64_t hidden_size;
+} hllm_b200_boundary_identity;
+
+/* worker::encode_tensor (cpp/src/worker/boundary_codec.cpp:68-108): the
+ * serialized StageMessage for `tokens` F16 rows of `width` (`payload_bytes`
+ * bytes at `payload`, host memory) as step `sequence` at `position`; the phase
+ * is prefill when sequence == 0 or `prefill`.  With out == NULL only the
+ * message size goes to *written.  RESOURCE_EXHAUSTED for a payload above
+ * 8 MiB, INTERNAL for a bad shape or a non-finite value (the reference's
+ * errors), INVALID_REQUEST when `capacity` is below the size. */
+hllm_b200_status hllm_b200_envelope_encode(const hllm_b200_boundary_identity* identity,
+                                           uint64_t sequence, uint64_t position, uint32_t prefill,
+                                           const uint16_t* payload, uint64_t payload_bytes,
+                                           uint64_t tokens, uint64_t width, uint8_t* out,
+                                           uint64_t capacity, uint64_t* written);
+
+/* worker::decode_tensor (cpp/src/worker/boundary_codec.cpp:15-66, with
+ * runtime::validate_tensor_envelope, cpp/src/tensor_envelope.cpp:26-83) on a
+ * received serialized StageMessage: on OK the F16 rows are the
+ * *tokens x hidden_size values at message + *payload_offset -- no copy; pass
+ * that address as hllm_b200_row.activations.  INVALID_REQUEST with the
+ * reference's message otherwise (and "malformed stage message" for bytes
+ * that do not parse). */
+hllm_b200_status hllm_b200_envelope_decode(const uint8_t* message, uint64_t bytes,
+                                           const hllm_b200_boundary_identity* identity,
+                                           uint64_t sequence, uint64_t position, uint32_t prefill,
+                                           uint64_t* payload_offset, uint64_t* tokens);
+
+/* The envelope of boundary rows [first_token, first_token + tokens) of the
+ * stage's last step (a non-final stage), built straight from device memory
+ * (no reference counterpart; it replaces the host copy that precedes
+ * encode_tensor): the message frame is written on the host and the payload is
+ * copied device->host into its place in `out` on a copy stream, ordered after
+ * the last step.  The call does not wait: `out` (pinned memory for an
+ * asynchronous copy) must stay valid until hllm_b200_stage_envelope_wait.
+ * Steps enqueued meanwhile run alongside the copy; only a later step's write
+ * of the boundary buffer waits for it.  The last step must have succeeded
+ * (its own completion reports a failure). */
+hllm_b200_status hllm_b200_stage_envelope(hllm_b200_stage* stage, uint64_t first_token,
+                                          uint64_t tokens,
+                                          const hllm_b200_boundary_identity* identity,
+                                          uint64_t sequence, uint64_t position, uint32_t prefill,
+                                          uint8_t* out, uint64_t capacity, uint64_t* written);
+/* Waits for the envelope copies issued since the last wait, then applies
+ * encode_tensor's finite check to their payloads (INTERNAL if one fails). */
+hllm_b200_status hllm_b200_stage_envelope_wait(hllm_b200_stage* stage);
+
 /* Host->device and device->host bytes the last step copied. */
 hllm_b200_status hllm_b200_stage_last_transfer(const hllm_b200_stage* stage, uint64_t* h2d_bytes,
                                                uint64_t* d2h_bytes);

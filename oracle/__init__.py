@@ -14,6 +14,9 @@ Two libraries sit behind this module:
   ``oracle/Makefile`` with ``ref_shim.cpp`` (present wherever the reference
   tree was available at build time).
 
+``oracle.envelope`` (pure Python) restates the boundary wire codec
+(cpp/src/worker/boundary_codec.cpp, cpp/src/tensor_envelope.cpp).
+
 ``OracleModel`` composes the layer functions the way the reference's
 ``DenseStage::run`` does (cpp/src/cpu/stage.cpp:129-191): embed, layers,
 last-row final norm + LM head, sampling; F16 boundary rounding between stages.

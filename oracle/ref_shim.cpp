@@ -16,6 +16,12 @@
 //   hllm::runtime::sample_token    cpp/src/sampling.cpp:65
 //   hllm::runtime::float_to_float16 / float16_to_float  cpp/src/half.cpp
 //   hllm::runtime::combine_decode_inputs  cpp/src/decode_batch.cpp:8
+//   hllm::runtime::validate_tensor_envelope, SequenceTracker  cpp/src/tensor_envelope.cpp
+//
+// cpp/src/safetensors.cpp (which also defines data_type_bytes) needs
+// nlohmann/json and is not compiled; this file defines data_type_bytes with
+// the element sizes of safetensors.hpp's DataType (the same table as
+// safetensors.cpp:118-138) so that tensor_envelope.cpp links.
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -28,6 +34,19 @@
 #include "hllm/runtime/half.hpp"
 #include "hllm/runtime/sampling.hpp"
 #include "hllm/runtime/stage_backend.hpp"
+#include "hllm/runtime/tensor_envelope.hpp"
+
+namespace hllm::runtime {
+std::size_t data_type_bytes(const DataType dtype) noexcept {
+  switch (dtype) {
+    case DataType::kBool: case DataType::kU8: case DataType::kI8: return 1U;
+    case DataType::kI16: case DataType::kU16: case DataType::kF16: case DataType::kBF16: return 2U;
+    case DataType::kI32: case DataType::kU32: case DataType::kF32: return 4U;
+    case DataType::kI64: case DataType::kU64: case DataType::kF64: return 8U;
+  }
+  return 0U;
+}
+}  // namespace hllm::runtime
 
 namespace {
 using hllm::cpu::LayerKvCache;
@@ -311,6 +330,62 @@ int ref_combine_decode_tokens(const std::uint64_t* ids, const std::uint64_t* cou
   } catch (const std::exception& e) {
     return status_of(e);
   }
+}
+
+// runtime::validate_tensor_envelope on the metadata decode_tensor builds
+// (F16, dense row-major; phase 0 prefill, 1 decode).  Returns 0 or the error
+// status, and the exception message in `message`.
+int ref_validate_envelope(std::uint32_t protocol_version, const char* deployment_id,
+                          std::uint64_t deployment_version, const char* request_id,
+                          std::uint64_t microbatch_id, std::uint64_t sequence_number,
+                          std::uint32_t decode, std::uint64_t first_position,
+                          const std::uint64_t* lengths, std::uint64_t n_lengths,
+                          const std::uint64_t* slots, std::uint64_t n_slots,
+                          const std::uint64_t* shape, std::uint64_t n_shape,
+                          std::uint64_t payload_length, std::uint64_t received,
+                          std::uint64_t maximum_batch, std::uint64_t maximum_sequence_length,
+                          std::uint64_t hidden_size, std::uint64_t maximum_payload_bytes,
+                          char* message, std::uint64_t message_size) {
+  try {
+    hllm::runtime::TensorEnvelopeMetadata m{
+        protocol_version, deployment_id, deployment_version, request_id, microbatch_id,
+        sequence_number,
+        decode ? hllm::runtime::ExecutionPhase::kDecode : hllm::runtime::ExecutionPhase::kPrefill,
+        first_position,
+        std::vector<std::uint64_t>(lengths, lengths + n_lengths),
+        std::vector<std::uint64_t>(slots, slots + n_slots),
+        std::vector<std::uint64_t>(shape, shape + n_shape),
+        hllm::runtime::DataType::kF16,
+        hllm::runtime::TensorLayout::kDenseRowMajorLittleEndian,
+        payload_length};
+    hllm::runtime::TensorEnvelopeLimits limits{};
+    limits.maximum_batch = maximum_batch;
+    limits.maximum_sequence_length = maximum_sequence_length;
+    limits.hidden_size = hidden_size;
+    limits.maximum_payload_bytes = maximum_payload_bytes;
+    hllm::runtime::validate_tensor_envelope(m, received, limits);
+    return 0;
+  } catch (const std::exception& e) {
+    if (message && message_size) {
+      std::strncpy(message, e.what(), message_size - 1);
+      message[message_size - 1] = 0;
+    }
+    return status_of(e);
+  }
+}
+
+// runtime::SequenceTracker: feeds `n` numbers; returns how many were accepted
+// before the first rejection (n when all were).
+std::uint64_t ref_sequence_tracker(const std::uint64_t* numbers, std::uint64_t n) {
+  hllm::runtime::SequenceTracker tracker;
+  for (std::uint64_t i = 0; i < n; ++i) {
+    try {
+      tracker.accept(numbers[i]);
+    } catch (const std::exception&) {
+      return i;
+    }
+  }
+  return n;
 }
 
 }  // extern "C"
