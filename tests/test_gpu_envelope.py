@@ -80,3 +80,54 @@ def test_envelope_issued_before_the_next_step_keeps_its_rows():
     assert second.payload != first.payload[:len(second.payload)]
     s0.close()
     s1.close()
+
+
+def test_b200_worker_to_cpu_worker_over_the_wire():
+    """Configuration 1 split as a B200 worker (layers 0-1) and a CPU worker
+    (layers 2-3, the reference's CPU math as restated by the oracle), with the
+    boundary carried as wire bytes: the B200 stage's device envelope, parsed and
+    checked by the CPU side's decode_tensor restatement.  The greedy tokens are
+    the reference's two-stage golden up to the first step whose top-2 logit gap
+    is below 1e-2."""
+    import numpy as np
+    import os
+    import oracle
+    from oracle import envelope as O
+    from tests.test_gpu_stage import GAP, GOLD, c1_spec, cfg_of, top2_gap
+    from hllm_b200 import B200Stage
+    from tests.gpu_util import torch_cuda
+
+    torch_cuda()
+    spec, seed = c1_spec()
+    g = np.load(os.path.join(GOLD, "tiny_llama_pipeline.npz"))
+    s0 = B200Stage(cfg_of(spec), 0, 2, first=True, final=False, kv_pool_tokens=4096)
+    s0.init_synthetic(seed)
+    cpu = oracle.OracleModel(spec, oracle.synth_weights(spec, seed), 2, 4)
+    lens = g["prompt_lengths"]
+    offs = np.concatenate([[0], np.cumsum(lens)])
+    for r in range(4):
+        prompt = [int(x) for x in g["prompt_ids"][offs[r]:offs[r + 1]]]
+        ident = BoundaryIdentity("c1-plan", 1, f"request-{r}", len(prompt) + 32, spec.hidden_size)
+        o_ident = O.Identity(b"c1-plan", 1, f"request-{r}".encode(), len(prompt) + 32,
+                             spec.hidden_size)
+        a = s0.allocate_sequence(len(prompt) + 32)
+        b = cpu.new_sequence(len(prompt) + 32)
+        inp, pos, agree = prompt, 0, True
+        for step in range(32):
+            s0.execute(TokenInput(inp), pos, a)
+            wire = s0.encode_boundary(0, len(inp), ident, step, pos)
+            off, tokens = O.decode_tensor(wire, o_ident, step, pos)
+            assert tokens == len(inp)
+            bits = np.frombuffer(wire, np.uint16, count=tokens * spec.hidden_size, offset=off)
+            h = oracle.f16_decode(bits.reshape(tokens, spec.hidden_size))
+            logits = cpu.logits(cpu.forward(h, pos, b)[-1:])[0]
+            tok = int(np.argmax(logits))
+            if agree:
+                if top2_gap(logits) < GAP:
+                    agree = False
+                else:
+                    assert tok == int(g["tokens"][r, step]), (r, step)
+            pos += len(inp)
+            inp = [tok]
+        s0.release(a)
+    s0.close()

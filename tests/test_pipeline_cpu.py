@@ -186,6 +186,13 @@ def test_three_rank_pipeline_over_gloo_matches_the_in_process_run():
 
 
 @pytest.mark.timeout(300)
+def test_four_rank_pipeline_over_gloo_matches_the_in_process_run():
+    """One layer per rank; four micro-batches ({0}, {1}, {2}, {3}) keep every
+    rank busy, two middle ranks relay every tick."""
+    np.testing.assert_array_equal(_run_ranks(4), _in_process_tokens(4))
+
+
+@pytest.mark.timeout(300)
 def test_two_rank_pipeline_over_gloo_matches_the_reference_two_stage_run():
     g = np.load(os.path.join(GOLD, "tiny_llama_pipeline.npz"))
     np.testing.assert_array_equal(_run_ranks(2), g["tokens"])
