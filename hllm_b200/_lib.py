@@ -61,6 +61,11 @@ class BoundaryIdentity(C.Structure):
                 ("hidden_size", C.c_uint64)]
 
 
+class ComponentTiming(C.Structure):
+    _fields_ = [("component", C.c_char * 16), ("layer_index", C.c_int64),
+                ("milliseconds", C.c_double)]
+
+
 class Sampled(C.Structure):
     _fields_ = [("token_id", C.c_uint64), ("logprob", C.c_double), ("has_logprob", C.c_uint32),
                 ("n_top", C.c_uint32), ("top_ids", C.c_uint64 * 5),
@@ -118,6 +123,9 @@ def lib():
         "hllm_b200_stage_envelope": (C.c_int, [vp, u64, u64, C.POINTER(BoundaryIdentity), u64,
                                                u64, u32, vp, u64, C.POINTER(u64)]),
         "hllm_b200_stage_envelope_wait": (C.c_int, [vp]),
+        "hllm_b200_stage_component_timing": (C.c_int, [vp, u32]),
+        "hllm_b200_stage_components": (C.c_int, [vp, C.POINTER(ComponentTiming), u32,
+                                                 C.POINTER(u32)]),
         "hllm_b200_seq_read_kv": (C.c_int, [vp, vp, u64, u32, C.POINTER(C.c_uint16)]),
         "hllm_b200_stage_read_hidden": (C.c_int, [vp, C.POINTER(C.c_float), u64]),
         "hllm_b200_stage_read_logits": (C.c_int, [vp, C.POINTER(C.c_float), u64]),

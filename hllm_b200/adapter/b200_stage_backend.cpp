@@ -175,19 +175,29 @@ runtime::StageOutput B200StageBackend::execute_profiled(runtime::StageInput inpu
                                                         runtime::SequenceState& state,
                                                         const std::atomic_bool& cancelled,
                                                         runtime::ExecutionTiming& timing) const {
+  // The reference's components (cpp/src/cuda/stage.cpp:394-454): input,
+  // one "layer" per owned layer, then final norm / LM head / sampling or the
+  // boundary output, timed with CUDA events on the stage stream.
   timing = {};
-  check(hllm_b200_stage_profile(stage_, 1U));
-  auto output = execute(std::move(input), first_position, state, cancelled);
-  static const char* kNames[] = {"gemm_decode", "gemm_prefill", "attention_decode",
-                                 "attention_prefill", "misc", "norm", "qkv_rope", "swiglu",
-                                 "sampling"};
-  for (std::uint32_t kind = 0; kind < 9; ++kind) {
-    double ms = 0, bytes = 0, flops = 0;
-    std::uint64_t launches = 0;
-    check(hllm_b200_stage_profile_read(stage_, kind, &ms, &launches, &bytes, &flops));
-    if (launches) timing.components.push_back({kNames[kind], std::nullopt, ms});
+  check(hllm_b200_stage_component_timing(stage_, 1U));
+  runtime::StageOutput output;
+  try {
+    output = execute(std::move(input), first_position, state, cancelled);
+  } catch (...) {
+    hllm_b200_stage_component_timing(stage_, 0U);
+    throw;
   }
-  check(hllm_b200_stage_profile(stage_, 0U));
+  std::uint32_t count = 0;
+  check(hllm_b200_stage_components(stage_, nullptr, 0, &count));
+  std::vector<hllm_b200_component_timing> parts(count);
+  check(hllm_b200_stage_components(stage_, parts.data(), count, &count));
+  check(hllm_b200_stage_component_timing(stage_, 0U));
+  for (const auto& c : parts)
+    timing.components.push_back(
+        {c.component,
+         c.layer_index >= 0 ? std::optional<std::size_t>(static_cast<std::size_t>(c.layer_index))
+                            : std::nullopt,
+         c.milliseconds});
   return output;
 }
 

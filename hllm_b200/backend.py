@@ -276,6 +276,28 @@ class B200Stage:
         return self.execute_mixed_batch([DecodeBatchItem(input, first_position, state, cancelled)],
                                         _check_cancel_all=True)[0]
 
+    def execute_profiled(self, input: StageInput, first_position: int, state: SequenceState,
+                         cancelled=None):
+        """execute() plus its component timing (stage_backend.hpp:103-106):
+        (output, [(component, layer index or None, milliseconds), ...]) with the
+        reference's components -- "embedding" / "from-wire", one "layer" per
+        owned layer, then "final_norm", "lm_head", "sampling" or "to-wire"."""
+        with self._lock:
+            check(lib().hllm_b200_stage_component_timing(self._h, 1))
+        try:
+            output = self.execute(input, first_position, state, cancelled)
+            n = C.c_uint32()
+            with self._lock:
+                check(lib().hllm_b200_stage_components(self._h, None, 0, C.byref(n)))
+                parts = (_lib.ComponentTiming * max(1, n.value))()
+                check(lib().hllm_b200_stage_components(self._h, parts, n.value, C.byref(n)))
+        finally:
+            with self._lock:
+                lib().hllm_b200_stage_component_timing(self._h, 0)
+        timing = [(p.component.decode(), p.layer_index if p.layer_index >= 0 else None,
+                   p.milliseconds) for p in parts[:n.value]]
+        return output, timing
+
     def execute_decode_batch(self, items: Sequence[DecodeBatchItem]):
         """combine_decode_inputs rules (cpp/src/decode_batch.cpp:8-38) then one pass.
         An in-flight batch is not pre-empted by one member's cancellation

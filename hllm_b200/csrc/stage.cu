@@ -227,6 +227,37 @@ struct hllm_b200_stage {
   uint64_t prof_n[kProfKinds] = {};
   cudaEvent_t prof_open = nullptr;
 
+  // Component timing (hllm_b200_stage_component_timing): CUDA events at the
+  // reference's phase boundaries of a step -- input, each layer, final norm,
+  // LM head, sampling or boundary output (cpp/src/cuda/stage.cpp:394-454).
+  struct Mark {
+    const char* name;
+    int64_t layer;
+    cudaEvent_t ev;
+  };
+  bool comp_timing = false;
+  std::vector<Mark> marks;  // the last step's
+  std::vector<cudaEvent_t> mark_pool;
+  cudaEvent_t mark_start = nullptr;
+
+  void mark_begin() {
+    if (!comp_timing) return;
+    marks.clear();
+    if (!mark_start) check_cuda(cudaEventCreate(&mark_start), "cudaEventCreate");
+    check_cuda(cudaEventRecord(mark_start, stream), "component timing");
+  }
+  void mark(const char* name, int64_t layer = -1) {
+    if (!comp_timing) return;
+    if (marks.size() == mark_pool.size()) {
+      cudaEvent_t e;
+      check_cuda(cudaEventCreate(&e), "cudaEventCreate");
+      mark_pool.push_back(e);
+    }
+    cudaEvent_t e = mark_pool[marks.size()];
+    check_cuda(cudaEventRecord(e, stream), "component timing");
+    marks.push_back({name, layer, e});
+  }
+
   ~hllm_b200_stage() {
     if (copy_stream) {
       cudaStreamSynchronize(copy_stream);
@@ -252,6 +283,8 @@ struct hllm_b200_stage {
       cudaEventDestroy(e.b);
     }
     for (auto e : event_pool) cudaEventDestroy(e);
+    for (auto e : mark_pool) cudaEventDestroy(e);
+    if (mark_start) cudaEventDestroy(mark_start);
   }
 
   cudaEvent_t take_event() {
@@ -775,6 +808,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
   const size_t R = s->R_max;
   const int T = static_cast<int>(p.tokens);
   s->launches = 0;
+  s->mark_begin();
   // ---- upload row descriptors (and ids / activations)
   const int ring = s->up_next;
   s->up_next = (s->up_next + 1) % hllm_b200_stage::kUpRing;
@@ -850,6 +884,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     PLAUNCH(kProfOther, 0, 0, hb::boundary_in_launch(s->bin, T, static_cast<int>(s->h), s->hidden, s->status,
                                   s->stream));
   }
+  s->mark(s->desc.first ? "embedding" : "from-wire");
 
   // ---- layers
   const float eps = s->desc.rms_norm_epsilon;
@@ -955,6 +990,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
               hb::residual_norm_launch(s->hidden, T, h, pd.stream_k ? &dslots : nullptr,
                                        next_norm, eps, s->xn, static_cast<int>(s->h_pad),
                                        s->stream));
+    s->mark("layer", static_cast<int64_t>(s->desc.layer_start + li));
   }
 
   // ---- output
@@ -964,6 +1000,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
       PLAUNCH(kProfOther, 0, 0, hb::last_token_launch(s->cu_seqlens, s->sample_rows, S, s->last_idx, s->stream));
       PLAUNCH(kProfNorm, 0, 0, hb::rmsnorm_launch(s->hidden, S, h, s->final_norm, eps, s->xs,
                                 static_cast<int>(s->h_pad), s->last_idx, s->stream));
+      s->mark("final_norm");
       const hb::GemmPlan ph = hb::gemm_plan(s->g_head, S, s->sm_count);
       hb::GemmSlots hslots{};
       PLAUNCH(S <= 128 ? kProfGemmDecode : kProfGemmPrefill,
@@ -974,6 +1011,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
         PLAUNCH(kProfSwiglu, 0, 0,
                 hb::gemm_finish_launch(hslots, S, hb::kEpiStoreF32, s->logits,
                                        static_cast<int>(s->V), s->stream));
+      s->mark("lm_head");
       PLAUNCH(kProfSample, 0, 0, hb::sample_launch(s->logits, S, static_cast<int>(s->V), static_cast<int>(s->V),
                                s->d_params, s->sample_scratch, s->results, s->status, s->stream));
     }
@@ -1192,6 +1230,10 @@ hllm_b200_status hllm_b200_step(hllm_b200_stage* stage, const hllm_b200_row* row
     if (!stage->desc.final)
       check_cuda(cudaMemcpyAsync(stage->h_act, stage->bout, p.tokens * stage->h * sizeof(__half),
                                  cudaMemcpyDeviceToHost, stage->stream), "boundary download");
+    if (!stage->desc.final)
+      stage->mark("to-wire");
+    else if (p.samples)
+      stage->mark("sampling");
     check_cuda(cudaStreamSynchronize(stage->stream), "step");
     stage->prof_collect();
     uint32_t bits;
@@ -1306,6 +1348,42 @@ uint32_t hllm_b200_stage_last_launches(const hllm_b200_stage* stage) {
 
 const void* hllm_b200_stage_boundary(const hllm_b200_stage* stage) {
   return stage && !stage->desc.final ? static_cast<const void*>(stage->bout) : nullptr;
+}
+
+hllm_b200_status hllm_b200_stage_component_timing(hllm_b200_stage* stage, uint32_t enable) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    std::scoped_lock lock(stage->mutex);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    stage->comp_timing = enable != 0;
+    stage->marks.clear();
+  });
+}
+
+hllm_b200_status hllm_b200_stage_components(hllm_b200_stage* stage,
+                                            hllm_b200_component_timing* out, uint32_t capacity,
+                                            uint32_t* count) {
+  return guarded([&] {
+    if (!stage || !count || (capacity && !out)) fail(HLLM_B200_INVALID_REQUEST, "null argument");
+    std::scoped_lock lock(stage->mutex);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    *count = static_cast<uint32_t>(stage->marks.size());
+    if (stage->marks.empty()) return;
+    check_cuda(cudaEventSynchronize(stage->marks.back().ev), "component timing");
+    cudaEvent_t prev = stage->mark_start;
+    for (size_t i = 0; i < stage->marks.size(); ++i) {
+      const auto& m = stage->marks[i];
+      float ms = 0.f;
+      check_cuda(cudaEventElapsedTime(&ms, prev, m.ev), "component timing");
+      prev = m.ev;
+      if (i >= capacity) continue;
+      hllm_b200_component_timing& o = out[i];
+      std::memset(&o, 0, sizeof(o));
+      std::strncpy(o.component, m.name, sizeof(o.component) - 1);
+      o.layer_index = m.layer;
+      o.milliseconds = ms;
+    }
+  });
 }
 
 hllm_b200_status hllm_b200_stage_envelope(hllm_b200_stage* stage, uint64_t first_token,

@@ -274,6 +274,28 @@ hllm_b200_status hllm_b200_stage_profile(hllm_b200_stage* stage, uint32_t enable
 hllm_b200_status hllm_b200_stage_profile_read(hllm_b200_stage* stage, uint32_t kind, double* ms,
                                               uint64_t* launches, double* bytes, double* flops);
 
+/* Component timing of a step in the reference's taxonomy
+ * (runtime::ExecutionTiming, cpp/include/hllm/runtime/timing.hpp:10-17, as
+ * cpp/src/cuda/stage.cpp:394-454 marks it): "embedding" or "from-wire", then
+ * "layer" for each owned layer (layer_index = its model index), then
+ * "final_norm", "lm_head", "sampling" on a final stage that samples, or
+ * "to-wire" on a non-final stage.  Each is the device time from the previous
+ * mark (the first from the start of the step, host->device input included),
+ * taken with CUDA events on the stage stream rather than host clocks after a
+ * synchronize.  enable != 0 records marks on every step; components() returns
+ * those of the last hllm_b200_step (the blocking call records the last mark
+ * after its device->host copies), *count = their number, at most `capacity`
+ * written.  Backs StageBackend::execute_profiled (stage_backend.hpp:103-106). */
+typedef struct hllm_b200_component_timing {
+  char component[16];
+  int64_t layer_index; /* -1: none */
+  double milliseconds;
+} hllm_b200_component_timing;
+hllm_b200_status hllm_b200_stage_component_timing(hllm_b200_stage* stage, uint32_t enable);
+hllm_b200_status hllm_b200_stage_components(hllm_b200_stage* stage,
+                                            hllm_b200_component_timing* out, uint32_t capacity,
+                                            uint32_t* count);
+
 /* Reads back one layer's K or V for positions [0, length) of a sequence as
  * F16 [length][kv_heads][head_dim] (the reference's contiguous cache layout,
  * cpp/src/cpu/llama.cpp:152-158), gathering the paged blocks.  Test trace;

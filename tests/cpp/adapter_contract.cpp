@@ -11,6 +11,11 @@
 //  2. The reference's StageScheduler (cpp/src/worker/scheduler.cpp) driving the
 //     backend from concurrent request threads: every request's tokens equal a
 //     serial run's, and the scheduler formed decode batches of at most 8.
+//  3. The reference's own paired timing contract (tests/cpp/profiling_contract.hpp
+//     in the reference tree, compiled from there with gtest_shim/): a first
+//     stage (layer 0) and a final stage (layer 1) whose execute_profiled outputs
+//     equal execute's and whose components run from "embedding" to "to-wire"
+//     and from "from-wire" to "sampling", with the right layer indices.
 #include <atomic>
 #include <chrono>
 #include <cmath>
@@ -23,6 +28,7 @@
 
 #include "b200_stage_backend.hpp"
 #include "hllm/worker/scheduler.hpp"
+#include "profiling_contract.hpp"
 
 using namespace hllm;
 
@@ -38,7 +44,9 @@ int failures = 0;
     }                                            \
   } while (0)
 
-std::unique_ptr<b200::B200StageBackend> make_stage(std::uint64_t seed) {
+std::unique_ptr<b200::B200StageBackend> make_stage(std::uint64_t seed, std::uint64_t start = 0,
+                                                   std::uint64_t end = 2, bool first = true,
+                                                   bool final = true) {
   hllm_b200_stage_desc d{};
   d.hidden_size = 256;
   d.intermediate_size = 688;
@@ -50,10 +58,10 @@ std::unique_ptr<b200::B200StageBackend> make_stage(std::uint64_t seed) {
   d.rope_theta = 1e6F;
   d.query_key_norm = 1;
   d.vocabulary_size = 4096;
-  d.layer_start = 0;
-  d.layer_end = 2;
-  d.first = 1;
-  d.final = 1;
+  d.layer_start = start;
+  d.layer_end = end;
+  d.first = first ? 1 : 0;
+  d.final = final ? 1 : 0;
   d.tied_head = 1;
   d.device_id = 0;
   d.kv_pool_tokens = 8192;
@@ -64,7 +72,7 @@ std::unique_ptr<b200::B200StageBackend> make_stage(std::uint64_t seed) {
   b200::check(hllm_b200_stage_create(&d, &stage));
   b200::check(hllm_b200_stage_init_synthetic(stage, seed));
   b200::check(hllm_b200_stage_finalize(stage));
-  return std::make_unique<b200::B200StageBackend>(stage, true, true);
+  return std::make_unique<b200::B200StageBackend>(stage, first, final);
 }
 
 void decode_batch_case(runtime::StageBackend& stage, double temperature) {
@@ -154,6 +162,14 @@ int main() {
   EXPECT(metrics.largest_decode_batch <= 8U, "largest batch %zu", metrics.largest_decode_batch);
   std::printf("decode_batches=%zu largest_decode_batch=%zu completed_steps=%zu\n",
               metrics.decode_batches, metrics.largest_decode_batch, metrics.completed_steps);
+  // The reference's profiling contract on a two-stage split.
+  {
+    auto first = make_stage(7, 0, 1, true, false);
+    auto last = make_stage(7, 1, 2, false, true);
+    test::paired_timing_contract(*first, *last);
+    failures += gtest_shim::failures();
+    std::printf("paired timing contract: %s\n", gtest_shim::failures() ? "failed" : "ok");
+  }
   std::printf(failures ? "adapter contract: %d failures\n" : "adapter contract: ok\n", failures);
   return failures ? 1 : 0;
 }

@@ -274,3 +274,36 @@ def test_qwen3_4b_geometry_two_layers_prefill_decode_and_mixed_batch():
         if top2_gap(la[i]) > GAP:
             assert mixed[i].id == alone[i].id
     stage.close()
+
+
+def test_execute_profiled_components_follow_the_reference_taxonomy():
+    """execute_profiled (stage_backend.hpp:103-106) reports the components of
+    cpp/src/cuda/stage.cpp:394-454 -- input, one "layer" per owned layer with
+    its model index, then final norm / LM head / sampling or the boundary
+    output -- and returns what execute returns."""
+    cfg, weights, _ = tiny_qwen()
+    s0 = make_stage(cfg, weights, layer_start=0, layer_end=1, first=True, final=False,
+                    kv_pool_tokens=256)
+    s1 = make_stage(cfg, weights, layer_start=1, layer_end=2, first=False, final=True,
+                    kv_pool_tokens=256)
+    a, b = s0.allocate_sequence(16), s0.allocate_sequence(16)
+    c, d = s1.allocate_sequence(16), s1.allocate_sequence(16)
+    ids = [1, 4, 2, 8, 3]
+    for pos in (0, 3, 4):
+        inp = TokenInput(ids[pos:pos + (3 if pos == 0 else 1)])
+        plain = s0.execute(inp, pos, a)
+        timed, parts = s0.execute_profiled(inp, pos, b)
+        assert plain.payload == timed.payload
+        assert [p[0] for p in parts] == ["embedding", "layer", "to-wire"]
+        assert parts[1][1] == 0 and parts[0][1] is None
+        assert all(np.isfinite(p[2]) and p[2] >= 0 for p in parts)
+        out_plain = s1.execute(plain, pos, c)
+        out_timed, parts = s1.execute_profiled(timed, pos, d)
+        assert out_plain.id == out_timed.id
+        assert [p[0] for p in parts] == ["from-wire", "layer", "final_norm", "lm_head",
+                                          "sampling"]
+        assert parts[1][1] == 1
+    # timing is off again: a plain step records nothing new
+    s0.execute(TokenInput([5]), 5, a)
+    s0.close()
+    s1.close()
