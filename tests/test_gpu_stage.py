@@ -307,3 +307,73 @@ def test_execute_profiled_components_follow_the_reference_taxonomy():
     s0.execute(TokenInput([5]), 5, a)
     s0.close()
     s1.close()
+
+
+FALCON3_3B = oracle.ModelSpec(hidden_size=3072, intermediate_size=9216, attention_heads=12,
+                              key_value_heads=4, head_dimension=256, layers=22,
+                              vocabulary_size=131072, maximum_sequence_length=2304,
+                              rms_norm_epsilon=1e-6, rope_theta=1e6, query_key_norm=False,
+                              tied=False)
+
+
+def test_falcon3_geometry_seeded_sampling_with_cancellation_and_slot_reuse():
+    """Configuration 4's shapes (h3072, 12q/4kv, d256, I9216, V131072, untied
+    LM head), two layers, seeded synthetic weights.  Eight requests with their
+    own seeds (temperature 0.7, top-p 0.9) prefill and then decode as one
+    batch; after the third decode step a quarter of them are cancelled and
+    released, and two new requests are admitted.  The pool and the sequence
+    slots hold exactly eight requests, so the new ones run only in the freed
+    KV blocks and slots.  Bars: every live row's logits at every step within
+    2e-2 of the F32 oracle on the GPU's own token path (stale K/V in a reused
+    block would break this), and every sampled token equal to the reference
+    sampler's draw on the GPU's logits row with the request's seed and draw
+    counter (sampling.cpp:65-90)."""
+    spec = FALCON3_3B
+    seed = 3303
+    cap = 128
+    torch_cuda()
+    stage = B200Stage(cfg_of(spec), 0, 2, first=True, final=True, kv_pool_tokens=8 * cap,
+                      max_sequences=8)
+    stage.init_synthetic(seed)
+    orc = oracle.OracleModel(spec, oracle.synth_weights(spec, seed, layers=range(2)), 0, 2)
+    rng = np.random.default_rng(44)
+
+    class Req:
+        def __init__(self, rid):
+            self.rid = rid
+            self.prompt = [int(x) for x in rng.integers(0, spec.vocabulary_size,
+                                                       int(rng.integers(16, 97)))]
+            self.seq = stage.allocate_sequence(cap)
+            self.seq.sampling = SamplingOptions(0.7, 0.9, 0, 1000 + rid, False, 0)
+            self.oseq = orc.new_sequence(cap)
+            self.pos = 0
+            self.next = self.prompt
+
+    live = [Req(r) for r in range(8)]
+    with pytest.raises(StageError) as e:  # the pool is full
+        stage.allocate_sequence(cap)
+    assert e.value.code == _lib.RESOURCE_EXHAUSTED
+    draws = 0
+    for step in range(8):
+        if step == 4:  # cancel a quarter mid-decode; their blocks and slots go back
+            for r in (live[1], live[5]):
+                stage.release(r.seq)
+            live = [r for i, r in enumerate(live) if i not in (1, 5)]
+            live += [Req(100), Req(101)]
+        items = [DecodeBatchItem(TokenInput(r.next), r.pos, r.seq) for r in live]
+        counters = [r.seq.generated_index for r in live]
+        outs = stage.execute_mixed_batch(items)
+        gpu = stage.read_logits(len(live))
+        for i, (r, out) in enumerate(zip(live, outs)):
+            ol = orc.logits(orc.forward(orc.embed(r.next), r.pos, r.oseq)[-1:])[0]
+            err = float(np.max(np.abs(gpu[i] - ol)))
+            assert err < LOGIT_TOL, (step, r.rid, err)
+            opts = oracle.Sampling(0.7, 0.9, 0, 1000 + r.rid, 0, 0)
+            st, want = oracle.sample_token(gpu[i], opts, counters[i])
+            assert st == 0 and out.id == want.token_id, (step, r.rid)
+            assert r.seq.generated_index == counters[i] + 1
+            draws += 1
+            r.pos += len(r.next)
+            r.next = [out.id]
+    assert draws == 8 * 8
+    stage.close()
