@@ -377,3 +377,63 @@ def test_falcon3_geometry_seeded_sampling_with_cancellation_and_slot_reuse():
             r.next = [out.id]
     assert draws == 8 * 8
     stage.close()
+
+
+QWEN3_06B = oracle.ModelSpec(hidden_size=1024, intermediate_size=3072, attention_heads=16,
+                             key_value_heads=8, head_dimension=128, layers=28,
+                             vocabulary_size=151936, maximum_sequence_length=2048,
+                             rms_norm_epsilon=1e-6, rope_theta=1e6, query_key_norm=True,
+                             tied=True)
+
+
+def test_qwen3_06b_geometry_two_stage_split_with_batched_decode():
+    """Configuration 2's shapes (h1024, 16q/8kv, d128, I3072, V151936, tied,
+    q/k-norm) as a two-stage split (layer 0 | layer 1, F16 boundary between
+    the stages, as 14 | 14 splits the model): sixteen requests with prompts
+    U[64, 1024) prefill in two mixed steps, then decode greedily as one batch.
+    Bars: every row's logits within 2e-2 of the F32 oracle (F16 boundary
+    rounding included) on the GPU's token path, greedy tokens by the top-2 gap
+    rule."""
+    spec = QWEN3_06B
+    seed = 606
+    torch_cuda()
+    cfg = cfg_of(spec)
+    s0 = B200Stage(cfg, 0, 1, first=True, final=False, kv_pool_tokens=16 * 1088,
+                   max_step_tokens=8192)
+    s1 = B200Stage(cfg, 1, 2, first=False, final=True, kv_pool_tokens=16 * 1088,
+                   max_step_tokens=8192)
+    s0.init_synthetic(seed)
+    s1.init_synthetic(seed)
+    weights = oracle.synth_weights(spec, seed, layers=range(2))
+    o0 = oracle.OracleModel(spec, weights, 0, 1)
+    o1 = oracle.OracleModel(spec, weights, 1, 2)
+    rng = np.random.default_rng(66)
+    reqs = []
+    for r in range(16):
+        prompt = [int(x) for x in rng.integers(0, spec.vocabulary_size, int(rng.integers(64, 1024)))]
+        reqs.append(dict(next=prompt, pos=0, a=s0.allocate_sequence(len(prompt) + 8),
+                         b=s1.allocate_sequence(len(prompt) + 8),
+                         oa=o0.new_sequence(len(prompt) + 8), ob=o1.new_sequence(len(prompt) + 8),
+                         agree=True))
+    groups = [reqs[:8], reqs[8:]]  # prefill in two mixed steps, then all sixteen decode
+    for step in range(6):
+        for grp in (groups if step == 0 else [reqs]):
+            bounds = s0.execute_mixed_batch([DecodeBatchItem(TokenInput(q["next"]), q["pos"], q["a"])
+                                             for q in grp])
+            outs = s1.execute_mixed_batch([DecodeBatchItem(bd, q["pos"], q["b"])
+                                           for bd, q in zip(bounds, grp)])
+            gpu = s1.read_logits(len(grp))
+            for i, (q, out) in enumerate(zip(grp, outs)):
+                h = oracle.f16_round(o0.forward(o0.embed(q["next"]), q["pos"], q["oa"]))
+                ol = o1.logits(o1.forward(h, q["pos"], q["ob"])[-1:])[0]
+                err = float(np.max(np.abs(gpu[i] - ol)))
+                assert err < LOGIT_TOL, (step, i, err)
+                if q["agree"]:
+                    if top2_gap(ol) < GAP:
+                        q["agree"] = False
+                    else:
+                        assert out.id == int(np.argmax(ol)), (step, i)
+                q["pos"] += len(q["next"])
+                q["next"] = [out.id]
+    s0.close()
+    s1.close()
