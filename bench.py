@@ -69,18 +69,58 @@ def peaks():
 
 # ---------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples during the timed region (clocks and throttle reasons)."""
+    """SM clocks and clock-event (throttle) reasons sampled during the timed
+    region: NVML polled every 10 ms from a thread (read only), or nvidia-smi
+    -lms 50 where NVML is unavailable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvml.h nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, device: int):
         self.device = device
         self.proc = None
         self.lines = []
+        self.samples = []  # (sm MHz, max MHz, reason bits)
+        self.stop_flag = threading.Event()
+        self.thread = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            props = torch.cuda.get_device_properties(self.device)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device)
 
     def start(self):
+        try:
+            nv, handle = self._nvml_handle()
+            event_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            mx = nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM)
+
+            def poll():
+                while not self.stop_flag.is_set():
+                    try:
+                        sm = nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)
+                        bits = event_reasons(handle)
+                    except Exception:
+                        break
+                    self.samples.append((float(sm), float(mx), int(bits)))
+                    self.stop_flag.wait(0.01)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -95,6 +135,15 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.thread:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            sm = [x[0] for x in self.samples]
+            reasons = {name for bits in (x[2] for x in self.samples)
+                       for bit, name in self.REASONS.items() if bits & bit}
+            return {"sm_mhz": statistics.median(sm) if sm else None,
+                    "sm_max_mhz": self.samples[0][1] if self.samples else None,
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml"}
         if self.proc:
             self.proc.terminate()
             try:
@@ -116,7 +165,7 @@ class ClockSampler:
                 if val.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------- schedule
