@@ -11,8 +11,9 @@
 //  2. The reference's StageScheduler (cpp/src/worker/scheduler.cpp) driving the
 //     backend from concurrent request threads: every request's tokens equal a
 //     serial run's, and the scheduler formed decode batches of at most 8.
-//  3. The reference's own paired timing contract (tests/cpp/profiling_contract.hpp
-//     in the reference tree, compiled from there with gtest_shim/): a first
+//  3. (`adapter_contract profiling`) The reference's own paired timing contract
+//     (tests/cpp/profiling_contract.hpp in the reference tree, compiled from
+//     there with gtest_shim/): a first
 //     stage (layer 0) and a final stage (layer 1) whose execute_profiled outputs
 //     equal execute's and whose components run from "embedding" to "to-wire"
 //     and from "from-wire" to "sampling", with the right layer indices.
@@ -22,6 +23,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <memory>
+#include <string>
 #include <thread>
 #include <variant>
 #include <vector>
@@ -132,7 +134,18 @@ std::vector<std::uint64_t> run_request(runtime::StageBackend& stage,
 }
 }  // namespace
 
-int main() {
+// The reference's profiling contract on a two-stage split (layer 0 | layer 1).
+int profiling_contract() {
+  auto first = make_stage(7, 0, 1, true, false);
+  auto last = make_stage(7, 1, 2, false, true);
+  test::paired_timing_contract(*first, *last);
+  const int n = gtest_shim::failures();
+  std::printf(n ? "paired timing contract: %d failures\n" : "paired timing contract: ok\n", n);
+  return n ? 1 : 0;
+}
+
+int main(int argc, char** argv) {
+  if (argc > 1 && std::string(argv[1]) == "profiling") return profiling_contract();
   auto stage = make_stage(7);
   decode_batch_case(*stage, 0.0);
   decode_batch_case(*stage, 0.8);
@@ -162,14 +175,6 @@ int main() {
   EXPECT(metrics.largest_decode_batch <= 8U, "largest batch %zu", metrics.largest_decode_batch);
   std::printf("decode_batches=%zu largest_decode_batch=%zu completed_steps=%zu\n",
               metrics.decode_batches, metrics.largest_decode_batch, metrics.completed_steps);
-  // The reference's profiling contract on a two-stage split.
-  {
-    auto first = make_stage(7, 0, 1, true, false);
-    auto last = make_stage(7, 1, 2, false, true);
-    test::paired_timing_contract(*first, *last);
-    failures += gtest_shim::failures();
-    std::printf("paired timing contract: %s\n", gtest_shim::failures() ? "failed" : "ok");
-  }
   std::printf(failures ? "adapter contract: %d failures\n" : "adapter contract: ok\n", failures);
   return failures ? 1 : 0;
 }

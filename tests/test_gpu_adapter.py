@@ -13,6 +13,8 @@ pytestmark = pytest.mark.gpu
 
 
 def test_reference_scheduler_and_decode_batch_contract_over_the_c_abi():
+    from tests.gpu_util import torch_cuda
+    torch_cuda()
     if not os.path.exists(BINARY):
         pytest.skip("adapter contract not built (needs the reference tree at build time)")
     r = subprocess.run([BINARY], capture_output=True, text=True, timeout=600)

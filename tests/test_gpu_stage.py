@@ -105,9 +105,9 @@ def test_tiny_llama_two_stage_pipeline_tokens_and_logits():
     spec, seed = c1_spec()
     g = np.load(os.path.join(GOLD, "tiny_llama_pipeline.npz"))
     cfg = cfg_of(spec)
+    torch_cuda()
     s0 = B200Stage(cfg, 0, 2, first=True, final=False, kv_pool_tokens=4096)
     s1 = B200Stage(cfg, 2, 4, first=False, final=True, kv_pool_tokens=4096)
-    torch_cuda()
     s0.init_synthetic(seed)
     s1.init_synthetic(seed)
     weights = oracle.synth_weights(spec, seed)
@@ -227,8 +227,8 @@ def test_qwen3_4b_geometry_two_layers_prefill_decode_and_mixed_batch():
     spec = QWEN3_4B
     seed = 4242
     cfg = cfg_of(spec)
-    stage = B200Stage(cfg, 0, 2, first=True, final=True, kv_pool_tokens=8192)
     torch_cuda()
+    stage = B200Stage(cfg, 0, 2, first=True, final=True, kv_pool_tokens=8192)
     stage.init_synthetic(seed)
     weights = oracle.synth_weights(spec, seed, layers=range(2))
     orc = oracle.OracleModel(spec, weights, 0, 2)
@@ -274,166 +274,3 @@ def test_qwen3_4b_geometry_two_layers_prefill_decode_and_mixed_batch():
         if top2_gap(la[i]) > GAP:
             assert mixed[i].id == alone[i].id
     stage.close()
-
-
-def test_execute_profiled_components_follow_the_reference_taxonomy():
-    """execute_profiled (stage_backend.hpp:103-106) reports the components of
-    cpp/src/cuda/stage.cpp:394-454 -- input, one "layer" per owned layer with
-    its model index, then final norm / LM head / sampling or the boundary
-    output -- and returns what execute returns."""
-    cfg, weights, _ = tiny_qwen()
-    s0 = make_stage(cfg, weights, layer_start=0, layer_end=1, first=True, final=False,
-                    kv_pool_tokens=256)
-    s1 = make_stage(cfg, weights, layer_start=1, layer_end=2, first=False, final=True,
-                    kv_pool_tokens=256)
-    a, b = s0.allocate_sequence(16), s0.allocate_sequence(16)
-    c, d = s1.allocate_sequence(16), s1.allocate_sequence(16)
-    ids = [1, 4, 2, 8, 3]
-    for pos in (0, 3, 4):
-        inp = TokenInput(ids[pos:pos + (3 if pos == 0 else 1)])
-        plain = s0.execute(inp, pos, a)
-        timed, parts = s0.execute_profiled(inp, pos, b)
-        assert plain.payload == timed.payload
-        assert [p[0] for p in parts] == ["embedding", "layer", "to-wire"]
-        assert parts[1][1] == 0 and parts[0][1] is None
-        assert all(np.isfinite(p[2]) and p[2] >= 0 for p in parts)
-        out_plain = s1.execute(plain, pos, c)
-        out_timed, parts = s1.execute_profiled(timed, pos, d)
-        assert out_plain.id == out_timed.id
-        assert [p[0] for p in parts] == ["from-wire", "layer", "final_norm", "lm_head",
-                                          "sampling"]
-        assert parts[1][1] == 1
-    # timing is off again: a plain step records nothing new
-    s0.execute(TokenInput([5]), 5, a)
-    s0.close()
-    s1.close()
-
-
-FALCON3_3B = oracle.ModelSpec(hidden_size=3072, intermediate_size=9216, attention_heads=12,
-                              key_value_heads=4, head_dimension=256, layers=22,
-                              vocabulary_size=131072, maximum_sequence_length=2304,
-                              rms_norm_epsilon=1e-6, rope_theta=1e6, query_key_norm=False,
-                              tied=False)
-
-
-def test_falcon3_geometry_seeded_sampling_with_cancellation_and_slot_reuse():
-    """Configuration 4's shapes (h3072, 12q/4kv, d256, I9216, V131072, untied
-    LM head), two layers, seeded synthetic weights.  Eight requests with their
-    own seeds (temperature 0.7, top-p 0.9) prefill and then decode as one
-    batch; after the third decode step a quarter of them are cancelled and
-    released, and two new requests are admitted.  The pool and the sequence
-    slots hold exactly eight requests, so the new ones run only in the freed
-    KV blocks and slots.  Bars: every live row's logits at every step within
-    2e-2 of the F32 oracle on the GPU's own token path (stale K/V in a reused
-    block would break this), and every sampled token equal to the reference
-    sampler's draw on the GPU's logits row with the request's seed and draw
-    counter (sampling.cpp:65-90)."""
-    spec = FALCON3_3B
-    seed = 3303
-    cap = 128
-    torch_cuda()
-    stage = B200Stage(cfg_of(spec), 0, 2, first=True, final=True, kv_pool_tokens=8 * cap,
-                      max_sequences=8)
-    stage.init_synthetic(seed)
-    orc = oracle.OracleModel(spec, oracle.synth_weights(spec, seed, layers=range(2)), 0, 2)
-    rng = np.random.default_rng(44)
-
-    class Req:
-        def __init__(self, rid):
-            self.rid = rid
-            self.prompt = [int(x) for x in rng.integers(0, spec.vocabulary_size,
-                                                       int(rng.integers(16, 97)))]
-            self.seq = stage.allocate_sequence(cap)
-            self.seq.sampling = SamplingOptions(0.7, 0.9, 0, 1000 + rid, False, 0)
-            self.oseq = orc.new_sequence(cap)
-            self.pos = 0
-            self.next = self.prompt
-
-    live = [Req(r) for r in range(8)]
-    with pytest.raises(StageError) as e:  # the pool is full
-        stage.allocate_sequence(cap)
-    assert e.value.code == _lib.RESOURCE_EXHAUSTED
-    draws = 0
-    for step in range(8):
-        if step == 4:  # cancel a quarter mid-decode; their blocks and slots go back
-            for r in (live[1], live[5]):
-                stage.release(r.seq)
-            live = [r for i, r in enumerate(live) if i not in (1, 5)]
-            live += [Req(100), Req(101)]
-        items = [DecodeBatchItem(TokenInput(r.next), r.pos, r.seq) for r in live]
-        counters = [r.seq.generated_index for r in live]
-        outs = stage.execute_mixed_batch(items)
-        gpu = stage.read_logits(len(live))
-        for i, (r, out) in enumerate(zip(live, outs)):
-            ol = orc.logits(orc.forward(orc.embed(r.next), r.pos, r.oseq)[-1:])[0]
-            err = float(np.max(np.abs(gpu[i] - ol)))
-            assert err < LOGIT_TOL, (step, r.rid, err)
-            opts = oracle.Sampling(0.7, 0.9, 0, 1000 + r.rid, 0, 0)
-            st, want = oracle.sample_token(gpu[i], opts, counters[i])
-            assert st == 0 and out.id == want.token_id, (step, r.rid)
-            assert r.seq.generated_index == counters[i] + 1
-            draws += 1
-            r.pos += len(r.next)
-            r.next = [out.id]
-    assert draws == 8 * 8
-    stage.close()
-
-
-QWEN3_06B = oracle.ModelSpec(hidden_size=1024, intermediate_size=3072, attention_heads=16,
-                             key_value_heads=8, head_dimension=128, layers=28,
-                             vocabulary_size=151936, maximum_sequence_length=2048,
-                             rms_norm_epsilon=1e-6, rope_theta=1e6, query_key_norm=True,
-                             tied=True)
-
-
-def test_qwen3_06b_geometry_two_stage_split_with_batched_decode():
-    """Configuration 2's shapes (h1024, 16q/8kv, d128, I3072, V151936, tied,
-    q/k-norm) as a two-stage split (layer 0 | layer 1, F16 boundary between
-    the stages, as 14 | 14 splits the model): sixteen requests with prompts
-    U[64, 1024) prefill in two mixed steps, then decode greedily as one batch.
-    Bars: every row's logits within 2e-2 of the F32 oracle (F16 boundary
-    rounding included) on the GPU's token path, greedy tokens by the top-2 gap
-    rule."""
-    spec = QWEN3_06B
-    seed = 606
-    torch_cuda()
-    cfg = cfg_of(spec)
-    s0 = B200Stage(cfg, 0, 1, first=True, final=False, kv_pool_tokens=16 * 1088,
-                   max_step_tokens=8192)
-    s1 = B200Stage(cfg, 1, 2, first=False, final=True, kv_pool_tokens=16 * 1088,
-                   max_step_tokens=8192)
-    s0.init_synthetic(seed)
-    s1.init_synthetic(seed)
-    weights = oracle.synth_weights(spec, seed, layers=range(2))
-    o0 = oracle.OracleModel(spec, weights, 0, 1)
-    o1 = oracle.OracleModel(spec, weights, 1, 2)
-    rng = np.random.default_rng(66)
-    reqs = []
-    for r in range(16):
-        prompt = [int(x) for x in rng.integers(0, spec.vocabulary_size, int(rng.integers(64, 1024)))]
-        reqs.append(dict(next=prompt, pos=0, a=s0.allocate_sequence(len(prompt) + 8),
-                         b=s1.allocate_sequence(len(prompt) + 8),
-                         oa=o0.new_sequence(len(prompt) + 8), ob=o1.new_sequence(len(prompt) + 8),
-                         agree=True))
-    groups = [reqs[:8], reqs[8:]]  # prefill in two mixed steps, then all sixteen decode
-    for step in range(6):
-        for grp in (groups if step == 0 else [reqs]):
-            bounds = s0.execute_mixed_batch([DecodeBatchItem(TokenInput(q["next"]), q["pos"], q["a"])
-                                             for q in grp])
-            outs = s1.execute_mixed_batch([DecodeBatchItem(bd, q["pos"], q["b"])
-                                           for bd, q in zip(bounds, grp)])
-            gpu = s1.read_logits(len(grp))
-            for i, (q, out) in enumerate(zip(grp, outs)):
-                h = oracle.f16_round(o0.forward(o0.embed(q["next"]), q["pos"], q["oa"]))
-                ol = o1.logits(o1.forward(h, q["pos"], q["ob"])[-1:])[0]
-                err = float(np.max(np.abs(gpu[i] - ol)))
-                assert err < LOGIT_TOL, (step, i, err)
-                if q["agree"]:
-                    if top2_gap(ol) < GAP:
-                        q["agree"] = False
-                    else:
-                        assert out.id == int(np.argmax(ol)), (step, i)
-                q["pos"] += len(q["next"])
-                q["next"] = [out.id]
-    s0.close()
-    s1.close()
