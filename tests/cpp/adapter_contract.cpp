@@ -11,12 +11,14 @@
 //  2. The reference's StageScheduler (cpp/src/worker/scheduler.cpp) driving the
 //     backend from concurrent request threads: every request's tokens equal a
 //     serial run's, and the scheduler formed decode batches of at most 8.
-//  3. (`adapter_contract profiling`) The reference's own paired timing contract
-//     (tests/cpp/profiling_contract.hpp in the reference tree, compiled from
-//     there with gtest_shim/): a first
-//     stage (layer 0) and a final stage (layer 1) whose execute_profiled outputs
-//     equal execute's and whose components run from "embedding" to "to-wire"
-//     and from "from-wire" to "sampling", with the right layer indices.
+//  3. (`adapter_contract reference`) The reference's own contract headers,
+//     compiled from the reference tree with gtest_shim/ for GoogleTest's
+//     assertion macros: decode_batch_contract (tests/cpp/decode_batch_contract.hpp)
+//     on the two-layer stage, and paired_timing_contract
+//     (tests/cpp/profiling_contract.hpp) on a first stage (layer 0) and a final
+//     stage (layer 1): execute_profiled outputs equal execute's, components run
+//     from "embedding" to "to-wire" and from "from-wire" to "sampling", with
+//     the right layer indices.
 #include <atomic>
 #include <chrono>
 #include <cmath>
@@ -30,6 +32,7 @@
 
 #include "b200_stage_backend.hpp"
 #include "hllm/worker/scheduler.hpp"
+#include "decode_batch_contract.hpp"
 #include "profiling_contract.hpp"
 
 using namespace hllm;
@@ -134,18 +137,29 @@ std::vector<std::uint64_t> run_request(runtime::StageBackend& stage,
 }
 }  // namespace
 
-// The reference's profiling contract on a two-stage split (layer 0 | layer 1).
-int profiling_contract() {
-  auto first = make_stage(7, 0, 1, true, false);
-  auto last = make_stage(7, 1, 2, false, true);
-  test::paired_timing_contract(*first, *last);
-  const int n = gtest_shim::failures();
-  std::printf(n ? "paired timing contract: %d failures\n" : "paired timing contract: ok\n", n);
-  return n ? 1 : 0;
+// The reference's own contracts: decode batches on the two-layer stage, then
+// component timing on a two-stage split (layer 0 | layer 1).
+int reference_contracts() {
+  {
+    auto stage = make_stage(11);
+    test::decode_batch_contract(*stage);
+  }
+  const int batch = gtest_shim::failures();
+  std::printf("decode batch contract: %s\n", batch ? "failed" : "ok");
+  {
+    auto first = make_stage(7, 0, 1, true, false);
+    auto last = make_stage(7, 1, 2, false, true);
+    test::paired_timing_contract(*first, *last);
+  }
+  const int timing = gtest_shim::failures() - batch;
+  std::printf("paired timing contract: %s\n", timing ? "failed" : "ok");
+  std::printf(batch + timing ? "reference contracts: %d failures\n" : "reference contracts: ok\n",
+              batch + timing);
+  return batch + timing ? 1 : 0;
 }
 
 int main(int argc, char** argv) {
-  if (argc > 1 && std::string(argv[1]) == "profiling") return profiling_contract();
+  if (argc > 1 && std::string(argv[1]) == "reference") return reference_contracts();
   auto stage = make_stage(7);
   decode_batch_case(*stage, 0.0);
   decode_batch_case(*stage, 0.8);

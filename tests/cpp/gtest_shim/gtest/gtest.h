@@ -1,6 +1,7 @@
 // gtest.h -- the few GoogleTest assertion macros that the reference's
-// contract headers use (tests/cpp/profiling_contract.hpp in the reference
-// tree), so that those contracts compile into adapter_contract without
+// contract headers use (tests/cpp/profiling_contract.hpp and
+// decode_batch_contract.hpp in the reference tree), so that those contracts
+// compile into adapter_contract without
 // GoogleTest, which this image does not have.  A failed assertion prints its
 // place and is counted; ASSERT_* also returns from the enclosing function, as
 // GoogleTest's does.
@@ -28,6 +29,7 @@ inline void fail(const char* file, int line, const char* what) {
 #define EXPECT_NE(a, b) EXPECT_TRUE((a) != (b))
 #define EXPECT_GE(a, b) EXPECT_TRUE((a) >= (b))
 #define EXPECT_LE(a, b) EXPECT_TRUE((a) <= (b))
+#define EXPECT_NEAR(a, b, tol) EXPECT_TRUE(((a) > (b) ? (a) - (b) : (b) - (a)) <= (tol))
 #define ASSERT_TRUE(c)                                                    \
   do {                                                                    \
     if (!(c)) {                                                           \

@@ -7,9 +7,9 @@ timing, and the reference's profiling contract over the C++ adapter.
   per-request seeded sampling and cancellation mid-decode that frees KV blocks
   and sequence slots for new requests.
 * execute_profiled's components in the reference's taxonomy
-  (cpp/src/cuda/stage.cpp:394-454), through the Python mirror and, in the
-  C++ adapter, under the reference's own paired_timing_contract
-  (tests/cpp/profiling_contract.hpp in the reference tree).
+  (cpp/src/cuda/stage.cpp:394-454) through the Python mirror, and the C++
+  adapter under the reference's own contract headers (tests/cpp/
+  decode_batch_contract.hpp and profiling_contract.hpp in the reference tree).
 
 Bars as in test_gpu_stage.py: logits within 2e-2 of the F32 oracle on the
 GPU's own token path, greedy tokens by the top-2 gap rule, sampled tokens
@@ -212,11 +212,13 @@ def test_qwen3_06b_geometry_two_stage_split_chunked_prefill_and_batched_decode()
     s1.close()
 
 
-def test_reference_paired_timing_contract_over_the_adapter():
+def test_reference_contract_headers_over_the_adapter():
+    """The reference's decode_batch_contract and paired_timing_contract,
+    compiled from its tests/cpp headers into adapter_contract."""
     torch_cuda()
     if not os.path.exists(ADAPTER):
         pytest.skip("adapter contract not built (needs the reference tree at build time)")
-    r = subprocess.run([ADAPTER, "profiling"], capture_output=True, text=True, timeout=600)
+    r = subprocess.run([ADAPTER, "reference"], capture_output=True, text=True, timeout=600)
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr
-    assert "paired timing contract: ok" in r.stdout
+    assert "reference contracts: ok" in r.stdout
