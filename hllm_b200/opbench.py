@@ -1,6 +1,6 @@
 """Per-operator timing of the executor's kernels through the C ABI.
 
-    python -m hllm_b200.opbench [gemm|attn|prefill|envelope|all] [--ncu-gemm M,K,N,PAIR,EPI]
+    python -m hllm_b200.opbench [gemm|attn|prefill|envelope|c5|all] [--ncu-gemm M,K,N,PAIR,EPI]
                                  [--ncu-attn ROWS] [--ncu-prefill FIRST,COUNT]
 
 Times the projection GEMM at the Qwen3-4B shapes (decode width 16/64 tokens,
@@ -10,6 +10,8 @@ placed in a pool), with CUDA events on the current stream after warm-up.
 Inputs are far larger than L2 for the weight-streaming shapes.  `--ncu-gemm`
 runs three launches of one GEMM shape and `--ncu-attn` three of the decode
 attention over ROWS configuration-3-like contexts (for profiler captures).
+`c5` runs configuration 5 (decode attention and GEMVs at batch 1-256, each
+launch after an L2 flush) as a markdown table of HBM GB/s against the roof.
 `envelope` times the boundary wire codec (host encode/decode, and the
 envelope built from device memory when a GPU is present).
 Device memory comes from torch; all compute is libhllm_b200.so.
@@ -29,11 +31,32 @@ def _torch():
     return torch
 
 
-def ev_time(fn, iters=20, warm=3):
+_FLUSH = None
+
+
+def ev_time(fn, iters=20, warm=3, cold=False):
+    """Microseconds per call, with CUDA events on the current stream after
+    `warm` untimed calls.  cold=True writes a 512 MB buffer (4x L2) before
+    every call, outside the timed region, and times each call alone, so that
+    inputs smaller than L2 are read from HBM."""
+    global _FLUSH
     torch = _torch()
     for _ in range(warm):
         fn()
     torch.cuda.synchronize()
+    if cold:
+        if _FLUSH is None:
+            _FLUSH = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+        total = 0.0
+        for _ in range(iters):
+            _FLUSH.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            total += a.elapsed_time(b)
+        return total / iters * 1e3
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(iters):
@@ -43,7 +66,23 @@ def ev_time(fn, iters=20, warm=3):
     return a.elapsed_time(b) / iters * 1e3  # microseconds per call
 
 
-def gemm_case(m, k, n, pair=1, epi=0, bn=0, grid=0, iters=20):
+def hbm_peak():
+    """(GB/s, source) of the HBM roof: MEASURED_PEAKS.json when present."""
+    import json
+    import os
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            v = json.load(f).get("hbm_gbs")
+        if v:
+            return float(v), "measured"
+    except (OSError, ValueError):
+        pass
+    return 6650.0, "fallback"
+
+
+def gemm_case(m, k, n, pair=1, epi=0, bn=0, grid=0, iters=20, cold=False):
     torch = _torch()
     from . import _lib
     L = _lib.lib()
@@ -57,15 +96,16 @@ def gemm_case(m, k, n, pair=1, epi=0, bn=0, grid=0, iters=20):
     def fn():
         _lib.check(L.hllm_b200_gemm(W.data_ptr(), m, k, pair, m if pair == 2 else 0, X.data_ptr(),
                                     n, epi, Y.data_ptr(), m, bn, grid, stream))
-    us = ev_time(fn, iters)
+    us = ev_time(fn, iters, cold=cold)
     nbytes = rows * k * 2 + n * k * 2 + n * m * (4 if outdt == torch.float32 else 2)
     flops = 2 * rows * n * k
     print(f"gemm m={m} pair={pair} k={k} n={n} epi={epi}: {us:8.1f} us  "
           f"{nbytes / us / 1e3:8.1f} GB/s  {flops / us / 1e6:8.1f} TFLOP/s", flush=True)
+    gemm_case.last = (us, nbytes, flops)
     return us
 
 
-def attn_case(rows_ctx, hq=32, hkv=8, d=128, split=256, iters=10):
+def attn_case(rows_ctx, hq=32, hkv=8, d=128, split=256, iters=10, cold=False):
     """Decode attention over rows with the given contexts (one new token each)."""
     torch = _torch()
     from . import _lib
@@ -100,10 +140,11 @@ def attn_case(rows_ctx, hq=32, hkv=8, d=128, split=256, iters=10):
                                          *[t.data_ptr() for t in dv], R, int(cu_s[-1]), 0, hq,
                                          hkv, d, mb, split, out.data_ptr(), hq * d,
                                          status.data_ptr(), stream))
-    us = ev_time(fn, iters)
+    us = ev_time(fn, iters, cold=cold)
     nbytes = sum(rows_ctx) * hkv * d * 2 * 2 + R * hq * d * 4
     print(f"decode attention B={R} sum_ctx={sum(rows_ctx)} split={split}: {us:8.1f} us  "
           f"{nbytes / us / 1e3:8.1f} GB/s", flush=True)
+    attn_case.last = (us, nbytes)
     return us
 
 
@@ -146,6 +187,41 @@ def prefill_case(first, count, rows=1, hq=32, hkv=8, d=128, iters=10):
     print(f"prefill attention rows={rows} first={first} count={count}: {us:8.1f} us  "
           f"{flops / us / 1e6:8.1f} TFLOP/s", flush=True)
     return us
+
+
+def stage_split(rows_ctx, hkv=8, sm=148):
+    """The decode split size the stage picks (stage.cu plan_step): about 16
+    (row, kv head, split) items per SM, at least 64 keys, a multiple of 16."""
+    keys = sum(c for c in rows_ctx)
+    target = max(1, (16 * sm) // hkv)
+    return max(64, -(-(-(-keys // target)) // 16) * 16)
+
+
+def c5_sweep():
+    """Configuration 5: the isolated decode-attention and GEMV sweep at Qwen3-4B
+    layer shapes, each launch timed alone after an L2 flush, as achieved HBM
+    GB/s against the roof.  Contexts log-uniform in [128, 32768] (seeded), 16-token
+    pages randomly placed in a pool 1.2x the KV."""
+    peak, src = hbm_peak()
+    print(f"| kernel | shape | B | µs | GB/s | of {src} {peak:.0f} GB/s |")
+    print("| --- | --- | --- | --- | --- | --- |")
+    rng = np.random.default_rng(5)
+    for B in (1, 8, 32, 128, 256):
+        ctx = np.exp(rng.uniform(np.log(128), np.log(32768), B)).astype(int).tolist()
+        attn_case(ctx, split=stage_split(ctx), cold=True)
+        us, nbytes = attn_case.last
+        gbs = nbytes / us / 1e3
+        print(f"| decode attention | Σctx {sum(ctx)} | {B} | {us:.1f} | {gbs:.0f} | "
+              f"{gbs / peak:.1%} |", flush=True)
+    shapes = [("QKV", 6144, 2560, 1, 0), ("O", 2560, 4096, 1, 2), ("gate/up", 9728, 2560, 2, 3),
+              ("down", 2560, 9728, 1, 2), ("LM head", 151936, 2560, 1, 0)]
+    for B in (1, 8, 32, 128, 256):
+        for name, m, k, pair, epi in shapes:
+            gemm_case(m, k, B, pair, epi, cold=True)
+            us, nbytes, _ = gemm_case.last
+            gbs = nbytes / us / 1e3
+            print(f"| GEMV {name} | {m * pair}x{k} | {B} | {us:.1f} | {gbs:.0f} | "
+                  f"{gbs / peak:.1%} |", flush=True)
 
 
 def gemm_suite():
@@ -259,6 +335,8 @@ def main(argv):
         prefill_suite()
     if what in ("envelope", "all"):
         envelope_suite()
+    if what == "c5":
+        c5_sweep()
 
 
 if __name__ == "__main__":
