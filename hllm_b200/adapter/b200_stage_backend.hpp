@@ -17,6 +17,7 @@
 
 #include "hllm/runtime/stage_backend.hpp"
 #include "hllm_b200.h"
+#include "mixed_scheduler.hpp"
 
 namespace hllm::b200 {
 
@@ -33,7 +34,7 @@ struct B200Sequence final : runtime::SequenceState {
   ~B200Sequence() override;
 };
 
-class B200StageBackend final : public runtime::StageBackend {
+class B200StageBackend final : public runtime::StageBackend, public MixedBatchBackend {
  public:
   // Takes ownership of a finalized stage (hllm_b200_stage_create + weights +
   // hllm_b200_stage_finalize).
@@ -62,9 +63,9 @@ class B200StageBackend final : public runtime::StageBackend {
                                                       runtime::ExecutionTiming& timing) const override;
 
   // One pass over rows that may mix prefill chunks and decode tokens (the
-  // reference scheduler never forms such batches; an optional extension).
+  // reference scheduler never forms such batches; MixedStageScheduler does).
   std::vector<runtime::StageOutput> execute_mixed_batch(
-      std::vector<runtime::DecodeBatchItem> items) const;
+      std::vector<runtime::DecodeBatchItem> items) const override;
 
  private:
   std::vector<runtime::StageOutput> run(std::vector<runtime::DecodeBatchItem>& items) const;

@@ -11,7 +11,12 @@
 //  2. The reference's StageScheduler (cpp/src/worker/scheduler.cpp) driving the
 //     backend from concurrent request threads: every request's tokens equal a
 //     serial run's, and the scheduler formed decode batches of at most 8.
-//  3. (`adapter_contract reference`) The reference's own contract headers,
+//  3. (`adapter_contract mixed`) MixedStageScheduler
+//     (hllm_b200/adapter/mixed_scheduler.cpp) driving the backend from
+//     concurrent requests with chunked prompts: mixed prefill + decode passes
+//     form, and every request's greedy tokens equal a serial run's up to the
+//     first near-tie (top-2 logprob gap below 1e-2).
+//  4. (`adapter_contract reference`) The reference's own contract headers,
 //     compiled from the reference tree with gtest_shim/ for GoogleTest's
 //     assertion macros: decode_batch_contract (tests/cpp/decode_batch_contract.hpp)
 //     on the two-layer stage, and paired_timing_contract
@@ -32,6 +37,7 @@
 
 #include "b200_stage_backend.hpp"
 #include "hllm/worker/scheduler.hpp"
+#include "mixed_scheduler.hpp"
 #include "decode_batch_contract.hpp"
 #include "profiling_contract.hpp"
 
@@ -137,6 +143,108 @@ std::vector<std::uint64_t> run_request(runtime::StageBackend& stage,
 }
 }  // namespace
 
+// Concurrent requests with chunked prompts through MixedStageScheduler against
+// the same requests run serially.  Greedy, with the top two logprobs: where a
+// concurrent token differs from the serial one, the serial top-2 gap must be
+// below 1e-2 (batch-dependent rounding decides near-ties), and the request is
+// compared no further.
+struct Run {
+  std::vector<std::uint64_t> tokens;
+  std::vector<double> gaps;
+};
+
+Run run_chunked(runtime::StageBackend& stage, b200::MixedStageScheduler* scheduler,
+                const std::vector<std::uint64_t>& prompt, std::size_t chunk, int steps) {
+  std::atomic_bool cancelled{false};
+  auto state = stage.allocate_sequence(prompt.size() + steps);
+  state->sampling = {0.0, 1.0, 0, 0, true, 2};
+  const auto deadline = std::chrono::system_clock::now() + std::chrono::minutes(5);
+  Run run;
+  std::size_t position = 0;
+  std::vector<std::uint64_t> input;
+  auto pass = [&](std::vector<std::uint64_t> ids) {
+    return scheduler ? scheduler->execute(stage, runtime::TokenInput{std::move(ids)}, position,
+                                          *state, cancelled, deadline)
+                     : stage.execute(runtime::TokenInput{std::move(ids)}, position, *state,
+                                     cancelled);
+  };
+  while (position < prompt.size()) {
+    const std::size_t n = std::min(chunk, prompt.size() - position);
+    state->prefilling = position > 0;
+    state->prefill_only = position + n < prompt.size();
+    auto out = pass({prompt.begin() + static_cast<std::ptrdiff_t>(position),
+                     prompt.begin() + static_cast<std::ptrdiff_t>(position + n)});
+    position += n;
+    if (!state->prefill_only) input = {std::get<runtime::SampledToken>(out).id};
+    if (!state->prefill_only) {
+      const auto& t = std::get<runtime::SampledToken>(out);
+      run.tokens.push_back(t.id);
+      run.gaps.push_back(t.top_logprobs.size() == 2
+                             ? t.top_logprobs[0].logprob - t.top_logprobs[1].logprob
+                             : 1.0);
+    }
+  }
+  state->prefilling = false;
+  state->prefill_only = false;
+  for (int s = 0; s < steps; ++s) {
+    auto out = pass(input);
+    const auto& t = std::get<runtime::SampledToken>(out);
+    run.tokens.push_back(t.id);
+    run.gaps.push_back(t.top_logprobs.size() == 2
+                           ? t.top_logprobs[0].logprob - t.top_logprobs[1].logprob
+                           : 1.0);
+    position += 1;
+    input = {t.id};
+  }
+  return run;
+}
+
+int mixed_scheduler_contract() {
+  auto stage = make_stage(13);
+  const int requests = 8, steps = 12;
+  const std::size_t chunk = 64;
+  std::vector<std::vector<std::uint64_t>> prompts;
+  for (int r = 0; r < requests; ++r) {
+    std::vector<std::uint64_t> p;
+    for (int i = 0; i < 5 + 23 * r; ++i)
+      p.push_back(static_cast<std::uint64_t>((r * 977 + i * 31) % 4096));
+    prompts.push_back(p);
+  }
+  std::vector<Run> serial;
+  for (int r = 0; r < requests; ++r)
+    serial.push_back(run_chunked(*stage, nullptr, prompts[r], chunk, steps));
+  b200::MixedStageScheduler scheduler;
+  scheduler.configure(16, 128);
+  std::vector<Run> concurrent(requests);
+  std::vector<std::thread> threads;
+  for (int r = 0; r < requests; ++r)
+    threads.emplace_back(
+        [&, r] { concurrent[r] = run_chunked(*stage, &scheduler, prompts[r], chunk, steps); });
+  for (auto& t : threads) t.join();
+  int compared = 0;
+  for (int r = 0; r < requests; ++r) {
+    const auto& a = serial[r].tokens;
+    const auto& b = concurrent[r].tokens;
+    EXPECT(a.size() == b.size(), "request %d token count", r);
+    for (std::size_t i = 0; i < a.size() && i < b.size(); ++i) {
+      if (a[i] != b[i]) {
+        EXPECT(serial[r].gaps[i] < 1e-2, "request %d step %zu: tokens differ with top-2 gap %g",
+               r, i, serial[r].gaps[i]);
+        break;
+      }
+      ++compared;
+    }
+  }
+  const auto m = scheduler.metrics();
+  EXPECT(m.completed_steps > 0 && m.mixed_batches > 0, "no mixed pass formed");
+  std::printf("mixed: tokens compared=%d passes_with_several=%zu mixed=%zu largest=%zu\n",
+              compared, m.decode_batches, m.mixed_batches, m.largest_decode_batch);
+  std::printf(failures ? "mixed scheduler contract: %d failures\n"
+                       : "mixed scheduler contract: ok\n",
+              failures);
+  return failures ? 1 : 0;
+}
+
 // The reference's own contracts: decode batches on the two-layer stage, then
 // component timing on a two-stage split (layer 0 | layer 1).
 int reference_contracts() {
@@ -160,6 +268,7 @@ int reference_contracts() {
 
 int main(int argc, char** argv) {
   if (argc > 1 && std::string(argv[1]) == "reference") return reference_contracts();
+  if (argc > 1 && std::string(argv[1]) == "mixed") return mixed_scheduler_contract();
   auto stage = make_stage(7);
   decode_batch_case(*stage, 0.0);
   decode_batch_case(*stage, 0.8);

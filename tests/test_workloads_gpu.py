@@ -222,3 +222,16 @@ def test_reference_contract_headers_over_the_adapter():
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "reference contracts: ok" in r.stdout
+
+
+def test_mixed_scheduler_over_the_adapter():
+    """MixedStageScheduler (hllm_b200/adapter/mixed_scheduler.cpp) driving the
+    C++ adapter from concurrent requests with chunked prompts: mixed passes
+    form, and tokens equal serial runs up to the first near-tie."""
+    torch_cuda()
+    if not os.path.exists(ADAPTER):
+        pytest.skip("adapter contract not built (needs the reference tree at build time)")
+    r = subprocess.run([ADAPTER, "mixed"], capture_output=True, text=True, timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "mixed scheduler contract: ok" in r.stdout
