@@ -12,7 +12,8 @@ BINARY = os.path.join(ROOT, "_build", "mixed_scheduler_test")
 
 def test_mixed_scheduler_on_fake_backends():
     if not os.path.exists(BINARY):
-        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "tests", "cpp")], check=False)
+        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "tests", "cpp"), "scheduler"],
+                       check=False)
     if not os.path.exists(BINARY):
         pytest.skip("scheduler test not built (needs the reference tree)")
     r = subprocess.run([BINARY], capture_output=True, text=True, timeout=300)
