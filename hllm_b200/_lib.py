@@ -61,6 +61,12 @@ class BoundaryIdentity(C.Structure):
                 ("hidden_size", C.c_uint64)]
 
 
+class EnvelopeRow(C.Structure):
+    _fields_ = [("first_token", C.c_uint64), ("tokens", C.c_uint64),
+                ("identity", BoundaryIdentity), ("sequence", C.c_uint64),
+                ("position", C.c_uint64), ("prefill", C.c_uint32)]
+
+
 class ComponentTiming(C.Structure):
     _fields_ = [("component", C.c_char * 16), ("layer_index", C.c_int64),
                 ("milliseconds", C.c_double)]
@@ -123,6 +129,8 @@ def lib():
         "hllm_b200_stage_envelope": (C.c_int, [vp, u64, u64, C.POINTER(BoundaryIdentity), u64,
                                                u64, u32, vp, u64, C.POINTER(u64)]),
         "hllm_b200_stage_envelope_wait": (C.c_int, [vp]),
+        "hllm_b200_stage_envelopes": (C.c_int, [vp, C.POINTER(EnvelopeRow), u32, vp, u64,
+                                                C.POINTER(u64)]),
         "hllm_b200_stage_component_timing": (C.c_int, [vp, u32]),
         "hllm_b200_stage_components": (C.c_int, [vp, C.POINTER(ComponentTiming), u32,
                                                  C.POINTER(u32)]),

@@ -151,6 +151,27 @@ class B200Stage:
             check(lib().hllm_b200_stage_envelope_wait(self._h))
         return out.raw[:n.value]
 
+    def encode_boundaries(self, rows) -> list:
+        """Envelopes of several row ranges of the last step's boundary at once
+        (hllm_b200_stage_envelopes, one device->host copy): `rows` holds
+        (first_token, tokens, identity, sequence, position, prefill) tuples;
+        returns one serialized StageMessage per row range, in order."""
+        n = len(rows)
+        arr = (_lib.EnvelopeRow * max(1, n))()
+        keep = []
+        for i, (first, tokens, identity, sequence, position, prefill) in enumerate(rows):
+            ident = identity.c()
+            keep.append(ident)
+            arr[i] = _lib.EnvelopeRow(first, tokens, ident, sequence, position, int(prefill))
+        offsets = (C.c_uint64 * (n + 1))()
+        with self._lock:
+            check(lib().hllm_b200_stage_envelopes(self._h, arr, n, None, 0, offsets))
+            out = C.create_string_buffer(max(1, offsets[n]))
+            check(lib().hllm_b200_stage_envelopes(self._h, arr, n, out, offsets[n], offsets))
+            check(lib().hllm_b200_stage_envelope_wait(self._h))
+        raw = out.raw
+        return [raw[offsets[i]:offsets[i + 1]] for i in range(n)]
+
     def close(self):
         if self._h:
             lib().hllm_b200_stage_destroy(self._h)

@@ -197,6 +197,14 @@ struct hllm_b200_stage {
   cudaEvent_t step_done = nullptr, env_done = nullptr;
   bool env_pending = false;
   std::vector<std::pair<const uint8_t*, uint64_t>> env_payloads;
+  // Batched envelopes (hllm_b200_stage_envelopes): one device->host copy of the
+  // rows into pinned staging, placed into the messages at the next wait.
+  uint8_t* h_env = nullptr;
+  struct EnvPlace {
+    uint8_t* dst;
+    uint64_t src, bytes;  // offset into h_env, length
+  };
+  std::vector<EnvPlace> env_places;
 
   std::map<std::string, Target> targets;
   std::set<std::string> loaded;
@@ -265,6 +273,7 @@ struct hllm_b200_stage {
     }
     if (step_done) cudaEventDestroy(step_done);
     if (env_done) cudaEventDestroy(env_done);
+    if (h_env) cudaFreeHost(h_env);
     if (stream) {
       cudaStreamSynchronize(stream);
       cudaStreamDestroy(stream);
@@ -1386,24 +1395,111 @@ hllm_b200_status hllm_b200_stage_components(hllm_b200_stage* stage,
   });
 }
 
+namespace {
+hb::EnvelopeIdentity envelope_identity(const hllm_b200_boundary_identity& c) {
+  if (!c.deployment_id || !c.request_id) fail(HLLM_B200_INVALID_REQUEST, "null argument");
+  hb::EnvelopeIdentity id;
+  id.deployment_id = c.deployment_id;
+  id.deployment_version = c.deployment_version;
+  id.request_id = c.request_id;
+  id.maximum_tokens = c.maximum_tokens;
+  id.hidden_size = c.hidden_size;
+  return id;
+}
+
+void envelope_streams(hllm_b200_stage* s) {
+  if (s->copy_stream) return;
+  check_cuda(cudaStreamCreateWithFlags(&s->copy_stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  check_cuda(cudaEventCreateWithFlags(&s->step_done, cudaEventDisableTiming), "cudaEventCreate");
+  check_cuda(cudaEventCreateWithFlags(&s->env_done, cudaEventDisableTiming), "cudaEventCreate");
+}
+
+// Waits for the envelope copies in flight, places staged payloads into their
+// messages, and applies encode_tensor's finite check to every payload
+// (cpp/src/worker/boundary_codec.cpp:96-100).  Caller holds the mutex.
+void envelope_finish(hllm_b200_stage* s) {
+  if (!s->env_pending) return;
+  check_cuda(cudaSetDevice(s->device), "cudaSetDevice");
+  check_cuda(cudaEventSynchronize(s->env_done), "envelope copy");
+  std::vector<std::pair<const uint8_t*, uint64_t>> payloads;
+  payloads.swap(s->env_payloads);
+  std::vector<hllm_b200_stage::EnvPlace> places;
+  places.swap(s->env_places);
+  s->env_pending = false;
+  for (const auto& pl : places) {
+    std::memcpy(pl.dst, s->h_env + pl.src, pl.bytes);
+    payloads.emplace_back(pl.dst, pl.bytes);
+  }
+  for (const auto& [p, n] : payloads)
+    if (!hb::f16_payload_finite(p, n))
+      fail(HLLM_B200_INTERNAL, "backend returned a non-finite boundary activation");
+}
+}  // namespace
+
+hllm_b200_status hllm_b200_stage_envelopes(hllm_b200_stage* stage,
+                                           const hllm_b200_envelope_row* rows, uint32_t n,
+                                           uint8_t* out, uint64_t capacity, uint64_t* offsets) {
+  return guarded([&] {
+    if (!stage || !rows || !n || !offsets) fail(HLLM_B200_INVALID_REQUEST, "null argument");
+    std::scoped_lock lock(stage->mutex);
+    if (stage->desc.final) fail(HLLM_B200_INVALID_REQUEST, "a final stage has no boundary output");
+    const size_t row_bytes = stage->h * sizeof(__half);
+    std::vector<hb::EnvelopeLayout> layouts(n);
+    uint64_t total = 0, lo = UINT64_MAX, hi = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+      const auto& r = rows[i];
+      if (r.tokens == 0 || r.first_token > stage->last_tokens ||
+          r.tokens > stage->last_tokens - r.first_token)
+        fail(HLLM_B200_INVALID_REQUEST, "rows outside the last step's boundary");
+      std::string why;
+      const hllm_b200_status st =
+          hb::envelope_plan(envelope_identity(r.identity), r.sequence, r.position, r.prefill != 0,
+                            r.tokens * row_bytes, r.tokens, stage->h, &layouts[i], &why);
+      if (st != HLLM_B200_OK) fail(st, why);
+      offsets[i] = total;
+      total += layouts[i].total;
+      lo = std::min<uint64_t>(lo, r.first_token);
+      hi = std::max<uint64_t>(hi, r.first_token + r.tokens);
+    }
+    offsets[n] = total;
+    if (!out) return;  // size query
+    if (capacity < total) fail(HLLM_B200_INVALID_REQUEST, "output buffer too small");
+    // The staging holds one batch: finish the previous one first.
+    envelope_finish(stage);
+    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
+    envelope_streams(stage);
+    if (!stage->h_env)
+      check_cuda(cudaMallocHost(&stage->h_env, stage->T_max * row_bytes), "cudaMallocHost");
+    for (uint32_t i = 0; i < n; ++i) {
+      const auto& r = rows[i];
+      hb::envelope_write_frame(envelope_identity(r.identity), r.sequence, r.position,
+                               r.prefill != 0, r.tokens, stage->h, out + offsets[i]);
+    }
+    check_cuda(cudaEventRecord(stage->step_done, stage->stream), "envelope order");
+    check_cuda(cudaStreamWaitEvent(stage->copy_stream, stage->step_done, 0), "envelope order");
+    check_cuda(cudaMemcpyAsync(stage->h_env + lo * row_bytes, stage->bout + lo * stage->h,
+                               (hi - lo) * row_bytes, cudaMemcpyDeviceToHost, stage->copy_stream),
+               "envelope copy");
+    check_cuda(cudaEventRecord(stage->env_done, stage->copy_stream), "envelope order");
+    stage->env_pending = true;
+    for (uint32_t i = 0; i < n; ++i)
+      stage->env_places.push_back({out + offsets[i] + layouts[i].payload_offset,
+                                   rows[i].first_token * row_bytes, rows[i].tokens * row_bytes});
+  });
+}
+
 hllm_b200_status hllm_b200_stage_envelope(hllm_b200_stage* stage, uint64_t first_token,
                                           uint64_t tokens,
                                           const hllm_b200_boundary_identity* identity,
                                           uint64_t sequence, uint64_t position, uint32_t prefill,
                                           uint8_t* out, uint64_t capacity, uint64_t* written) {
   return guarded([&] {
-    if (!stage || !identity || !identity->deployment_id || !identity->request_id || !written)
-      fail(HLLM_B200_INVALID_REQUEST, "null argument");
+    if (!stage || !identity || !written) fail(HLLM_B200_INVALID_REQUEST, "null argument");
     std::scoped_lock lock(stage->mutex);
     if (stage->desc.final) fail(HLLM_B200_INVALID_REQUEST, "a final stage has no boundary output");
     if (tokens == 0 || first_token > stage->last_tokens || tokens > stage->last_tokens - first_token)
       fail(HLLM_B200_INVALID_REQUEST, "rows outside the last step's boundary");
-    hb::EnvelopeIdentity id;
-    id.deployment_id = identity->deployment_id;
-    id.deployment_version = identity->deployment_version;
-    id.request_id = identity->request_id;
-    id.maximum_tokens = identity->maximum_tokens;
-    id.hidden_size = identity->hidden_size;
+    const hb::EnvelopeIdentity id = envelope_identity(*identity);
     const uint64_t bytes = tokens * stage->h * sizeof(__half);
     hb::EnvelopeLayout layout;
     std::string why;
@@ -1414,14 +1510,7 @@ hllm_b200_status hllm_b200_stage_envelope(hllm_b200_stage* stage, uint64_t first
     if (!out) return;  // size query
     if (capacity < layout.total) fail(HLLM_B200_INVALID_REQUEST, "output buffer too small");
     check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
-    if (!stage->copy_stream) {
-      check_cuda(cudaStreamCreateWithFlags(&stage->copy_stream, cudaStreamNonBlocking),
-                 "cudaStreamCreate");
-      check_cuda(cudaEventCreateWithFlags(&stage->step_done, cudaEventDisableTiming),
-                 "cudaEventCreate");
-      check_cuda(cudaEventCreateWithFlags(&stage->env_done, cudaEventDisableTiming),
-                 "cudaEventCreate");
-    }
+    envelope_streams(stage);
     hb::envelope_write_frame(id, sequence, position, prefill != 0, tokens, stage->h, out);
     check_cuda(cudaEventRecord(stage->step_done, stage->stream), "envelope order");
     check_cuda(cudaStreamWaitEvent(stage->copy_stream, stage->step_done, 0), "envelope order");
@@ -1438,15 +1527,7 @@ hllm_b200_status hllm_b200_stage_envelope_wait(hllm_b200_stage* stage) {
   return guarded([&] {
     if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
     std::scoped_lock lock(stage->mutex);
-    if (!stage->env_pending) return;
-    check_cuda(cudaSetDevice(stage->device), "cudaSetDevice");
-    check_cuda(cudaEventSynchronize(stage->env_done), "envelope copy");
-    std::vector<std::pair<const uint8_t*, uint64_t>> payloads;
-    payloads.swap(stage->env_payloads);
-    stage->env_pending = false;
-    for (const auto& [p, n] : payloads)
-      if (!hb::f16_payload_finite(p, n))  // cpp/src/worker/boundary_codec.cpp:96-100
-        fail(HLLM_B200_INTERNAL, "backend returned a non-finite boundary activation");
+    envelope_finish(stage);
   });
 }
 

@@ -251,8 +251,31 @@ hllm_b200_status hllm_b200_stage_envelope(hllm_b200_stage* stage, uint64_t first
                                           const hllm_b200_boundary_identity* identity,
                                           uint64_t sequence, uint64_t position, uint32_t prefill,
                                           uint8_t* out, uint64_t capacity, uint64_t* written);
-/* Waits for the envelope copies issued since the last wait, then applies
- * encode_tensor's finite check to their payloads (INTERNAL if one fails). */
+/* One row range of the last step's boundary to encode, for
+ * hllm_b200_stage_envelopes. */
+typedef struct hllm_b200_envelope_row {
+  uint64_t first_token;
+  uint64_t tokens;
+  hllm_b200_boundary_identity identity;
+  uint64_t sequence;
+  uint64_t position;
+  uint32_t prefill;
+} hllm_b200_envelope_row;
+
+/* The envelopes of `n` row ranges at once, e.g. one per request of a decode
+ * batch (no reference counterpart; each message is what encode_tensor makes
+ * for its row).  Messages are written back to back into `out`; message i
+ * occupies [offsets[i], offsets[i + 1]) (offsets has n + 1 entries; with
+ * out == NULL only offsets are filled).  The rows' payloads go device->host in
+ * one copy into pinned staging and are placed into the messages by
+ * hllm_b200_stage_envelope_wait; `out` must stay valid until then.  A second
+ * call finishes the previous batch first. */
+hllm_b200_status hllm_b200_stage_envelopes(hllm_b200_stage* stage,
+                                           const hllm_b200_envelope_row* rows, uint32_t n,
+                                           uint8_t* out, uint64_t capacity, uint64_t* offsets);
+/* Waits for the envelope copies issued since the last wait, places batched
+ * payloads into their messages, then applies encode_tensor's finite check to
+ * every payload (INTERNAL if one fails). */
 hllm_b200_status hllm_b200_stage_envelope_wait(hllm_b200_stage* stage);
 
 /* Host->device and device->host bytes the last step copied. */

@@ -35,10 +35,31 @@ def test_status_codes_mirror_reference_error_codes():
             _lib.DEADLINE_EXCEEDED, _lib.CANCELLED, _lib.INTERNAL) == (1, 2, 3, 4, 5, 6)
 
 
-def test_structs_match_header_layout():
-    assert C.sizeof(_lib.Sampling) == 40
-    assert C.sizeof(_lib.Sampled) == 8 + 8 + 4 + 4 + 40 + 40
-    assert C.sizeof(_lib.Row) == 8 * 5 + 8 + 40 + 8
+def test_structs_match_header_layout(tmp_path):
+    """The ctypes mirrors have the C header's sizes and field offsets (gcc)."""
+    structs = {"hllm_b200_sampling": _lib.Sampling, "hllm_b200_sampled": _lib.Sampled,
+               "hllm_b200_row": _lib.Row, "hllm_b200_stage_desc": _lib.StageDesc,
+               "hllm_b200_boundary_identity": _lib.BoundaryIdentity,
+               "hllm_b200_envelope_row": _lib.EnvelopeRow,
+               "hllm_b200_component_timing": _lib.ComponentTiming}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{_lib.HEADER}"',
+             'int main(void) {']
+    for cname, cls in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ['  return 0;', '}']
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    r = subprocess.run(["gcc", "-std=c11", str(src), "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    got = {tuple(line.split()[:2]): int(line.split()[2]) for line in out if line}
+    for cname, cls in structs.items():
+        assert got[(cname, "size")] == C.sizeof(cls), cname
+        for field, _ in cls._fields_:
+            assert got[(cname, field)] == getattr(cls, field).offset, (cname, field)
 
 
 def test_no_cpu_fallback_without_gpu():

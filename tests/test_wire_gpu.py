@@ -131,3 +131,30 @@ def test_b200_worker_to_cpu_worker_over_the_wire():
             inp = [tok]
         s0.release(a)
     s0.close()
+
+
+def test_batched_envelopes_equal_per_row_host_encodings():
+    """hllm_b200_stage_envelopes: one device->host copy for all rows of a
+    decode batch, each message equal to encode_tensor of its row."""
+    cfg, s0, s1 = _stages()
+    prompts = [[1, 4, 2, 8, 3], [5, 6], [7], [9, 9, 9]]
+    seqs = [s0.allocate_sequence(16) for _ in prompts]
+    outs = s0.execute_mixed_batch([DecodeBatchItem(TokenInput(p), 0, q)
+                                   for p, q in zip(prompts, seqs)])
+    idents = [BoundaryIdentity("plan-1", 1, f"request-{i}" * (i + 1), 64, cfg.hidden_size)
+              for i in range(len(prompts))]
+    rows, off = [], 0
+    for p, ident in zip(prompts, idents):
+        rows.append((off, len(p), ident, 0, 0, False))
+        off += len(p)
+    got = s0.encode_boundaries(rows)
+    assert got == [encode_tensor(o, ident, 0, 0) for o, ident in zip(outs, idents)]
+    # one decode step later: sequence number 1, decode phase, one row each
+    outs = s0.execute_mixed_batch([DecodeBatchItem(TokenInput([3]), len(p), q)
+                                   for p, q in zip(prompts, seqs)])
+    got = s0.encode_boundaries([(i, 1, ident, 1, len(p), False)
+                                for i, (p, ident) in enumerate(zip(prompts, idents))])
+    assert got == [encode_tensor(o, ident, 1, len(p))
+                   for o, ident, p in zip(outs, idents, prompts)]
+    s0.close()
+    s1.close()
