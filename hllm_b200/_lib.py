@@ -132,6 +132,7 @@ def lib():
         "hllm_b200_stage_envelopes": (C.c_int, [vp, C.POINTER(EnvelopeRow), u32, vp, u64,
                                                 C.POINTER(u64)]),
         "hllm_b200_stage_component_timing": (C.c_int, [vp, u32]),
+        "hllm_b200_stage_memory": (C.c_int, [vp] + [C.POINTER(u64)] * 5),
         "hllm_b200_stage_components": (C.c_int, [vp, C.POINTER(ComponentTiming), u32,
                                                  C.POINTER(u32)]),
         "hllm_b200_seq_read_kv": (C.c_int, [vp, vp, u64, u32, C.POINTER(C.c_uint16)]),

@@ -151,6 +151,14 @@ class B200Stage:
             check(lib().hllm_b200_stage_envelope_wait(self._h))
         return out.raw[:n.value]
 
+    def memory(self) -> dict:
+        """Device bytes (hllm_b200_stage_memory): weights, workspace, kv_pool,
+        kv_in_use, kv_peak -- what BackendFactory::allocator_metrics reports."""
+        v = [C.c_uint64() for _ in range(5)]
+        check(lib().hllm_b200_stage_memory(self._h, *[C.byref(x) for x in v]))
+        return dict(zip(("weights", "workspace", "kv_pool", "kv_in_use", "kv_peak"),
+                        (x.value for x in v)))
+
     def encode_boundaries(self, rows) -> list:
         """Envelopes of several row ranges of the last step's boundary at once
         (hllm_b200_stage_envelopes, one device->host copy): `rows` holds

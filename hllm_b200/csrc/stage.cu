@@ -145,6 +145,7 @@ struct hllm_b200_stage {
   hb::GemmWeight g_head{};
   __half* kv = nullptr;  // [layers][2][blocks][Hkv][16][d]
   size_t kv_layer_elems = 0;
+  size_t kv_peak_blocks = 0;  // most pool blocks ever held by live sequences
   float* rope_pow = nullptr;
   float2* rope_table = nullptr;  // [max positions][d/2] (cos, sin)
   int rope_positions = 0;
@@ -1138,6 +1139,23 @@ hllm_b200_status hllm_b200_stage_info(const hllm_b200_stage* stage, uint64_t* we
   });
 }
 
+hllm_b200_status hllm_b200_stage_memory(hllm_b200_stage* stage, uint64_t* weights,
+                                        uint64_t* workspace, uint64_t* kv_pool,
+                                        uint64_t* kv_in_use, uint64_t* kv_peak) {
+  return guarded([&] {
+    if (!stage) fail(HLLM_B200_INVALID_REQUEST, "null stage");
+    std::scoped_lock lock(stage->mutex);
+    const uint64_t block = static_cast<uint64_t>(std::max<size_t>(1, stage->n_layers)) * 2 *
+                           stage->hkv * hb::kBlockTokens * stage->dim * sizeof(__half);
+    const uint64_t used = stage->num_blocks - stage->free_blocks.size();
+    if (weights) *weights = stage->weight_bytes;
+    if (workspace) *workspace = stage->workspace_bytes - stage->num_blocks * block;
+    if (kv_pool) *kv_pool = stage->num_blocks * block;
+    if (kv_in_use) *kv_in_use = used * block;
+    if (kv_peak) *kv_peak = stage->kv_peak_blocks * block;
+  });
+}
+
 hllm_b200_status hllm_b200_sequence_memory(const hllm_b200_stage* stage, uint64_t tokens,
                                            uint64_t maximum_query_tokens,
                                            uint64_t* cache_device_bytes,
@@ -1192,6 +1210,8 @@ hllm_b200_status hllm_b200_seq_alloc(hllm_b200_stage* stage, uint64_t tokens, hl
     check_cuda(cudaEventRecord(done, stage->stream), "slot staging");
     stage->free_slots.pop_back();
     stage->free_blocks.resize(stage->free_blocks.size() - need);
+    stage->kv_peak_blocks = std::max(stage->kv_peak_blocks,
+                                     stage->num_blocks - stage->free_blocks.size());
     stage->live.insert(seq.get());
     *out = seq.release();
   });

@@ -133,6 +133,15 @@ hllm_b200_status hllm_b200_stage_info(const hllm_b200_stage* stage, uint64_t* we
                                       uint64_t* hidden_size, uint64_t* vocabulary_size,
                                       uint64_t* maximum_tokens);
 
+/* Device bytes of the stage, for BackendFactory::allocator_metrics
+ * (cpp/include/hllm/runtime/backend_factory.hpp:24-26, 33-35): weights, the
+ * step workspace, the paged KV pool, the pool bytes held by live sequences
+ * now, and the most they ever held.  All device memory is allocated when the
+ * stage is created; nothing is cached or freed during steps. */
+hllm_b200_status hllm_b200_stage_memory(hllm_b200_stage* stage, uint64_t* weights,
+                                        uint64_t* workspace, uint64_t* kv_pool,
+                                        uint64_t* kv_in_use, uint64_t* kv_peak);
+
 /* StageBackend::sequence_memory (stage_backend.hpp:80-81; SequenceMemory
  * memory.hpp:46-49): device bytes a sequence of `tokens` positions holds for
  * its life (whole 16-token KV blocks over this stage's layers), and the shared

@@ -235,3 +235,24 @@ def test_mixed_scheduler_over_the_adapter():
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "mixed scheduler contract: ok" in r.stdout
+
+
+def test_stage_memory_tracks_kv_blocks():
+    """hllm_b200_stage_memory (BackendFactory::allocator_metrics): the KV bytes
+    held by live sequences follow allocation and release in whole 16-token
+    blocks, and the peak stays."""
+    cfg, weights, _ = tiny_qwen()
+    s = make_stage(cfg, weights, kv_pool_tokens=256)
+    m0 = s.memory()
+    assert m0["weights"] > 0 and m0["workspace"] > 0 and m0["kv_in_use"] == 0
+    block = m0["kv_pool"] // (256 // 16)
+    a = s.allocate_sequence(40)  # 3 blocks
+    b = s.allocate_sequence(16)  # 1 block
+    m1 = s.memory()
+    assert m1["kv_in_use"] == 4 * block and m1["kv_peak"] == 4 * block
+    s.release(a)
+    m2 = s.memory()
+    assert m2["kv_in_use"] == block and m2["kv_peak"] == 4 * block
+    assert m2["weights"] == m0["weights"] and m2["kv_pool"] == m0["kv_pool"]
+    s.release(b)
+    s.close()
