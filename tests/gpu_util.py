@@ -1,6 +1,5 @@
 """Shared helpers for the GPU tests: device tensors (torch is plumbing only)
 and calls through the C ABI."""
-import ctypes as C
 
 import numpy as np
 import pytest
