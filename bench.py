@@ -501,6 +501,18 @@ def ours(args, world, rank, local):
               generated, prof, clock_info, cpu, parallelism="single stage")
 
 
+WORKLOAD = ("configuration 3: Qwen3-4B architecture with seeded random-init F16 weights "
+            "(F32 accumulate), 64 concurrent requests, prompts lognormal(512, 1.0) in "
+            "[32, 4096], outputs U[64, 512], 512-token chunks mixed into decode batches, greedy")
+
+
+def workload_config(world, parallelism, fast_forward):
+    """The `config` object both arms report."""
+    return {"workload": WORKLOAD, "global_batch": MAX_ACTIVE * world, "seq_len": 4608,
+            "parallelism": parallelism, "fast_forward_steps": fast_forward,
+            "l2": "inputs larger than L2: 8.0 GB of weights and the KV cache stream every step"}
+
+
 def emit_line(args, world, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d_step, d2h_step,
               ttft, generated, prof, clock_info, cpu, parallelism):
     """Prints the benchmark's JSON line (rank 0)."""
@@ -538,14 +550,7 @@ def emit_line(args, world, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d
                for k, v in prof.items()}
     value = dev_tokens / (dev_ms / 1e3)
     e2e_value = e2e_tokens / (e2e_ms / 1e3)
-    config = {"workload": "configuration 3: Qwen3-4B, 64 concurrent requests, prompts "
-                          "lognormal(512, 1.0) in [32, 4096], outputs U[64, 512], 512-token "
-                          "chunks mixed into decode batches, greedy",
-              "model": "Qwen3-4B-architecture random init (seeded), F16 weights, F32 accumulate",
-              "global_batch": MAX_ACTIVE * world, "seq_len": 4608,
-              "parallelism": parallelism,
-              "fast_forward_steps": args.fast_forward,
-              "l2": "inputs larger than L2: 8.0 GB of weights and the KV cache stream every step"}
+    config = workload_config(world, parallelism, args.fast_forward)
     if world > 1:
         config["microbatches"] = world
         config["timed_microbatch_steps"] = steps_timed
@@ -840,10 +845,10 @@ def reference(args, world, rank):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "configuration 3 (Qwen3-4B), bounded CPU sample",
-                       "model": "Qwen3-4B-architecture random init (seeded)",
-                       "parallelism": f"{threads} CPU threads, one decode stream each (the "
-                                      f"reference CPU stage is single-threaded)"},
+            "config": workload_config(
+                world, f"reference CPU math on {threads} host threads, one decode stream each "
+                       f"(the reference CPU stage is single-threaded); a bounded sample of the "
+                       f"workload, see cpu_baseline.sample", args.fast_forward),
             "cpu_baseline": {"value": round(value, 5), "unit": "tokens/s", "cores": threads,
                              "kind": ref.kind,
                              "sample": f"each step one decode token through one Qwen3-4B "
