@@ -11,6 +11,7 @@ forms).  Every computation runs in libhllm_b200.so on the GPU.
 from __future__ import annotations
 
 import ctypes as C
+import itertools
 import threading
 from dataclasses import dataclass, field
 from typing import Optional, Sequence, Union
@@ -74,6 +75,25 @@ class SamplingOptions:
     seed: int = 0
     return_logprobs: bool = False
     top_logprobs: int = 0
+
+
+def _dtype_of(ctype):
+    """numpy dtype with the memory layout of a ctypes scalar, pointer or
+    Structure (field offsets and size taken from the ctypes mirror)."""
+    if isinstance(ctype, type) and issubclass(ctype, C.Structure):
+        names = [f for f, _ in ctype._fields_]
+        return np.dtype({"names": names,
+                         "formats": [_dtype_of(t) for _, t in ctype._fields_],
+                         "offsets": [getattr(ctype, f).offset for f in names],
+                         "itemsize": C.sizeof(ctype)})
+    if ctype is C.c_void_p or (isinstance(ctype, type) and issubclass(ctype, C._Pointer)):
+        return np.dtype(np.uintp)
+    return np.dtype(ctype)
+
+
+_ROW = _dtype_of(_lib.Row)
+_SAMPLING = _dtype_of(_lib.Sampling)
+_SAMPLED = _dtype_of(_lib.Sampled)
 
 
 @dataclass
@@ -356,67 +376,35 @@ class B200Stage:
                 if _is_cancelled(it.cancelled):
                     raise StageError(_lib.CANCELLED, "request cancelled")
         n = len(items)
-        rows = (_lib.Row * n)()
-        keep = []
-        total = 0
-        for i, it in enumerate(items):
-            s = it.sequence
-            if s is None or s.owner is not self or not s.handle:
-                raise StageError(_lib.INVALID_REQUEST, "sequence state or position is invalid")
-            r = rows[i]
-            r.sequence = s.handle
-            r.first_position = it.position
-            if isinstance(it.input, TokenInput):
-                if not self.first:
-                    raise StageError(_lib.INVALID_REQUEST, "only stage zero accepts tokens")
-                ids = np.asarray(it.input.ids, np.uint64)
-                if ids.size == 0:
-                    raise StageError(_lib.INVALID_REQUEST, "invalid stage input")
-                keep.append(ids)
-                r.tokens = ids.size
-                r.token_ids = ids.ctypes.data_as(C.POINTER(C.c_uint64))
-            else:
-                if self.first:
-                    raise StageError(_lib.INVALID_REQUEST, "stage zero requires tokens")
-                b = it.input
-                if (b.width != self.config.hidden_size or b.tokens == 0
-                        or len(b.payload) != b.tokens * b.width * 2):
-                    raise StageError(_lib.INVALID_REQUEST, "invalid boundary activation")
-                act = np.frombuffer(b.payload, dtype=np.uint16)
-                keep.append(act)
-                r.tokens = b.tokens
-                r.activations = act.ctypes.data_as(C.POINTER(C.c_uint16))
-            total += r.tokens
-            sampling = self.final and not s.prefill_only
-            r.sample = int(sampling)
-            o = s.sampling
-            r.sampling = _lib.Sampling(o.temperature, o.top_p, o.top_k, o.seed,
-                                       int(o.return_logprobs), o.top_logprobs)
-            r.generated_index = s.generated_index
-        n_samples = sum(1 for i in range(n) if rows[i].sample)
-        sampled = (_lib.Sampled * max(1, n_samples))()
+        rows, keep, tokens = self._build_rows(items)
+        total = int(tokens.sum())
+        samples = rows["sample"]
+        n_samples = int(samples.sum())
+        sampled = np.zeros(max(1, n_samples), _SAMPLED)
         boundary = None
         if not self.final:
             boundary = np.empty(total * self.config.hidden_size, np.uint16)
         with self._lock:
             check(lib().hllm_b200_step(
-                self._h, rows, n, sampled,
+                self._h, rows.ctypes.data_as(C.POINTER(_lib.Row)), n,
+                sampled.ctypes.data_as(C.POINTER(_lib.Sampled)),
                 boundary.ctypes.data_as(C.POINTER(C.c_uint16)) if boundary is not None else None))
         outputs = []
         if self.final:
+            ids = sampled["token_id"].tolist()
             k = 0
             for i, it in enumerate(items):
-                if not rows[i].sample:
+                if not samples[i]:
                     outputs.append(PrefillProgress())
                     continue
-                res = sampled[k]
-                k += 1
                 o = it.sequence.sampling
-                tok = SampledToken(int(res.token_id))
+                tok = SampledToken(ids[k])
                 if o.return_logprobs:
-                    tok.logprob = float(res.logprob)
-                    tok.top_logprobs = [(int(res.top_ids[j]), float(res.top_logprobs[j]))
-                                        for j in range(res.n_top)]
+                    res = sampled[k]
+                    tok.logprob = float(res["logprob"])
+                    tok.top_logprobs = [(int(res["top_ids"][j]), float(res["top_logprobs"][j]))
+                                        for j in range(int(res["n_top"]))]
+                k += 1
                 # The greedy fast path does not consume a draw (cpp/src/cpu/stage.cpp:165-166).
                 if not (o.temperature == 0.0 and not o.return_logprobs):
                     it.sequence.generated_index += 1
@@ -424,14 +412,71 @@ class B200Stage:
         else:
             off = 0
             h = self.config.hidden_size
-            for i in range(n):
-                t = rows[i].tokens
+            for t in tokens.tolist():
                 outputs.append(BoundaryActivation(t, h, boundary[off * h:(off + t) * h].tobytes()))
                 off += t
         for it in items:
             if _check_cancel_all and _is_cancelled(it.cancelled):
                 raise StageError(_lib.CANCELLED, "request cancelled")
         return outputs
+
+    def _build_rows(self, items):
+        """The step's hllm_b200_row array (numpy, the C struct's layout), the
+        host buffers its pointers reference, and each row's token count.  One
+        Python pass reads the items; columns are then filled at once."""
+        n = len(items)
+        first, final = self.first, self.final
+        handles, positions, counts, samples, draws, options = [], [], [], [], [], []
+        id_lists, id_rows, acts = [], [], []
+        for i, it in enumerate(items):
+            s = it.sequence
+            if s is None or s.owner is not self or not s.handle:
+                raise StageError(_lib.INVALID_REQUEST, "sequence state or position is invalid")
+            inp = it.input
+            if isinstance(inp, TokenInput):
+                if not first:
+                    raise StageError(_lib.INVALID_REQUEST, "only stage zero accepts tokens")
+                k = len(inp.ids)
+                if k == 0:
+                    raise StageError(_lib.INVALID_REQUEST, "invalid stage input")
+                id_lists.append(inp.ids)
+                id_rows.append(i)
+            else:
+                if first:
+                    raise StageError(_lib.INVALID_REQUEST, "stage zero requires tokens")
+                if (inp.width != self.config.hidden_size or inp.tokens == 0
+                        or len(inp.payload) != inp.tokens * inp.width * 2):
+                    raise StageError(_lib.INVALID_REQUEST, "invalid boundary activation")
+                k = inp.tokens
+                acts.append((i, np.frombuffer(inp.payload, dtype=np.uint16)))
+            handles.append(s.handle)
+            positions.append(it.position)
+            counts.append(k)
+            samples.append(final and not s.prefill_only)
+            o = s.sampling
+            options.append((o.temperature, o.top_p, o.top_k, o.seed, int(o.return_logprobs),
+                            o.top_logprobs))
+            draws.append(s.generated_index)
+        rows = np.zeros(n, _ROW)
+        tokens = np.asarray(counts, np.uint64)
+        rows["sequence"] = handles
+        rows["first_position"] = positions
+        rows["tokens"] = tokens
+        rows["sample"] = samples
+        rows["sampling"] = np.array(options, _SAMPLING)
+        rows["generated_index"] = draws
+        keep = []
+        if id_lists:
+            sizes = tokens[id_rows]
+            flat = np.fromiter(itertools.chain.from_iterable(id_lists), np.uint64,
+                               count=int(sizes.sum()))
+            starts = np.concatenate(([0], np.cumsum(sizes)[:-1])).astype(np.uint64)
+            rows["token_ids"][id_rows] = flat.ctypes.data + 8 * starts
+            keep.append(flat)
+        for i, a in acts:
+            rows["activations"][i] = a.ctypes.data
+            keep.append(a)
+        return rows, keep, tokens
 
     # ----------------------------------------------------------- test trace
     def read_kv(self, state: SequenceState, layer: int, values: bool) -> np.ndarray:
