@@ -101,3 +101,68 @@ def test_row_errors_match():
     with pytest.raises(StageError):  # payload size disagrees with the shape
         st2._build_rows([DecodeBatchItem(BoundaryActivation(2, CFG.hidden_size, bytes(128)), 0,
                                          SequenceState(handle=3, capacity=8, owner=st2))])
+
+
+class _FakeLib:
+    """Stands in for libhllm_b200's step call: checks the rows it receives and
+    writes known results, as the library does."""
+
+    def __init__(self):
+        self.calls = []
+
+    def hllm_b200_step(self, handle, rows_ptr, n, sampled_ptr, boundary_ptr):
+        rows = C.cast(rows_ptr, C.POINTER(_lib.Row))
+        k = 0
+        total = 0
+        for i in range(n):
+            r = rows[i]
+            total += r.tokens
+            if r.sample:
+                res = C.cast(sampled_ptr, C.POINTER(_lib.Sampled))[k]
+                res.token_id = 1000 + i
+                res.logprob = -0.25 * (i + 1)
+                res.has_logprob = 1
+                res.n_top = 3
+                for j in range(3):
+                    res.top_ids[j] = 10 * i + j
+                    res.top_logprobs[j] = -float(j)
+                k += 1
+        if boundary_ptr:
+            buf = C.cast(boundary_ptr, C.POINTER(C.c_uint16))
+            for e in range(total * CFG.hidden_size):
+                buf[e] = e % 65000
+        self.calls.append((n, k, total))
+        return 0
+
+
+def test_outputs_read_back_from_the_step(monkeypatch):
+    import threading
+    from hllm_b200 import backend
+    fake = _FakeLib()
+    monkeypatch.setattr(backend, "lib", lambda: fake)
+    st = _stage()
+    st._lock, st._h = threading.Lock(), C.c_void_p(1)
+    greedy = SequenceState(handle=1, capacity=64, owner=st)
+    hot = SequenceState(handle=2, capacity=64, owner=st)
+    hot.sampling = SamplingOptions(0.7, 0.9, 0, 5, True, 3)
+    mid = SequenceState(handle=3, capacity=64, owner=st, prefill_only=True)
+    outs = st.execute_mixed_batch([DecodeBatchItem(TokenInput([1]), 4, greedy),
+                                   DecodeBatchItem(TokenInput([2, 3]), 0, mid),
+                                   DecodeBatchItem(TokenInput([7]), 9, hot)])
+    assert fake.calls == [(3, 2, 4)]
+    assert outs[0].id == 1000 and outs[0].logprob is None
+    assert outs[1] == backend.PrefillProgress()
+    assert outs[2].id == 1002 and outs[2].logprob == -0.75
+    assert outs[2].top_logprobs == [(20, 0.0), (21, -1.0), (22, -2.0)]
+    assert (greedy.generated_index, hot.generated_index, mid.generated_index) == (0, 1, 0)
+    # a non-final stage returns each row's slice of the boundary
+    st2 = _stage(first=True, final=False)
+    st2._lock, st2._h = threading.Lock(), C.c_void_p(1)
+    a = SequenceState(handle=4, capacity=64, owner=st2)
+    b = SequenceState(handle=5, capacity=64, owner=st2)
+    outs = st2.execute_mixed_batch([DecodeBatchItem(TokenInput([1, 2]), 0, a),
+                                    DecodeBatchItem(TokenInput([3]), 0, b)])
+    h = CFG.hidden_size
+    flat = (np.arange(3 * h) % 65000).astype(np.uint16)
+    assert outs[0].tokens == 2 and outs[0].payload == flat[:2 * h].tobytes()
+    assert outs[1].tokens == 1 and outs[1].payload == flat[2 * h:].tobytes()
