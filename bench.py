@@ -266,6 +266,7 @@ def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, cl
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     greedy = _lib.Sampling(0.0, 1.0, 0, 0, 0, 0)
     tokens = launches = 0
+    step_events, step_rows = [], []
     for i, (admits, rows, fin) in enumerate(steps):
         if i == first_timed:
             _lib.check(L.hllm_b200_stage_sync(stage.handle))
@@ -290,6 +291,10 @@ def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, cl
         if i >= first_timed:
             tokens += sum(r[2] for r in rows)
             launches += int(L.hllm_b200_stage_last_launches(stage.handle))
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(stream)
+            step_events.append(ev)
+            step_rows.append(([(r[1], r[2], r[3]) for r in rows], all(r[4] for r in rows)))
         for rid in fin:
             stage.release(seqs.pop(rid))
     end.record(stream)
@@ -305,6 +310,8 @@ def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, cl
         _lib.check(L.hllm_b200_stage_profile(stage.handle, 0))
     for s in seqs.values():
         stage.release(s)
+    marks = [start] + step_events
+    run_device_phase.last_steps = (step_rows, [a.elapsed_time(b) for a, b in zip(marks, marks[1:])])
     return ms, tokens, launches, prof, clock_info
 
 
@@ -473,6 +480,7 @@ def ours(args, world, rank, local):
     dev_ms, dev_tokens, launches, _, clock_info = run_device_phase(
         stage, cfg, trace, steps, first_timed, K, clocks=clocks,
         profiler_range=args.profiler_range)
+    dev_steps = run_device_phase.last_steps
     if args.device_phase_only:
         print(json.dumps({"device_phase_ms_per_step": round(dev_ms / K, 4),
                           "tokens_per_s": round(dev_tokens / (dev_ms / 1e3), 1),
@@ -497,8 +505,10 @@ def ours(args, world, rank, local):
                           f"({t_head:.3f} s per round), -O2 -ffp-contract=off; extrapolated as "
                           f"36 layers + {GEN_FRACTION:.3f} LM-head rows per token"),
                "host_cores": host_cores()}
+    hbm, _, tf_sust, _ = peaks()
+    phases = phase_summary(*dev_steps, hbm, tf_sust)
     emit_line(args, 1, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d, d2h, ttft,
-              generated, prof, clock_info, cpu, parallelism="single stage")
+              generated, prof, clock_info, cpu, parallelism="single stage", phases=phases)
 
 
 WORKLOAD = ("configuration 3: Qwen3-4B architecture with seeded random-init F16 weights "
@@ -514,7 +524,7 @@ def workload_config(world, parallelism, fast_forward):
 
 
 def emit_line(args, world, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d_step, d2h_step,
-              ttft, generated, prof, clock_info, cpu, parallelism):
+              ttft, generated, prof, clock_info, cpu, parallelism, phases=None):
     """Prints the benchmark's JSON line (rank 0)."""
     K = args.steps
     steps_timed = K * world  # micro-batch steps completed in the timed region
@@ -564,7 +574,8 @@ def emit_line(args, world, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d
                 "ms_per_step": round(e2e_ms / steps_timed, 4)},
         "ttft_p50_ms": round(statistics.median(ttft), 3) if ttft else None,
         "output_tokens_per_s_e2e": round(generated / (e2e_ms / 1e3), 1),
-        "roofline": roof, "kernels": kernels, "cpu_baseline": cpu, "clocks": clock_info,
+        "roofline": roof, "kernels": kernels, "phases": phases, "cpu_baseline": cpu,
+        "clocks": clock_info,
         "gpu_launches": int(launches),
     }
     print(json.dumps(line), flush=True)
@@ -578,6 +589,59 @@ def qwen_stage_bytes():
     q, kv = Q["attention_heads"] * d, Q["key_value_heads"] * d
     layer = 2.0 * (h * (q + 2 * kv) + q * h + 2 * i * h + i * h)
     return layer, 2.0 * Q["vocabulary_size"] * h
+
+
+def step_work(rows, layers=None):
+    """Algorithmic work of one Qwen3-4B step from its rows (first position,
+    token count, samples): (bytes, FLOPs).
+
+    bytes follow the decode-step formula: every owned layer's weights, the LM
+    head, each row's K/V context read, the new K/V written, and the hidden
+    rows in and out.  FLOPs follow the prefill formula: 2 x layer parameters
+    per token, causal attention 4 x Hq x d per (token, key) pair per layer,
+    and 2 x V x h per sampled row."""
+    from hllm_b200.workload import QWEN3_4B as Q
+    L = Q["layers"] if layers is None else layers
+    h, d = Q["hidden_size"], Q["head_dimension"]
+    hq, hkv, V = Q["attention_heads"], Q["key_value_heads"], Q["vocabulary_size"]
+    layer_bytes, head_bytes = qwen_stage_bytes()
+    kv_token = 2 * hkv * d * 2  # K and V, F16, one layer
+    nbytes = L * layer_bytes + head_bytes
+    flops = 0.0
+    for first, count, sample in rows:
+        keys = sum(first + j + 1 for j in range(count))  # causal (query, key) pairs
+        nbytes += L * kv_token * (first + count) + L * kv_token * count + count * h * 2 * 2
+        flops += (layer_bytes / 2.0) * 2.0 * L * count + 4.0 * hq * d * L * keys
+        if sample:
+            flops += 2.0 * V * h
+    return nbytes, flops
+
+
+def phase_summary(steps, step_ms, hbm_gbs, tflops):
+    """Decode-only steps against the HBM roof, steps carrying a prefill chunk
+    against the tensor roof: {phase: steps, ms per step, tokens/s, achieved,
+    frac}.  steps: per step (rows, decode_only) with rows as for step_work."""
+    out = {}
+    for name, decode in (("decode", True), ("prefill", False)):
+        picked = [(rows, ms) for (rows, only), ms in zip(steps, step_ms) if only == decode]
+        if not picked:
+            continue
+        ms = sum(m for _, m in picked)
+        tokens = sum(c for rows, _ in picked for _, c, _ in rows)
+        nbytes = sum(step_work(rows)[0] for rows, _ in picked)
+        flops = sum(step_work(rows)[1] for rows, _ in picked)
+        entry = {"steps": len(picked), "ms_per_step": round(ms / len(picked), 4),
+                 "tokens_per_s": round(tokens / (ms / 1e3), 1)}
+        if decode:
+            achieved = nbytes / (ms / 1e3) / 1e9
+            entry.update(bound="hbm", achieved=round(achieved, 1), unit="GB/s",
+                         frac=round(achieved / hbm_gbs, 4))
+        else:
+            achieved = flops / (ms / 1e3) / 1e12
+            entry.update(bound="tensor", achieved=round(achieved, 1), unit="TFLOP/s",
+                         frac=round(achieved / tflops, 4))
+        out[name] = entry
+    return out
 
 
 def pipeline_ranges(world: int):
