@@ -39,39 +39,15 @@ def partition_layers(n_layers: int, n_stages: int, layer_bytes: float,
     """Contiguous ranges [(start, end)] of `n_layers` layers over `n_stages`
     stages that minimise the most bytes any stage streams per step: a stage
     costs (its layers) x `layer_bytes`, plus `head_bytes` on the last stage.
-    Every stage gets at least one layer; among equal optima the earlier
-    stages take the extra layers."""
-    if n_stages < 1 or n_layers < n_stages:
-        raise ValueError(f"cannot split {n_layers} layers over {n_stages} stages")
-    # Smallest cap (in layers) for the first n_stages - 1 stages such that the
-    # rest fits: with uniform layers the optimum is max(ceil(rest / (N-1)), ...).
-    best = None
-    for last in range(1, n_layers - n_stages + 2):
-        rest = n_layers - last
-        if n_stages == 1:
-            if rest:
-                continue
-            cap = 0
-        else:
-            cap = -(-rest // (n_stages - 1))
-            if cap < 1:
-                continue
-        cost = max(cap * layer_bytes, last * layer_bytes + head_bytes)
-        if best is None or cost < best[0] - 1e-9 * max(1.0, abs(cost)):
-            best = (cost, last, cap)
-    _, last, cap = best
-    ranges, start = [], 0
-    rest = n_layers - last
-    for s in range(n_stages - 1):
-        # distribute `rest` layers over the first N-1 stages, at most `cap` each,
-        # earlier stages first, keeping at least one layer for each later stage
-        left = n_stages - 1 - s - 1
-        take = min(cap, rest - left)
-        ranges.append((start, start + take))
-        start += take
-        rest -= take
-    ranges.append((start, n_layers))
-    return ranges
+    Every stage gets at least one layer; among equal optima the most even
+    split wins, then the one whose earlier stages are longer
+    (``hllm_b200.planner.split_costs``, which also plans from a manifest's
+    per-layer bytes)."""
+    from .planner import split_costs
+
+    return split_costs(0, n_layers, n_stages,
+                       lambda g, s, e: (e - s) * layer_bytes +
+                       (head_bytes if g == n_stages - 1 else 0.0))
 
 
 def stage_bytes(ranges: Sequence[Tuple[int, int]], layer_bytes: float,
