@@ -37,7 +37,7 @@ import math
 from dataclasses import dataclass
 from typing import Any, Callable, List, Mapping, Optional, Tuple
 
-__all__ = ["DTYPE_BYTES", "PlanningError", "Tensor", "ModelShape", "usable_bytes",
+__all__ = ["DTYPE_BYTES", "PlanningError", "NoFeasibleSplit", "Tensor", "ModelShape", "usable_bytes",
            "stage_weight_bytes", "stage_memory", "stream_bytes", "split_costs",
            "split_stage", "plan_worker", "ranges_of"]
 
@@ -54,6 +54,10 @@ _STATE = "ARCHITECTURE_STATE"
 
 class PlanningError(ValueError):
     """Inconsistent planner inputs (the reference's PlanningError, planner.py:37)."""
+
+
+class NoFeasibleSplit(PlanningError):
+    """Every split of the stage leaves some GPU over its memory budget."""
 
 
 def _get(obj: Any, name: str, default: Any = None) -> Any:
@@ -286,7 +290,7 @@ def split_costs(lo: int, hi: int, parts: int,
                              for e in ends(g, s)), default=inf)
     opt = suf[0][lo]
     if opt == inf:
-        raise PlanningError("no split of the stage fits every GPU")
+        raise NoFeasibleSplit("no split of the stage fits every GPU")
     cap = opt + abs(opt) * 1e-12
     # Pass 2, sq[g][s]: the least sum of squares of parts g.. with every cost <= cap.
     sq = [[inf] * (hi + 1) for _ in range(parts + 1)]
@@ -375,12 +379,14 @@ def plan_worker(shape: ModelShape, worker: Any, workload: Any, gpus: int, *,
         raise PlanningError(f"stage layers [{lo}, {hi}) outside the model's {shape.num_layers}")
     if hi - lo < gpus:
         raise PlanningError(f"cannot split {hi - lo} layers over {gpus} GPUs")
+    if objective not in ("stream", "pressure"):
+        raise PlanningError(f"unknown objective {objective!r}")
     mem = _Memory(shape, worker, workload, execution_dtype, weight_dtype)
     try:
         ranges = split_stage(shape, worker, workload, gpus, assignment=assignment,
                              objective=objective, execution_dtype=execution_dtype,
                              weight_dtype=weight_dtype, kv_tokens=kv_tokens)
-    except PlanningError:
+    except NoFeasibleSplit:
         # Nothing fits: show the split that comes closest.
         first_owner = bool(a["owns_token_embedding"])
         final_owner = bool(a["owns_lm_head"] or a["owns_final_norm"])

@@ -60,7 +60,7 @@ def test_pressure_split_on_two_gpus_is_the_reference_selection(gold):
     for c in gold["cases"]:
         shape = shape_of(gold, c["model"])
         if c["selected"] is None:
-            with pytest.raises(P.PlanningError):
+            with pytest.raises(P.NoFeasibleSplit):
                 P.split_stage(shape, c["worker"], c["workload"], 2, objective="pressure")
             continue
         k = c["selected"]["split_layer"]
@@ -181,6 +181,8 @@ def test_planner_input_errors(gold):
                                   "owns_lm_head": True, "owns_sampling": True})
     with pytest.raises(P.PlanningError):
         P.split_stage(shape, c["worker"], c["workload"], 2, objective="latency")
+    with pytest.raises(P.PlanningError):
+        P.plan_worker(shape, c["worker"], c["workload"], 2, objective="latency")
     homeless = {**c["worker"], "primary_memory_domain": "UNIFIED"}
     with pytest.raises(P.PlanningError):
         P.stage_memory(shape, homeless, c["workload"], start=0, end=4, is_first=True,
