@@ -94,6 +94,54 @@ def test_restatement_equals_reference_bit_for_bit_on_tiny_llama_pipeline():
             inp = [tok]
 
 
+# The attention geometry of the benchmark configurations, on small hidden and
+# vocabulary sizes: C2 (16q/8kv, d 128, q/k-norm, tied), C3 (32q/8kv, d 128,
+# q/k-norm, tied), C4 (12q/4kv: G = 3, d 256, no q/k-norm, untied).
+GEOMETRIES = {
+    "c2": dict(attention_heads=16, key_value_heads=8, head_dimension=128, query_key_norm=True,
+               tied=True),
+    "c3": dict(attention_heads=32, key_value_heads=8, head_dimension=128, query_key_norm=True,
+               tied=True),
+    "c4": dict(attention_heads=12, key_value_heads=4, head_dimension=256, query_key_norm=False,
+               tied=False),
+}
+
+
+@pytest.mark.parametrize("name", sorted(GEOMETRIES))
+def test_restatement_equals_reference_layers_at_config_geometries(name):
+    """Two layers of the C restatement against the reference's own
+    transformer_layer and final_logits (oracle/_ref, built from
+    cpp/src/cpu/llama.cpp): a 37-token prefill, then three decode tokens;
+    every layer output, every logit and both layers' K/V caches equal bit
+    for bit."""
+    if oracle.ref() is None:
+        pytest.skip("oracle/_ref not built")
+    spec = oracle.ModelSpec(hidden_size=256, intermediate_size=512, layers=2,
+                            vocabulary_size=640, maximum_sequence_length=4096,
+                            rms_norm_epsilon=1e-6, rope_theta=1e6, **GEOMETRIES[name])
+    weights = oracle.synth_weights(spec, 77)
+    ours = oracle.OracleModel(spec, weights)
+    theirs = oracle.OracleModel(spec, weights, use_ref=True)
+    a, b = ours.new_sequence(64), theirs.new_sequence(64)
+    rng = np.random.default_rng(len(name))
+    inp, pos = [int(x) for x in rng.integers(0, spec.vocabulary_size, 37)], 0
+    for _ in range(4):
+        ta, tb = [], []
+        ha = ours.forward(ours.embed(inp), pos, a, trace=ta)
+        hb = theirs.forward(theirs.embed(inp), pos, b, trace=tb)
+        for x, y in zip(ta, tb):
+            assert np.array_equal(x, y)
+        la, lb = ours.logits(ha[-1:]), theirs.logits(hb[-1:])
+        assert np.array_equal(la, lb)
+        pos += len(inp)
+        inp = [oracle.greedy(la)]
+    for layer in range(spec.layers):  # the caches hold the same K and V
+        for x, y in zip(ours.kv(a, layer), theirs.kv(b, layer)):
+            assert x.shape == (pos, spec.key_value_heads, spec.head_dimension)
+            assert np.array_equal(x, y)
+    theirs.free_sequence(b)
+
+
 def test_restatement_equals_reference_functions():
     r = oracle.ref()
     if r is None:
