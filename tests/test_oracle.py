@@ -174,6 +174,42 @@ def test_restatement_equals_reference_functions():
         assert (fa == fb) or (math.isnan(fa) and math.isnan(fb))
 
 
+def test_sampler_restatement_equals_reference_at_full_vocabulary():
+    """oracle.sample_token against the reference's own sample_token
+    (cpp/src/sampling.cpp:19-90, in oracle/_ref) on full-vocabulary rows of the
+    benchmark models: configuration 4's seeded T 0.7 / top-p 0.9 draws over many
+    draw counters, greedy, top-k with logprobs and top-5 logprobs, and rows with
+    tied maxima.  Tokens, logprobs and top lists are equal exactly."""
+    r = oracle.ref()
+    if r is None:
+        pytest.skip("oracle/_ref not built")
+    rng = np.random.default_rng(11)
+    opts = [oracle.sampling(0.7, 0.9, 0, 1000 + i) for i in range(4)] + [
+        oracle.sampling(),
+        oracle.sampling(0.0, 1.0, 0, 0, True, 5),
+        oracle.sampling(1.0, 1.0, 40, 7, True, 5),
+        oracle.sampling(1.3, 0.5, 0, 9, True, 2),
+        oracle.sampling(0.7, 0.9, 100, 123, True, 0)]
+    for V in (131072, 151936):
+        rows = [rng.standard_normal(V).astype(np.float32) * 3]
+        tied = rng.standard_normal(V).astype(np.float32)
+        tied[[5, 77, V - 1]] = tied.max() + 1.0  # three equal maxima
+        rows.append(tied)
+        rows.append(np.round(rng.standard_normal(V) * 2).astype(np.float32))  # many ties
+        for lg in rows:
+            for o in opts:
+                for gi in (0, 1, 17):
+                    st_a, a = oracle.sample_token(lg, o, gi)
+                    b = oracle.Sampled()
+                    st_b = r.ref_sample_token(oracle.fp(lg), V, C.byref(o), gi, C.byref(b))
+                    assert st_a == st_b == 0
+                    assert a.token_id == b.token_id
+                    assert (a.has_logprob, a.n_top) == (b.has_logprob, b.n_top)
+                    assert a.logprob == b.logprob
+                    assert list(a.top_ids[:a.n_top]) == list(b.top_ids[:b.n_top])
+                    assert list(a.top_logprobs[:a.n_top]) == list(b.top_logprobs[:b.n_top])
+
+
 def test_rms_norm_hand_calculation():
     out = oracle.rms_norm(np.float32([[3.0, 4.0]]), np.float32([1.0, 2.0]), 1e-6)
     inv = 1.0 / math.sqrt(12.5 + 1e-6)
