@@ -196,3 +196,32 @@ def test_manifest_json_form_reads_like_the_compact_one(gold):
                          "shape": [n], "dtype": "F16"}
                         for i, (role, layer, n) in enumerate(compact["tensors"])]}
     assert P.ModelShape.from_manifest(full) == P.ModelShape.from_manifest(compact)
+
+
+def test_object_inputs_read_like_dicts(gold):
+    """The reference's pydantic models (ModelManifest, WorkerProfile,
+    WorkloadProfile, StageAssignment) are read by attribute, their StrEnum
+    fields by value: the same plan as from the JSON forms."""
+    from types import SimpleNamespace as NS
+
+    class Role:  # a StrEnum member stand-in: compared by .value
+        def __init__(self, v):
+            self.value = v
+
+    compact = gold["models"]["falcon3_3b"]
+    manifest = NS(config=NS(**compact["config"]),
+                  tensors=[NS(role=Role(r), layer_index=li, num_elements=n)
+                           for r, li, n in compact["tensors"]])
+    c = case(gold, "falcon3_3b", "b200", "batch-64")
+    worker = NS(**{**c["worker"], "primary_memory_domain": Role("DEVICE"),
+                   "memory_budgets": [NS(**{**b, "domain": Role(b["domain"])})
+                                      for b in c["worker"]["memory_budgets"]]})
+    workload = NS(**{**c["workload"], "kv_dtype": Role("F16"), "activation_dtype": Role("F16")})
+    stage = NS(stage_index=1, worker_id="b200", layer_start=11, layer_end=22,
+               owns_token_embedding=False, owns_final_norm=True, owns_lm_head=True,
+               owns_sampling=True)
+    shape = P.ModelShape.from_manifest(manifest)
+    assert shape == shape_of(gold, "falcon3_3b")
+    a = P.plan_worker(shape, worker, workload, 2, assignment=stage)
+    b = P.plan_worker(shape, c["worker"], c["workload"], 2, assignment=vars(stage))
+    assert a == b and a["feasible"]
