@@ -165,7 +165,7 @@ PAIRS = [("qwen3_4b", "b200", "interactive"), ("qwen3_4b", "b200", "batch64"),
 def main(reference: Path) -> None:
     sys.path.insert(0, str(reference / "python"))
     sys.modules["hllm_control.proto.control_pb2_grpc"] = types.ModuleType("control_pb2_grpc")
-    from hllm_control.models import (DTYPE_BYTES, DType, PlannerSettings, WorkerProfile,
+    from hllm_control.models import (DTYPE_BYTES, PlannerSettings, WorkerProfile,
                                      WorkloadProfile)
     from hllm_control.planner import planner as P
     from hllm_control.prepare.manifest import prepare_model
