@@ -72,14 +72,19 @@ def _free_port():
         return sk.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_q):
+def _rank_main(rank, world, port, out_q, fail_at=None, pg_timeout_s=None):
+    """One pipeline rank over gloo.  `fail_at` = (rank, tick) makes that rank
+    raise at the start of that tick (a host-side failure); every rank reports
+    an exception as ("error", rank, text) on `out_q`."""
+    import datetime
     import torch.distributed as dist
     import oracle
     from hllm_b200.pipeline import HostLinks, Schedule, partition_layers, run_ticks
     from tests.golden.make_golden import C1, C1_SEED, c1_workload
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    kw = {"timeout": datetime.timedelta(seconds=pg_timeout_s)} if pg_timeout_s else {}
+    dist.init_process_group("gloo", rank=rank, world_size=world, **kw)
     try:
         steps = 32
         lo, hi = partition_layers(C1.layers, world, 1.0)[rank]
@@ -96,6 +101,8 @@ def _rank_main(rank, world, port, out_q):
         sched = Schedule(world, steps)
 
         def tick(t, m, j):
+            if fail_at == (rank, t):
+                raise RuntimeError(f"injected failure on rank {rank} at tick {t}")
             reqs = mbs[m]
             if rank == 0 and j > 0:
                 fed = links.recv_tokens(len(reqs)) if world > 1 else np.asarray(
@@ -126,8 +133,12 @@ def _rank_main(rank, world, port, out_q):
             if world > 1 and j + 1 < steps:
                 links.send_tokens(ids)
 
-        run_ticks(sched, rank, tick)
-        links.drain()
+        try:
+            run_ticks(sched, rank, tick)
+            links.drain()
+        except Exception as e:  # noqa: BLE001 -- reported to the parent, then re-raised
+            out_q.put(("error", rank, repr(e)))
+            raise
         if rank == world - 1:
             out_q.put(tokens)
     finally:
@@ -196,3 +207,41 @@ def test_four_rank_pipeline_over_gloo_matches_the_in_process_run():
 def test_two_rank_pipeline_over_gloo_matches_the_reference_two_stage_run():
     g = np.load(os.path.join(GOLD, "tiny_llama_pipeline.npz"))
     np.testing.assert_array_equal(_run_ranks(2), g["tokens"])
+
+
+@pytest.mark.timeout(300)
+def test_a_failing_rank_ends_the_others_with_an_error_not_a_hang():
+    """Rank 1 of three raises at tick 4 (a host-side failure between its
+    exchanges).  Its neighbours learn of it at their next exchange with it:
+    the receive fails (the peer closed its connection, or the process group's
+    10 s timeout ran out) and each surviving rank exits with its own error
+    well inside the limit, instead of waiting forever."""
+    import multiprocessing as mp
+    import time
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = 3
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, (1, 4), 10))
+             for r in range(world)]
+    t0 = time.monotonic()
+    for p in procs:
+        p.start()
+    errors = {}
+    try:
+        while len(errors) < world and time.monotonic() - t0 < 120:
+            try:
+                msg = q.get(timeout=5)
+            except Exception:  # noqa: BLE001 -- queue.Empty: keep waiting
+                continue
+            if isinstance(msg, tuple) and msg[0] == "error":
+                errors[msg[1]] = msg[2]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert "injected failure on rank 1 at tick 4" in errors.get(1, "")
+    assert set(errors) == {0, 1, 2}, errors
+    assert all(p.exitcode not in (0, None) for p in procs)
+    assert time.monotonic() - t0 < 200
