@@ -578,6 +578,11 @@ def emit_line(args, world, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d
         "clocks": clock_info,
         "gpu_launches": int(launches),
     }
+    if world > 1:  # the planner's per-GPU split (hllm_b200.planner)
+        plan = pipeline_plan(world)
+        line["pipeline"] = {"ranges": [list(r) for r in pipeline_ranges(world)],
+                            "memory_pressure": [round(g["memory"]["pressure"], 4)
+                                                for g in plan["gpus"]]}
     print(json.dumps(line), flush=True)
 
 
@@ -644,11 +649,23 @@ def phase_summary(steps, step_ms, hbm_gbs, tflops):
     return out
 
 
-def pipeline_ranges(world: int):
-    from hllm_b200.pipeline import partition_layers
+def pipeline_plan(world: int) -> dict:
+    """The per-GPU plan of the whole Qwen3-4B stage over `world` B200s
+    (hllm_b200.planner): layers split by the weight bytes each rank streams per
+    step (the LM head on the last rank), and each GPU's memory by the reference
+    planner's model for this workload (64 concurrent requests of up to 4,608
+    tokens, 512-token chunks)."""
+    from hllm_b200 import planner as P
     from hllm_b200.workload import QWEN3_4B as Q
-    layer, head = qwen_stage_bytes()
-    return partition_layers(Q["layers"], world, layer, head)
+    workload = dict(workload_id="configuration-3", prompt_tokens=CHUNK, output_tokens=512,
+                    concurrency=MAX_ACTIVE, total_cached_tokens=MAX_ACTIVE * 4608)
+    return P.plan_worker(P.shape_from_geometry(**Q), P.B200_WORKER, workload, world,
+                         kv_tokens=0)
+
+
+def pipeline_ranges(world: int):
+    from hllm_b200.planner import ranges_of
+    return ranges_of(pipeline_plan(world))
 
 
 def run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, host_mode,

@@ -39,7 +39,7 @@ from typing import Any, Callable, List, Mapping, Optional, Tuple
 
 __all__ = ["DTYPE_BYTES", "PlanningError", "NoFeasibleSplit", "Tensor", "ModelShape", "usable_bytes",
            "stage_weight_bytes", "stage_memory", "stream_bytes", "split_costs",
-           "split_stage", "plan_worker", "ranges_of"]
+           "split_stage", "plan_worker", "ranges_of", "shape_from_geometry", "B200_WORKER"]
 
 # python/hllm_control/models.py:43-57
 DTYPE_BYTES = {"BOOL": 1, "U8": 1, "I8": 1, "I16": 2, "U16": 2, "I32": 4, "U32": 4,
@@ -152,6 +152,42 @@ class _Sums:
             if not self.tied:
                 n += self.head
         return n
+
+
+def shape_from_geometry(*, hidden_size: int, intermediate_size: int, attention_heads: int,
+                        key_value_heads: int, head_dimension: int, layers: int,
+                        vocabulary_size: int, query_key_norm: bool, tied: bool,
+                        **_ignored) -> ModelShape:
+    """The tensor records a Llama/Qwen3 checkpoint of this geometry carries, as
+    the reference's prepare_model classifies them (embedding, final norm,
+    untied LM head, and per layer the two norms, q/k/v/o, gate/up/down and the
+    q/k norms when present): what the planner needs without a manifest."""
+    h, I, d = hidden_size, intermediate_size, head_dimension
+    q, kv = attention_heads * d, key_value_heads * d
+    per_layer = [h, h, q * h, kv * h, kv * h, h * q, I * h, I * h, h * I]
+    if query_key_norm:
+        per_layer += [d, d]
+    tensors = [Tensor(_EMBED, None, vocabulary_size * h), Tensor(_NORM, None, h)]
+    if not tied:
+        tensors.append(Tensor(_HEAD, None, vocabulary_size * h))
+    for li in range(layers):
+        tensors += [Tensor(_LAYER, li, n) for n in per_layer]
+    return ModelShape(num_layers=layers, hidden_size=h, num_kv_heads=key_value_heads,
+                      head_dim=d, vocabulary_size=vocabulary_size, tied_embeddings=tied,
+                      tensors=tuple(tensors))
+
+
+# One B200 as a planner worker profile (field names of the reference's
+# WorkerProfile): 183,359 MiB of HBM3e, 2 GiB kept for the driver and context.
+B200_WORKER = dict(worker_id="b200", endpoint="", backend="cuda",
+                   primary_memory_domain="DEVICE",
+                   supported_architectures=["llama.v1", "qwen3.v1"],
+                   supported_execution_dtypes=["F16", "F32"],
+                   memory_budgets=[dict(domain="DEVICE", capacity_bytes=183359 * 1024 * 1024,
+                                        runtime_reserve_bytes=2 * 1024 ** 3,
+                                        safety_fraction=0.05)],
+                   fixed_workspace_bytes=4 * 1024 ** 3, activation_buffer_count=2,
+                   allocator_allowance_fraction=0.05)
 
 
 def usable_bytes(budget: Any) -> int:
