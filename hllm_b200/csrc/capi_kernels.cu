@@ -91,6 +91,15 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
   if (st != HLLM_B200_OK) return st;
   const hb::GemmPlan plan = hb::gemm_plan(gw, static_cast<int>(n), sc.sm_count,
                                           static_cast<int>(bn), static_cast<int>(grid));
+  // The scratch holds the partial sums of one CTA per SM; a grid override
+  // larger than that would write past it.
+  const size_t need = hb::gemm_slot_floats(plan, static_cast<int>(pair));
+  if (need > hb::gemm_max_slot_floats(sc.sm_count)) {
+    set_error("GEMM split needs " + std::to_string(need * 4) + " bytes of partial sums; the " +
+              "library's scratch holds " + std::to_string(hb::gemm_max_slot_floats(sc.sm_count) * 4) +
+              " (use at most one CTA per SM)");
+    return HLLM_B200_RESOURCE_EXHAUSTED;
+  }
   hb::GemmSlots slots{};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = hb::gemm_launch(gw, gx, static_cast<int>(n), plan, static_cast<int>(epilogue), y,

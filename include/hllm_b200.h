@@ -350,7 +350,10 @@ hllm_b200_status hllm_b200_stage_read_logits(hllm_b200_stage* stage, float* out,
  * gate rows then up rows), X: F16 [n][k_pad] with zero padding columns,
  * k_pad % 64 == 0.  epilogue: 0 store F32, 1 store F16, 2 add into F32 Y,
  * 3 SwiGLU of the pair into F16 Y.  Uses a scratch area owned by the library
- * (allocated on first use per device). */
+ * (allocated on first use per device) that holds one CTA per SM: a split with
+ * a larger grid is refused with HLLM_B200_RESOURCE_EXHAUSTED.  A device wait
+ * inside the kernel that runs out (2 s) ends the kernel early; this
+ * asynchronous entry point does not report it (hllm_b200_step does). */
 hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint32_t pair,
                                 uint64_t second_row, const void* x, uint64_t n, uint32_t epilogue,
                                 void* y, uint64_t ldy, uint32_t bn, uint32_t grid, void* stream);
@@ -359,15 +362,17 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
  * it exists for callers that cannot let a library allocate device memory --
  * a serving process that fixes its device budget at start-up and admits
  * requests against it, or a host that owns all of a plugin's device memory.
- * Its split-K scratch is a static device array of 32 MiB (+68 KiB of segment
- * lists) that every GPU loading the library holds until the process exits.
+ * Its split-K scratch is a static device array of 32 MiB of partial sums, plus
+ * 34 KiB of per-tile segment lists (512 x 17 ints) and a 256-byte status word,
+ * that every GPU loading the library holds until the process exits.
  * Splits that need more partial-sum storage than that are rejected with
  * HLLM_B200_RESOURCE_EXHAUSTED and a message; plans that need none always run.
  * The first call on a device, with that device current, resolves the array's
  * device address (cudaGetSymbolAddress); make that first call before any
  * stream capture.  All calls on a device share the array: calls whose GPU
  * work overlaps (e.g. on two streams) race and must not be issued.  Calls no
- * cudaMalloc/cudaFree. */
+ * cudaMalloc/cudaFree.  As for hllm_b200_gemm, a device wait that runs out is
+ * not reported by this asynchronous call. */
 hllm_b200_status hllm_b200_gemm_noalloc(const void* w, uint64_t m, uint64_t k_pad, uint32_t pair,
                                         uint64_t second_row, const void* x, uint64_t n,
                                         uint32_t epilogue, void* y, uint64_t ldy, uint32_t bn,

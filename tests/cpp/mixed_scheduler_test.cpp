@@ -5,11 +5,16 @@
 // decode steps through the scheduler, as the worker's RPC handlers drive the
 // reference's StageScheduler (cpp/src/worker/execution_service.cpp); the fake
 // backends record every pass and return outputs derived from (sequence,
-// position), so each request can check that it got its own results.
+// position), so each request can check that it got its own results.  A fake
+// pass busy-waits 20-100 us, the length of a small stage's pass on a B200:
+// nothing sleeps, so passes form only through the scheduler's own logic.
+// Every sequence is allocated before the request threads start, and the
+// threads are released together from one latch.
 //
 //  1. A mixing backend: passes carry decode tickets and prefill chunks
 //     together, never more decodes than configured, never more prefill tokens
-//     than the budget (except a single chunk), distinct sequences per pass.
+//     than the budget (except a single chunk), distinct sequences per pass;
+//     mixed passes form and returning callers regroup into multi-ticket passes.
 //  2. A backend without the capability: the reference's policy (prefills
 //     alone, decode batches of at most 8, no mixed pass).
 //  3. Cancellation and deadlines before a ticket is claimed, and an exception
@@ -18,6 +23,7 @@
 #include <atomic>
 #include <chrono>
 #include <cstdio>
+#include <latch>
 #include <memory>
 #include <mutex>
 #include <set>
@@ -63,7 +69,7 @@ class FakeBackend : public runtime::StageBackend {
  public:
   mutable std::mutex mutex;
   mutable std::vector<Pass> passes;
-  std::chrono::microseconds delay{1500};
+  std::chrono::microseconds delay{50};
   mutable std::atomic<int> fail_next{0};
 
   runtime::MemoryAmounts weight_memory() const override { return {}; }
@@ -94,7 +100,9 @@ class FakeBackend : public runtime::StageBackend {
 
  protected:
   std::vector<runtime::StageOutput> pass(const std::vector<runtime::DecodeBatchItem>& items) const {
-    std::this_thread::sleep_for(delay);
+    const auto until = std::chrono::steady_clock::now() + delay;
+    while (std::chrono::steady_clock::now() < until) {
+    }
     if (fail_next.exchange(0)) throw runtime::Error::internal("injected backend failure");
     Pass p;
     std::set<const runtime::SequenceState*> seen;
@@ -130,46 +138,52 @@ class FakeMixingBackend final : public FakeBackend, public b200::MixedBatchBacke
 
 // One request: prompt in chunks of `chunk` tokens, then `steps` decode tokens.
 void run_request(const runtime::StageBackend& backend, b200::MixedStageScheduler& scheduler,
-                 int id, std::size_t prompt, std::size_t chunk, int steps) {
-  auto state = backend.allocate_sequence(prompt + steps);
-  static_cast<FakeSequence*>(state.get())->id = id;
+                 runtime::SequenceState& state, int id, std::size_t prompt, std::size_t chunk,
+                 int steps) {
   std::atomic_bool cancelled{false};
   const auto deadline = Clock::now() + std::chrono::minutes(5);
   std::size_t position = 0;
   while (position < prompt) {
     const std::size_t n = std::min(chunk, prompt - position);
-    state->prefilling = position > 0;
-    state->prefill_only = position + n < prompt;
+    state.prefilling = position > 0;
+    state.prefill_only = position + n < prompt;
     auto out = scheduler.execute(backend, runtime::TokenInput{std::vector<std::uint64_t>(n, 1)},
-                                 position, *state, cancelled, deadline);
-    if (state->prefill_only) {
+                                 position, state, cancelled, deadline);
+    if (state.prefill_only) {
       EXPECT(std::holds_alternative<runtime::PrefillProgress>(out), "request %d chunk", id);
     } else {
       EXPECT(std::holds_alternative<runtime::SampledToken>(out) &&
-                 std::get<runtime::SampledToken>(out).id == token_of(state.get(), position + n - 1),
+                 std::get<runtime::SampledToken>(out).id == token_of(&state, position + n - 1),
              "request %d first token", id);
     }
     position += n;
   }
-  state->prefilling = false;
-  state->prefill_only = false;
+  state.prefilling = false;
+  state.prefill_only = false;
   for (int s = 0; s < steps; ++s) {
-    auto out = scheduler.execute(backend, runtime::TokenInput{{7}}, position, *state, cancelled,
+    auto out = scheduler.execute(backend, runtime::TokenInput{{7}}, position, state, cancelled,
                                  deadline);
     EXPECT(std::holds_alternative<runtime::SampledToken>(out) &&
-               std::get<runtime::SampledToken>(out).id == token_of(state.get(), position),
+               std::get<runtime::SampledToken>(out).id == token_of(&state, position),
            "request %d step %d", id, s);
     ++position;
   }
 }
 
+// `requests` requests with prompts of 100 + 37 r tokens in 64-token chunks and
+// 12 decode steps each; sequences first, then every thread from one latch.
 void run_many(const FakeBackend& backend, b200::MixedStageScheduler& scheduler, int requests) {
+  std::vector<std::unique_ptr<runtime::SequenceState>> states;
+  for (int r = 0; r < requests; ++r) {
+    states.push_back(backend.allocate_sequence(1024));
+    static_cast<FakeSequence*>(states.back().get())->id = r + 1;
+  }
+  std::latch start(requests);
   std::vector<std::thread> threads;
   for (int r = 0; r < requests; ++r)
     threads.emplace_back([&, r] {
-      // staggered arrivals: prefills keep arriving while others decode
-      std::this_thread::sleep_for(std::chrono::milliseconds(3 * r));
-      run_request(backend, scheduler, r + 1, 100 + 37 * r, 64, 12);
+      start.arrive_and_wait();
+      run_request(backend, scheduler, *states[r], r + 1, 100 + 37 * r, 64, 12);
     });
   for (auto& t : threads) t.join();
 }
@@ -193,8 +207,13 @@ void mixing_case() {
          m.mixed_batches);
   EXPECT(m.completed_steps == rows, "completed %zu rows %zu", m.completed_steps, rows);
   EXPECT(m.queued_prefills == 0 && m.queued_decodes == 0 && m.executing == 0, "queues drained");
-  std::printf("mixing: passes=%zu mixed=%zu largest=%zu rows=%zu\n", backend.passes.size(),
-              mixed, m.largest_decode_batch, rows);
+  // 24 callers that all come back after each pass: most passes carry several.
+  EXPECT(m.decode_batches * 2 > backend.passes.size(), "multi-ticket passes %zu of %zu",
+         m.decode_batches, backend.passes.size());
+  // 16 decodes and two 64-token chunks at most: 18 tickets.
+  EXPECT(m.largest_decode_batch >= 10, "largest pass %zu", m.largest_decode_batch);
+  std::printf("mixing: passes=%zu mixed=%zu largest=%zu rows=%zu gather=%.2f ms\n",
+              backend.passes.size(), mixed, m.largest_decode_batch, rows, m.gather_wait_ms);
 }
 
 void reference_policy_case() {

@@ -146,7 +146,9 @@ def sampling_kat() -> None:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <reference tree>")
+    root = sys.argv[1]
     tiny_qwen(root)
     tiny_llama()
     sampling_kat()

@@ -98,6 +98,21 @@ def test_gemm_swiglu_pair(I, k, n, grid):
     np.testing.assert_allclose(f16_vals(host(Y, np.uint16)), ref, rtol=3e-3, atol=3e-3)
 
 
+def test_gemm_refuses_a_grid_beyond_its_scratch():
+    """The library's stream-K scratch holds one CTA per SM: a grid override of
+    two CTAs per SM with wide tiles would write past it and is refused before
+    any launch."""
+    torch = torch_cuda()
+    m, k, n = 2560, 4096, 256
+    W = torch.zeros((m, k), dtype=torch.float16, device="cuda")
+    X = torch.zeros((n, k), dtype=torch.float16, device="cuda")
+    Y = torch.zeros((n, m), dtype=torch.float32, device="cuda")
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    st = lib().hllm_b200_gemm(ptr(W), m, k, 1, 0, ptr(X), n, 0, ptr(Y), m, 256, 2 * sms, stream())
+    assert st == _lib.RESOURCE_EXHAUSTED
+    assert "scratch holds" in _lib.last_error()
+
+
 # ----------------------------------------------------------------------------- RMSNorm
 def test_rmsnorm_matches_oracle():
     torch = torch_cuda()

@@ -1,16 +1,20 @@
 """The allocation-free GEMM entry point (hllm_b200_gemm_noalloc).
 
 Some callers cannot let a library allocate device memory: a serving process
-that fixes its device budget when it starts and admits requests against it, or
-a host that owns all of a plugin's device memory.  For them the GEMM has a
-variant whose split-K scratch is a static device array.  This test calls it
-through the C ABI and checks its output against the allocating entry point
-(hllm_b200_gemm) within the GEMM tolerance used elsewhere (1e-4 for F32
-outputs, 2e-3 for F16), on two calls in a row -- the second call reuses the
-scratch the first one left behind -- and checks that a split too large for
-the static array is refused with a clear error.
+that fixes its device budget when it starts and admits requests against it
+(hLLM's worker reserves each request's bytes before it runs), or a host that
+owns all of a plugin's device memory.  For them the GEMM has a variant whose
+split-K scratch is a static device array of fixed size.
 
-It lives in a file of its own that pytest collects last, and it passes both on
+This test calls it through the C ABI on two calls in a row -- the second call
+finds the scratch as the first one left it -- and checks each result against
+the allocating entry point (hllm_b200_gemm), within the GEMM tolerance the
+kernel tests use (1e-4 for F32 outputs, 2e-3 for F16) and also bit for bit,
+since both run the same plan and sum partial tiles in the same fixed order;
+and against the float64 product of the same F16 inputs.  A split too large
+for the static array is refused with a clear error.
+
+It lives in a file of its own that pytest collects last, and passes both on
 its own in a fresh process and after the other tests.
 """
 import numpy as np
@@ -45,10 +49,20 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls(m, k, n, pair, epi)
     L = _lib.lib()
     rng = np.random.default_rng(m + n)
     k_pad = (k + 63) // 64 * 64
-    W = dev(padded(f16_bits(rng.standard_normal((m * pair, k)).astype(np.float32) * 0.03), k_pad))
-    X = dev(padded(f16_bits(rng.standard_normal((n, k)).astype(np.float32)), k_pad))
+    Wb = f16_bits(rng.standard_normal((m * pair, k)).astype(np.float32) * 0.03)
+    Xb = f16_bits(rng.standard_normal((n, k)).astype(np.float32))
+    W, X = dev(padded(Wb, k_pad)), dev(padded(Xb, k_pad))
     f16_out = epi in (1, 3)
     base = rng.standard_normal((n, m)).astype(np.float32)
+
+    full = f16_vals(Xb).astype(np.float64) @ f16_vals(Wb).astype(np.float64).T
+    if epi == 3:
+        g, u = full[:, :m], full[:, m:]
+        exact, tol64 = g / (1.0 + np.exp(-g)) * u, 3e-3
+    elif epi == 2:
+        exact, tol64 = base + full, 1e-4
+    else:
+        exact, tol64 = full, 2e-3 if f16_out else 1e-4
 
     def fresh():
         if f16_out:
@@ -62,12 +76,16 @@ def test_noalloc_matches_allocating_entry_point_on_two_calls(m, k, n, pair, epi)
     _lib.check(call(L.hllm_b200_gemm, W, X, m, k_pad, n, pair, epi, Y_ref))
     sync()
     expected = read(Y_ref)
+    np.testing.assert_allclose(expected, exact, rtol=tol64, atol=tol64)
     tol = 2e-3 if f16_out else 1e-4
     for _ in range(2):
         Y = fresh()
         _lib.check(call(L.hllm_b200_gemm_noalloc, W, X, m, k_pad, n, pair, epi, Y))
         sync()
-        np.testing.assert_allclose(read(Y), expected, rtol=tol, atol=tol)
+        got = read(Y)
+        np.testing.assert_allclose(got, expected, rtol=tol, atol=tol)
+        assert np.array_equal(got, expected)
+        np.testing.assert_allclose(got, exact, rtol=tol64, atol=tol64)
 
 
 def test_noalloc_refuses_a_split_beyond_its_static_scratch():
