@@ -858,6 +858,7 @@ def ours_pipeline(args, world, rank, local):
     stream = torch.cuda.ExternalStream(L.hllm_b200_stage_stream(stage.handle))
     links = DeviceLinks(rank, world, stream, MAX_ACTIVE + CHUNK + 64, cfg.hidden_size,
                         token_group=token_group, pair_groups=pair_groups)
+    links.connect()
 
     def fresh_plans():
         traces, plans = [], []

@@ -194,6 +194,25 @@ class DeviceLinks:
         self.sends = 0
         self.token_sends = []
 
+    def connect(self) -> None:
+        """Opens every neighbour link before the first step, in one order on all
+        ranks.  NCCL point-to-point communicators are created on first use, and
+        creating one blocks the host until both ends take part; a link first
+        used inside the schedule could then hold one rank's host in creation
+        while its peer waits in a collective.  Here the links open as a chain
+        (0 -> 1, then 1 -> 2, ...): each rank first receives from its left
+        neighbour, then sends to its right one, so every creation meets its
+        peer.  Called collectively by all ranks after construction."""
+        import torch
+        import torch.distributed as dist
+        probe = torch.zeros(1, self.hidden, dtype=torch.float16, device=self.recv_buf.device)
+        with torch.cuda.stream(self.stream):
+            if self.rank > 0:
+                dist.recv(self.recv_buf[:1], src=self.rank - 1, group=self.recv_group)
+            if self.rank < self.world - 1:
+                dist.send(probe, dst=self.rank + 1, group=self.send_group)
+        self.stream.synchronize()
+
     def recv_activation(self, tokens: int) -> int:
         import torch
         import torch.distributed as dist

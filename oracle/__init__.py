@@ -336,25 +336,33 @@ def layer_shapes(spec: ModelSpec):
     return shapes
 
 
-def synth_weights(spec: ModelSpec, seed: int, layers=None):
-    """F16 bit patterns of the seeded synthetic model: {name: uint16 array}, named
-    like the reference's Safetensors tensors (cpp/src/cpu/stage.cpp:246-259)."""
-    out = {}
+def synth_head_weights(spec: ModelSpec, seed: int):
+    """The embedding, final norm and (untied) LM head of the seeded synthetic
+    model, as F16 bit patterns named like the reference's Safetensors tensors."""
     h = spec.hidden_size
-    out["model.embed_tokens.weight"] = synth_matrix(seed, TAG_EMBED, (spec.vocabulary_size, h))
+    out = {"model.embed_tokens.weight": synth_matrix(seed, TAG_EMBED, (spec.vocabulary_size, h))}
     if not spec.tied:
         out["lm_head.weight"] = synth_matrix(seed, TAG_HEAD, (spec.vocabulary_size, h))
     out["model.norm.weight"] = synth_norm(seed, TAG_FINAL_NORM, h)
-    names = dict(input_norm="input_layernorm", query="self_attn.q_proj", key="self_attn.k_proj",
-                 value="self_attn.v_proj", attention_output="self_attn.o_proj",
-                 post_attention_norm="post_attention_layernorm", gate="mlp.gate_proj",
-                 up="mlp.up_proj", down="mlp.down_proj", query_norm="self_attn.q_norm",
-                 key_norm="self_attn.k_norm")
+    return out
+
+
+def synth_layer_weights(spec: ModelSpec, seed: int, i: int):
+    """Layer i's tensors of the seeded synthetic model (F16 bit patterns)."""
+    out = {}
+    for kind, shape in layer_shapes(spec).items():
+        tag = i * 16 + KIND[kind]
+        arr = synth_norm(seed, tag, shape[0]) if len(shape) == 1 else synth_matrix(seed, tag, shape)
+        out[f"model.layers.{i}.{LAYER_NAMES[kind]}.weight"] = arr
+    return out
+
+
+def synth_weights(spec: ModelSpec, seed: int, layers=None):
+    """F16 bit patterns of the seeded synthetic model: {name: uint16 array}, named
+    like the reference's Safetensors tensors (cpp/src/cpu/stage.cpp:246-259)."""
+    out = synth_head_weights(spec, seed)
     for i in (range(spec.layers) if layers is None else layers):
-        for kind, shape in layer_shapes(spec).items():
-            tag = i * 16 + KIND[kind]
-            arr = synth_norm(seed, tag, shape[0]) if len(shape) == 1 else synth_matrix(seed, tag, shape)
-            out[f"model.layers.{i}.{names[kind]}.weight"] = arr
+        out.update(synth_layer_weights(spec, seed, i))
     return out
 
 

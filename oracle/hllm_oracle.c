@@ -109,6 +109,7 @@ void oracle_f32_to_f16_array(const float* in, uint16_t* out, size_t n) {
   for (size_t i = 0; i < n; ++i) out[i] = oracle_f32_to_f16(in[i]);
 }
 void oracle_f16_to_f32_array(const uint16_t* in, float* out, size_t n) {
+#pragma omp parallel for schedule(static) if (n > (1u << 20))
   for (size_t i = 0; i < n; ++i) out[i] = oracle_f16_to_f32(in[i]);
 }
 

@@ -57,6 +57,7 @@ def main(out_path):
     stream = torch.cuda.ExternalStream(L.hllm_b200_stage_stream(stage.handle))
     links = DeviceLinks(rank, world, stream, 128, cfg.hidden_size, token_group=token_group,
                         pair_groups=pair_groups)
+    links.connect()
     boundary = None if rank == 1 else device_view(L.hllm_b200_stage_boundary(stage.handle),
                                                   (128, cfg.hidden_size))
     mbs = [[0, 2], [1, 3]]
