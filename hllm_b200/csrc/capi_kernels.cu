@@ -38,7 +38,7 @@ hllm_b200_status cuda_status(cudaError_t e) {
 // use and kept until the process exits.
 struct DeviceScratch {
   float* slots = nullptr;
-  int* segmap = nullptr;
+  int* counters = nullptr;
   uint32_t* status = nullptr;
   int sm_count = 0;
 };
@@ -55,7 +55,8 @@ hllm_b200_status scratch_for_device(DeviceScratch* out) {
     e = cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
       e = cudaMalloc(&s.slots, hb::gemm_max_slot_floats(s.sm_count) * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&s.segmap, hb::kGemmMapInts * sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&s.counters, hb::kGemmCounterInts * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(s.counters, 0, hb::kGemmCounterInts * sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&s.status, 256);
     if (e == cudaSuccess) e = cudaMemset(s.status, 0, 256);
     if (e != cudaSuccess) {
@@ -100,14 +101,15 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
               " (use at most one CTA per SM)");
     return HLLM_B200_RESOURCE_EXHAUSTED;
   }
-  hb::GemmSlots slots{};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = hb::gemm_launch(gw, gx, static_cast<int>(n), plan, static_cast<int>(epilogue), y,
-                                  static_cast<int>(ldy), sc.slots, sc.segmap, &slots, sc.status,
-                                  s);
-  if (e == cudaSuccess && plan.stream_k)
-    e = hb::gemm_finish_launch(slots, static_cast<int>(n), static_cast<int>(epilogue), y,
-                               static_cast<int>(ldy), s);
+  // The tile counters start each call at zero, even after a kernel that ended
+  // early on a failed wait.
+  cudaError_t e = plan.stream_k
+                      ? cudaMemsetAsync(sc.counters, 0, hb::kGemmCounterInts * sizeof(int), s)
+                      : cudaSuccess;
+  if (e == cudaSuccess)
+    e = hb::gemm_launch(gw, gx, static_cast<int>(n), plan, static_cast<int>(epilogue), y,
+                        static_cast<int>(ldy), sc.slots, sc.counters, sc.status, s);
   return cuda_status(e);
 }
 

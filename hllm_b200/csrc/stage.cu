@@ -171,12 +171,14 @@ struct hllm_b200_stage {
   double* sample_scratch = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
   int* attn_counters = nullptr;  // [R_max][Hkv] split arrival counters (self-resetting)
+  size_t attn_counter_ints = 0;
   float* pre_part = nullptr;     // prefill key-split pieces
   int* pre_counters = nullptr;   // [max qtiles][Hkv] split arrival counters (self-resetting)
+  size_t pre_counter_ints = 0;
   int max_qtiles = 0;
   hb::GemmInput in_xn{}, in_attn{}, in_act{}, in_xs{};
-  float* slots = nullptr;  // stream-K GEMM slots, consumed by the next kernel
-  int* segmap = nullptr;   // their per-tile segment lists
+  float* slots = nullptr;        // stream-K GEMM partial tiles
+  int* tile_counters = nullptr;  // their per-tile completion counters (kept at zero)
 
   // pinned host staging
   // Descriptor uploads go through a ring of pinned buffers so that enqueue-only
@@ -564,7 +566,8 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
     s->part_o = s->alloc<float>(std::max(s->max_splits * s->hq, pieces * group) * s->dim);
     s->part_ml = s->alloc<float>(std::max(s->max_splits * s->hq, pieces * group) * 2);
   }
-  s->attn_counters = s->alloc<int>(R * s->hkv);
+  s->attn_counter_ints = R * s->hkv;
+  s->attn_counters = s->alloc<int>(s->attn_counter_ints);
   {
     // Prefill tiles: at most one partial tile per row beyond T / qtile_tokens.
     const int qt = hb::attn_qtile_tokens(static_cast<int>(s->hq / s->hkv));
@@ -572,10 +575,11 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
     s->pre_part = s->alloc<float>(std::max<size_t>(
         1, hb::attn_prefill_part_floats(static_cast<int>(s->dim), static_cast<int>(s->hkv),
                                         s->max_qtiles, hb::kPrefillMaxSplits)));
-    s->pre_counters = s->alloc<int>(static_cast<size_t>(s->max_qtiles) * s->hkv);
+    s->pre_counter_ints = static_cast<size_t>(s->max_qtiles) * s->hkv;
+    s->pre_counters = s->alloc<int>(s->pre_counter_ints);
   }
   s->slots = s->alloc<float>(hb::gemm_max_slot_floats(s->sm_count));
-  s->segmap = s->alloc<int>(hb::kGemmMapInts);
+  s->tile_counters = s->alloc<int>(hb::kGemmCounterInts);
   if (!hb::gemm_make_input(&s->in_xn, s->xn, static_cast<int>(T), static_cast<int>(s->h_pad),
                            static_cast<int>(s->h_pad)) ||
       !hb::gemm_make_input(&s->in_attn, s->attn, static_cast<int>(T), static_cast<int>(s->qw_pad),
@@ -910,14 +914,12 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
       PLAUNCH(kProfNorm, 0, 0, hb::rmsnorm_launch(s->hidden, T, h, L.in_norm, eps, s->xn,
                                                    static_cast<int>(s->h_pad), nullptr, s->stream));
     const hb::GemmPlan pq = hb::gemm_plan(L.g_qkv, T, s->sm_count);
-    hb::GemmSlots qslots{};
     PLAUNCH(gk, gemm_bytes(s->qkvw, T, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->qkvw, T, s->h, 1),
             hb::gemm_launch(L.g_qkv, s->in_xn, T, pq, hb::kEpiStoreF32, s->qkv,
-                            static_cast<int>(s->qkvw), s->slots, s->segmap, &qslots, s->status, s->stream));
+                            static_cast<int>(s->qkvw), s->slots, s->tile_counters, s->status,
+                            s->stream));
     hb::QkvPostArgs qa{};
     qa.qkv = s->qkv;
-    qa.slots = qslots;
-    qa.from_slots = pq.stream_k ? 1 : 0;
     qa.tokens = T;
     qa.hq = static_cast<int>(s->hq);
     qa.hkv = static_cast<int>(s->hkv);
@@ -969,37 +971,30 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     }
     if (p.total_qtiles)
       PLAUNCH(kProfAttnPrefill, p.attn_pre_bytes, p.attn_pre_flops, hb::attn_prefill_launch(aa, p.total_qtiles, s->stream));
-    // o_proj, then the fused residual add + post-attention RMSNorm.
+    // o_proj adds itself into the residual stream, then the post-attention RMSNorm.
     const hb::GemmPlan po = hb::gemm_plan(L.g_o, T, s->sm_count);
-    hb::GemmSlots oslots{};
     PLAUNCH(gk, gemm_bytes(s->h, T, s->qw, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->qw, 1),
-            hb::gemm_launch(L.g_o, s->in_attn, T, po, hb::kEpiResidual, s->hidden, h, s->slots, s->segmap,
-                            &oslots, s->status, s->stream));
+            hb::gemm_launch(L.g_o, s->in_attn, T, po, hb::kEpiResidual, s->hidden, h, s->slots,
+                            s->tile_counters, s->status, s->stream));
     PLAUNCH(kProfNorm, 0, 0,
-            hb::residual_norm_launch(s->hidden, T, h, po.stream_k ? &oslots : nullptr,
-                                     L.post_norm, eps, s->xn, static_cast<int>(s->h_pad),
-                                     s->stream));
-    // gate/up with SwiGLU: in the GEMM epilogue, or from the stream-K slots.
+            hb::residual_norm_launch(s->hidden, T, h, L.post_norm, eps, s->xn,
+                                     static_cast<int>(s->h_pad), s->stream));
+    // gate/up with SwiGLU in the GEMM's epilogue.
     const hb::GemmPlan pg = hb::gemm_plan(L.g_gu, T, s->sm_count);
-    hb::GemmSlots gslots{};
     PLAUNCH(gk, gemm_bytes(s->I, T, s->h, 2, hb::kEpiSwiGLU), gemm_flops(s->I, T, s->h, 2),
             hb::gemm_launch(L.g_gu, s->in_xn, T, pg, hb::kEpiSwiGLU, s->act,
-                            static_cast<int>(s->I_pad), s->slots, s->segmap, &gslots, s->status, s->stream));
-    if (pg.stream_k)
-      PLAUNCH(kProfSwiglu, 0, 0,
-              hb::swiglu_launch(gslots, T, s->act, static_cast<int>(s->I_pad), s->stream));
-    // down_proj, then the residual add fused with the next layer's input norm.
+                            static_cast<int>(s->I_pad), s->slots, s->tile_counters, s->status,
+                            s->stream));
+    // down_proj adds itself into the residual stream, then the next layer's input norm.
     const hb::GemmPlan pd = hb::gemm_plan(L.g_down, T, s->sm_count);
-    hb::GemmSlots dslots{};
     PLAUNCH(gk, gemm_bytes(s->h, T, s->I, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->I, 1),
-            hb::gemm_launch(L.g_down, s->in_act, T, pd, hb::kEpiResidual, s->hidden, h, s->slots, s->segmap,
-                            &dslots, s->status, s->stream));
+            hb::gemm_launch(L.g_down, s->in_act, T, pd, hb::kEpiResidual, s->hidden, h, s->slots,
+                            s->tile_counters, s->status, s->stream));
     const float* next_norm = li + 1 < s->n_layers ? s->layers[li + 1].in_norm : nullptr;
-    if (pd.stream_k || next_norm)
+    if (next_norm)
       PLAUNCH(kProfNorm, 0, 0,
-              hb::residual_norm_launch(s->hidden, T, h, pd.stream_k ? &dslots : nullptr,
-                                       next_norm, eps, s->xn, static_cast<int>(s->h_pad),
-                                       s->stream));
+              hb::residual_norm_launch(s->hidden, T, h, next_norm, eps, s->xn,
+                                       static_cast<int>(s->h_pad), s->stream));
     s->mark("layer", static_cast<int64_t>(s->desc.layer_start + li));
   }
 
@@ -1012,15 +1007,11 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
                                 static_cast<int>(s->h_pad), s->last_idx, s->stream));
       s->mark("final_norm");
       const hb::GemmPlan ph = hb::gemm_plan(s->g_head, S, s->sm_count);
-      hb::GemmSlots hslots{};
       PLAUNCH(S <= 128 ? kProfGemmDecode : kProfGemmPrefill,
               gemm_bytes(s->V, S, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->V, S, s->h, 1),
               hb::gemm_launch(s->g_head, s->in_xs, S, ph, hb::kEpiStoreF32, s->logits,
-                              static_cast<int>(s->V), s->slots, s->segmap, &hslots, s->status, s->stream));
-      if (ph.stream_k)
-        PLAUNCH(kProfSwiglu, 0, 0,
-                hb::gemm_finish_launch(hslots, S, hb::kEpiStoreF32, s->logits,
-                                       static_cast<int>(s->V), s->stream));
+                              static_cast<int>(s->V), s->slots, s->tile_counters, s->status,
+                              s->stream));
       s->mark("lm_head");
       PLAUNCH(kProfSample, 0, 0, hb::sample_launch(s->logits, S, static_cast<int>(s->V), static_cast<int>(s->V),
                                s->d_params, s->sample_scratch, s->results, s->status, s->stream));
@@ -1032,6 +1023,18 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
   }
   s->last_samples = p.samples;
   s->last_tokens = p.tokens;
+}
+
+// Kernels return their arrival counters (GEMM tiles, attention streams and
+// prefill tiles) to zero when they finish; a kernel that ended early on a
+// failed wait may leave one behind, so a failed step clears them all.
+void reset_counters(hllm_b200_stage* s) {
+  check_cuda(cudaMemsetAsync(s->tile_counters, 0, hb::kGemmCounterInts * sizeof(int), s->stream),
+             "counter reset");
+  check_cuda(cudaMemsetAsync(s->attn_counters, 0, s->attn_counter_ints * sizeof(int), s->stream),
+             "counter reset");
+  check_cuda(cudaMemsetAsync(s->pre_counters, 0, s->pre_counter_ints * sizeof(int), s->stream),
+             "counter reset");
 }
 
 hllm_b200_status status_to_code(uint32_t bits, std::string* msg) {
@@ -1269,7 +1272,10 @@ hllm_b200_status hllm_b200_step(hllm_b200_stage* stage, const hllm_b200_row* row
     std::memcpy(&bits, stage->h_down, sizeof(bits));
     std::string msg;
     const hllm_b200_status code = status_to_code(bits, &msg);
-    if (code != HLLM_B200_OK) fail(code, msg);
+    if (code != HLLM_B200_OK) {
+      reset_counters(stage);
+      fail(code, msg);
+    }
     if (stage->desc.final) {
       const auto* res = reinterpret_cast<const hb::SampleResult*>(stage->h_down + 8);
       for (uint32_t i = 0; i < p.samples; ++i) copy_sampled(res[i], &sampled[i]);
@@ -1315,6 +1321,7 @@ hllm_b200_status hllm_b200_stage_sync(hllm_b200_stage* stage) {
     std::string msg;
     const hllm_b200_status code = status_to_code(bits, &msg);
     if (code != HLLM_B200_OK) {
+      reset_counters(stage);
       for (auto* q : stage->pending)
         if (stage->live.count(q)) q->failed = true;
       stage->pending.clear();

@@ -1,7 +1,7 @@
 """Per-operator timing of the executor's kernels through the C ABI.
 
-    python -m hllm_b200.opbench [gemm|attn|prefill|envelope|c5|all] [--ncu-gemm M,K,N,PAIR,EPI]
-                                 [--ncu-attn ROWS] [--ncu-prefill FIRST,COUNT]
+    python opbench.py [gemm|attn|prefill|envelope|c5|all] [--ncu-gemm M,K,N,PAIR,EPI]
+                      [--ncu-attn ROWS] [--ncu-prefill FIRST,COUNT]
 
 Times the projection GEMM at the Qwen3-4B shapes (decode width 16/64 tokens,
 prefill width 575 tokens) and the paged decode attention at configuration-5
@@ -70,8 +70,7 @@ def hbm_peak():
     """(GB/s, source) of the HBM roof: MEASURED_PEAKS.json when present."""
     import json
     import os
-    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
-                        "MEASURED_PEAKS.json")
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             v = json.load(f).get("hbm_gbs")
@@ -84,7 +83,7 @@ def hbm_peak():
 
 def gemm_case(m, k, n, pair=1, epi=0, bn=0, grid=0, iters=20, cold=False):
     torch = _torch()
-    from . import _lib
+    from hllm_b200 import _lib
     L = _lib.lib()
     stream = torch.cuda.current_stream().cuda_stream
     rows = m * pair
@@ -108,7 +107,7 @@ def gemm_case(m, k, n, pair=1, epi=0, bn=0, grid=0, iters=20, cold=False):
 def attn_case(rows_ctx, hq=32, hkv=8, d=128, split=256, iters=10, cold=False):
     """Decode attention over rows with the given contexts (one new token each)."""
     torch = _torch()
-    from . import _lib
+    from hllm_b200 import _lib
     L = _lib.lib()
     stream = torch.cuda.current_stream().cuda_stream
     R = len(rows_ctx)
@@ -152,7 +151,7 @@ def prefill_case(first, count, rows=1, hq=32, hkv=8, d=128, iters=10):
     """Prefill attention of `rows` chunks of `count` tokens at positions
     [first, first + count) (causal over first + count keys each)."""
     torch = _torch()
-    from . import _lib
+    from hllm_b200 import _lib
     L = _lib.lib()
     stream = torch.cuda.current_stream().cuda_stream
     ctx = first + count
@@ -261,7 +260,7 @@ def envelope_suite(tokens=512, width=2560, iters=200):
     (hllm_b200_stage_envelope + _wait) into pinned memory."""
     import ctypes as C
     import time
-    from . import _lib
+    from hllm_b200 import _lib
     L = _lib.lib()
     ident = _lib.BoundaryIdentity(b"qwen3-4b-plan", 3, b"request-000001", 4608, width)
     x = (np.random.default_rng(0).standard_normal(tokens * width)).astype("<f2")
@@ -288,7 +287,7 @@ def envelope_suite(tokens=512, width=2560, iters=200):
             return
     except ImportError:
         return
-    from .backend import B200Stage, DecodeBatchItem, ModelConfig, TokenInput
+    from hllm_b200.backend import B200Stage, DecodeBatchItem, ModelConfig, TokenInput
     cfg = ModelConfig(width, 9728, 32, 8, 128, 4608, 1e-6, 1e6, True, 151936, 36, True)
     stage = B200Stage(cfg, 0, 1, first=True, final=False, kv_pool_tokens=8192,
                       max_step_tokens=tokens + 64, max_step_rows=80, max_sequences=80)
