@@ -143,7 +143,7 @@ def lib():
                                              u32, vp]),
         "hllm_b200_rmsnorm": (C.c_int, [vp, u64, u64, vp, f32, vp, u64, vp]),
         "hllm_b200_pack": (C.c_int, [vp, vp, vp, u32, u32, vp, u32, u32, u32] + [vp] * 9 + [vp]),
-        "hllm_b200_attention": (C.c_int, [vp] * 10 + [u32] * 8 + [vp, u64, vp, vp]),
+        "hllm_b200_attention": (C.c_int, [vp] * 10 + [u32] * 8 + [vp, u64, u64, u64, vp, vp]),
         "hllm_b200_attention_qtile_tokens": (u32, [u32]),
         "hllm_b200_qkv_post": (C.c_int, [vp, u64, u32, u32, u32, vp, vp, vp, vp, f32, vp, vp, vp,
                                          vp, vp]),

@@ -1,11 +1,20 @@
 // attention.cuh -- paged-KV GQA attention launchers.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace hb {
+
+// TMA tensor maps of one layer's attention inputs: the query buffer (tcgen05
+// prefill) and the K and V caches, all with the 128-byte swizzle.
+struct TcMaps {
+  CUtensorMap q;  // [tokens][Hq][d] F16, box 64 dims x group heads x 128/group tokens
+  CUtensorMap k;  // [blocks * Hkv * 16][d] F16, box 64 dims x one 16-key page
+  CUtensorMap v;
+};
 
 struct AttnArgs {
   const __half* q;             // [T][Hq*d] (normed, RoPE applied)
@@ -62,5 +71,21 @@ cudaError_t attn_prefill_launch(const AttnArgs& a, int total_qtiles, cudaStream_
 int attn_prefill_splits(int dim, int hkv, int total_qtiles, int sm_count, size_t table_bytes);
 size_t attn_prefill_part_floats(int dim, int hkv, int total_qtiles, int splits);
 size_t prefill_table_bytes(const AttnArgs& a);
+
+// Prefill rows on tcgen05 / TMEM (attention_tc.cu) for head sizes 64 and 128
+// and GQA groups 1, 2, 4, 8.
+bool attn_prefill_tc_supported(int dim, int group);
+// The K and V maps only (head sizes 64, 128, 256).
+bool attn_make_kv_maps(TcMaps* maps, int hkv, int dim, const void* k_cache, const void* v_cache,
+                       long long kv_blocks);
+// All three maps (head sizes 64 and 128, groups 1/2/4/8).
+bool attn_tc_make_maps(TcMaps* maps, const void* q, long long q_tokens, int hq, int hkv, int dim,
+                       const void* k_cache, const void* v_cache, long long kv_blocks);
+// Key splits per tile for the tcgen05 kernel (one resident CTA per SM).
+int attn_prefill_tc_splits(int hkv, int total_qtiles, int sm_count);
+// Same contract as attn_prefill_launch (the same partial-tile workspace and
+// counters for split tiles).
+cudaError_t attn_prefill_tc_launch(const TcMaps& maps, const AttnArgs& a, int total_qtiles,
+                                   cudaStream_t stream);
 
 }  // namespace hb

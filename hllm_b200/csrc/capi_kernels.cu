@@ -6,6 +6,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -160,7 +161,8 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
                                      uint32_t rows, uint32_t total_splits, uint32_t total_qtiles,
                                      uint32_t hq, uint32_t hkv, uint32_t dim, uint32_t max_blocks,
                                      uint32_t split_tokens, uint16_t* out, uint64_t ld_out,
-                                     uint32_t* status, void* stream) {
+                                     uint64_t q_tokens, uint64_t kv_blocks, uint32_t* status,
+                                     void* stream) {
   if (hkv == 0 || hq % hkv != 0 || dim == 0) return HLLM_B200_INVALID_REQUEST;
   hb::AttnArgs a{};
   a.q = reinterpret_cast<const __half*>(q);
@@ -202,12 +204,28 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
                                                        static_cast<int>(hkv),
                                                        static_cast<int>(dim), a.decode_ctas));
   }
-  // Prefill: key splits per tile, merged by the last split of each tile.
-  a.prefill_splits = total_qtiles ? hb::attn_prefill_splits(static_cast<int>(dim),
-                                                            static_cast<int>(hkv),
-                                                            static_cast<int>(total_qtiles),
-                                                            sm_count, hb::prefill_table_bytes(a))
-                                  : 1;
+  // Prefill: tcgen05 tiles where the stage uses them (head sizes 64/128, and
+  // HLLM_B200_TC_PREFILL not 0), else the mma.sync kernel; key splits per
+  // tile, merged by the last split of each tile.
+  const char* env = std::getenv("HLLM_B200_TC_PREFILL");
+  const bool tc = total_qtiles && q_tokens && kv_blocks &&
+                  hb::attn_prefill_tc_supported(static_cast<int>(dim), static_cast<int>(hq / hkv)) &&
+                  !(env && env[0] == '0');
+  hb::TcMaps maps{};
+  if (tc && !hb::attn_tc_make_maps(&maps, q, static_cast<long long>(q_tokens), static_cast<int>(hq),
+                                   static_cast<int>(hkv), static_cast<int>(dim), k_cache, v_cache,
+                                   static_cast<long long>(kv_blocks))) {
+    set_error("tensor map creation failed");
+    return HLLM_B200_INTERNAL;
+  }
+  a.prefill_splits = !total_qtiles ? 1
+                     : tc          ? hb::attn_prefill_tc_splits(static_cast<int>(hkv),
+                                                                static_cast<int>(total_qtiles),
+                                                                sm_count)
+                                   : hb::attn_prefill_splits(static_cast<int>(dim),
+                                                             static_cast<int>(hkv),
+                                                             static_cast<int>(total_qtiles),
+                                                             sm_count, hb::prefill_table_bytes(a));
   const size_t pre_floats = hb::attn_prefill_part_floats(
       static_cast<int>(dim), static_cast<int>(hkv), static_cast<int>(total_qtiles), a.prefill_splits);
   if (part_floats || pre_floats) {
@@ -251,7 +269,8 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
     e = hb::attn_decode_launch(a, static_cast<int>(total_splits), st);
     if (e != cudaSuccess) return cuda_status(e);
   }
-  return cuda_status(hb::attn_prefill_launch(a, static_cast<int>(total_qtiles), st));
+  return cuda_status(tc ? hb::attn_prefill_tc_launch(maps, a, static_cast<int>(total_qtiles), st)
+                        : hb::attn_prefill_launch(a, static_cast<int>(total_qtiles), st));
 }
 
 hllm_b200_status hllm_b200_qkv_post(const float* qkv, uint64_t tokens, uint32_t hq, uint32_t hkv,

@@ -20,6 +20,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -177,6 +178,11 @@ struct hllm_b200_stage {
   size_t pre_counter_ints = 0;
   int max_qtiles = 0;
   hb::GemmInput in_xn{}, in_attn{}, in_act{}, in_xs{};
+  // Prefill attention on tcgen05 (head sizes 64/128): per-layer TMA maps of
+  // the query buffer and the layer's K/V caches.  HLLM_B200_TC_PREFILL=0
+  // selects the mma.sync kernel instead (for comparisons).
+  bool tc_prefill = false;
+  std::vector<hb::TcMaps> tc_maps;
   float* slots = nullptr;        // stream-K GEMM partial tiles
   int* tile_counters = nullptr;  // their per-tile completion counters (kept at zero)
 
@@ -580,6 +586,23 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
   }
   s->slots = s->alloc<float>(hb::gemm_max_slot_floats(s->sm_count));
   s->tile_counters = s->alloc<int>(hb::kGemmCounterInts);
+  {
+    const char* env = std::getenv("HLLM_B200_TC_PREFILL");
+    s->tc_prefill = hb::attn_prefill_tc_supported(static_cast<int>(s->dim),
+                                                  static_cast<int>(s->hq / s->hkv)) &&
+                    !(env && env[0] == '0');
+    if (s->tc_prefill) {
+      s->tc_maps.resize(std::max<size_t>(1, s->n_layers));
+      for (size_t li = 0; li < s->n_layers; ++li) {
+        const __half* kc = s->kv + li * s->kv_layer_elems;
+        if (!hb::attn_tc_make_maps(&s->tc_maps[li], s->q, static_cast<long long>(T),
+                                   static_cast<int>(s->hq), static_cast<int>(s->hkv),
+                                   static_cast<int>(s->dim), kc, kc + s->kv_layer_elems / 2,
+                                   static_cast<long long>(s->num_blocks)))
+          fail(HLLM_B200_INTERNAL, "tensor map creation failed");
+      }
+    }
+  }
   if (!hb::gemm_make_input(&s->in_xn, s->xn, static_cast<int>(T), static_cast<int>(s->h_pad),
                            static_cast<int>(s->h_pad)) ||
       !hb::gemm_make_input(&s->in_attn, s->attn, static_cast<int>(T), static_cast<int>(s->qw_pad),
@@ -761,7 +784,10 @@ StepPlan plan_step(hllm_b200_stage* s, const hllm_b200_row* rows, uint32_t n, bo
     if (rows[i].tokens > 1)
       p.total_qtiles += static_cast<int>((rows[i].tokens + p.qtile_tokens - 1) / p.qtile_tokens);
   if (p.total_qtiles > s->max_qtiles) fail(HLLM_B200_INTERNAL, "prefill tiles exceed the workspace");
-  {
+  if (s->tc_prefill) {
+    p.prefill_splits = hb::attn_prefill_tc_splits(static_cast<int>(s->hkv), p.total_qtiles,
+                                                  s->sm_count);
+  } else {
     hb::AttnArgs probe{};
     probe.max_blocks = static_cast<int>(s->max_blocks);
     p.prefill_splits = hb::attn_prefill_splits(static_cast<int>(s->dim), static_cast<int>(s->hkv),
@@ -970,7 +996,9 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
       s->launches += hb::attn_decode_launches(static_cast<int>(s->dim)) - 1;  // combine pass
     }
     if (p.total_qtiles)
-      PLAUNCH(kProfAttnPrefill, p.attn_pre_bytes, p.attn_pre_flops, hb::attn_prefill_launch(aa, p.total_qtiles, s->stream));
+      PLAUNCH(kProfAttnPrefill, p.attn_pre_bytes, p.attn_pre_flops,
+              s->tc_prefill ? hb::attn_prefill_tc_launch(s->tc_maps[li], aa, p.total_qtiles, s->stream)
+                            : hb::attn_prefill_launch(aa, p.total_qtiles, s->stream));
     // o_proj adds itself into the residual stream, then the post-attention RMSNorm.
     const hb::GemmPlan po = hb::gemm_plan(L.g_o, T, s->sm_count);
     PLAUNCH(gk, gemm_bytes(s->h, T, s->qw, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->qw, 1),

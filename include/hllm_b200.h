@@ -397,16 +397,19 @@ hllm_b200_status hllm_b200_pack(const int32_t* row_slot, const int32_t* row_firs
                                 int32_t* cu_qtiles, uint32_t* status, void* stream);
 
 /* Paged GQA attention over a packed batch (reference `attention`,
- * cpp/src/cpu/llama.cpp:67-112).  q F16 [tokens][Hq*d]; caches F16
- * [blocks][Hkv][16][d]; packer outputs as above; out F16 [tokens][ld_out].
+ * cpp/src/cpu/llama.cpp:67-112).  q F16 [q_tokens][Hq*d]; caches F16
+ * [kv_blocks][Hkv][16][d]; packer outputs as above; out F16 [tokens][ld_out].
  * Decode rows (one token): for head sizes 64/128/256 the decode rows' KV
  * pages are split evenly over one wave of warps and the pieces of each
  * (row, kv head) are merged by its last warp (cu_splits and split_tokens only
  * bound the work); other head sizes use split-K over `split_tokens`-key
- * splits.  Prefill rows: causal tensor-core tiles of
- * hllm_b200_attention_qtile_tokens(Hq/Hkv) tokens, each tile's keys split over
- * CTAs that fill one wave.  Split outputs and arrival counters live in a
- * per-device workspace that the first call allocates. */
+ * splits.  Prefill rows: causal tiles of hllm_b200_attention_qtile_tokens(
+ * Hq/Hkv) tokens, each tile's keys split over CTAs that fill one wave; for
+ * head sizes 64 and 128 (GQA groups 1/2/4/8) on tcgen05 with S and O in TMEM
+ * and TMA-fed K/V pages (q_tokens and kv_blocks bound the TMA maps; 0 selects
+ * the mma.sync tiles, as HLLM_B200_TC_PREFILL=0 does).  Split outputs and
+ * arrival counters live in a per-device workspace that the first call
+ * allocates. */
 hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
                                      const uint16_t* v_cache, const int32_t* row_first,
                                      const int32_t* row_count, const int32_t* cu_seqlens,
@@ -415,7 +418,8 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
                                      uint32_t rows, uint32_t total_splits, uint32_t total_qtiles,
                                      uint32_t hq, uint32_t hkv, uint32_t dim, uint32_t max_blocks,
                                      uint32_t split_tokens, uint16_t* out, uint64_t ld_out,
-                                     uint32_t* status, void* stream);
+                                     uint64_t q_tokens, uint64_t kv_blocks, uint32_t* status,
+                                     void* stream);
 /* Query tokens per prefill tile for a GQA group size (128 query rows per
  * tile: 128 / group tokens). */
 uint32_t hllm_b200_attention_qtile_tokens(uint32_t group);

@@ -137,7 +137,7 @@ def attn_case(rows_ctx, hq=32, hkv=8, d=128, split=256, iters=10, cold=False):
     def fn():
         _lib.check(L.hllm_b200_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                          *[t.data_ptr() for t in dv], R, int(cu_s[-1]), 0, hq,
-                                         hkv, d, mb, split, out.data_ptr(), hq * d,
+                                         hkv, d, mb, split, out.data_ptr(), hq * d, R, nblocks,
                                          status.data_ptr(), stream))
     us = ev_time(fn, iters, cold=cold)
     nbytes = sum(rows_ctx) * hkv * d * 2 * 2 + R * hq * d * 4
@@ -178,7 +178,7 @@ def prefill_case(first, count, rows=1, hq=32, hkv=8, d=128, iters=10):
     def fn():
         _lib.check(L.hllm_b200_attention(q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                          *[t.data_ptr() for t in dv], rows, 0, rows * tiles, hq,
-                                         hkv, d, need, 16, out.data_ptr(), hq * d,
+                                         hkv, d, need, 16, out.data_ptr(), hq * d, T, nblocks,
                                          status.data_ptr(), stream))
     us = ev_time(fn, iters)
     pairs = rows * (count * first + count * (count + 1) / 2)

@@ -281,8 +281,8 @@ def run_attention(kc, vc, q, tables, rows_spec, hq, hkv, d, split):
     keep = [dev(x) for x in (q, kc, vc, row_first, row_count, cu, ctx.astype(np.int32), tables,
                              cu_s, cu_q)]
     check(lib().hllm_b200_attention(*[ptr(t) for t in keep], R, int(cu_s[-1]), int(cu_q[-1]), hq,
-                                    hkv, d, tables.shape[1], split, ptr(out), hq * d, ptr(status),
-                                    stream()))
+                                    hkv, d, tables.shape[1], split, ptr(out), hq * d, T,
+                                    kc.shape[0], ptr(status), stream()))
     sync()
     assert int(host(status)[0]) == 0
     return f16_vals(host(out, np.uint16))
@@ -331,6 +331,85 @@ def test_decode_attention_split_invariance_long_context(split):
     got = run_attention(kc, vc, q, tables, rows_spec, hq, hkv, d, split=split)
     ref = oracle_attention(kc, vc, q, tables, rows_spec, hq, hkv, d)
     np.testing.assert_allclose(got, ref, rtol=5e-3, atol=3e-3)
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 8)])
+def test_prefill_attention_long_chunks(hq, hkv):
+    """512-token chunks at configuration 3's positions (first chunk, last chunk
+    of a 4,096-token prompt) and a short chunk, one batch: many key tiles per
+    query tile and key splits merged across CTAs."""
+    d = 128
+    rng = np.random.default_rng(hq + 7)
+    rows_spec = [(0, 512), (3584, 512), (1000, 100), (777, 1)]
+    kc, vc, q, tables = attention_case(rng, hq, hkv, d, rows_spec)
+    got = run_attention(kc, vc, q, tables, rows_spec, hq, hkv, d, split=256)
+    ref = oracle_attention(kc, vc, q, tables, rows_spec, hq, hkv, d)
+    np.testing.assert_allclose(got, ref, rtol=5e-3, atol=3e-3)
+
+
+def oracle_row(kpages, vpages, q_row, ctx, hq, hkv, d):
+    """The oracle's attention for one decode row whose pages are given in
+    order ([pages][Hkv][16][d] F16 bits)."""
+    K = f16_vals(kpages).transpose(0, 2, 1, 3).reshape(-1, hkv, d)[:ctx]
+    V = f16_vals(vpages).transpose(0, 2, 1, 3).reshape(-1, hkv, d)[:ctx]
+    kk, vv = np.ascontiguousarray(K), np.ascontiguousarray(V)
+    cfg = oracle.Config(hq * d, 1, hq, hkv, d, 1 << 20, 1e-6, 1e4, 0)
+    kv = oracle.KV(ctx, hkv, d, ctx, oracle.fp(kk), oracle.fp(vv))
+    qr = np.ascontiguousarray(f16_vals(q_row)[None, :])
+    out = np.zeros((1, hq * d), np.float32)
+    oracle.lib().oracle_attention(oracle.fp(qr), 1, C.byref(cfg), ctx - 1, C.byref(kv),
+                                  oracle.fp(out))
+    return out[0]
+
+
+@pytest.mark.parametrize("B", [128, 256])
+def test_decode_attention_configuration5_batches(B):
+    """Configuration 5 at full size: B decode rows (Qwen3-4B heads), contexts
+    log-uniform over [128, 32768] (one row at each end), pages randomly placed
+    in a pool 1.2x the KV, Q/K/V ~ N(0,1)/sqrt(128) generated on the device.
+    Every row runs; twelve rows, the longest and shortest among them, are
+    checked against the oracle."""
+    torch = torch_cuda()
+    hq, hkv, d = 32, 8, 128
+    rng = np.random.default_rng(B)
+    ctx = np.exp(rng.uniform(np.log(128), np.log(32768), B)).astype(np.int64)
+    ctx[0], ctx[1] = 32768, 128
+    need = (ctx + 15) // 16
+    nblocks = int(need.sum() * 1.2) + 1
+    perm = rng.permutation(nblocks)[:need.sum()].astype(np.int32)
+    mb = int(need.max())
+    tables = np.full((B, mb), -1, np.int32)
+    off = np.concatenate([[0], np.cumsum(need)])
+    for r in range(B):
+        tables[r, :need[r]] = perm[off[r]:off[r + 1]]
+    gen = torch.Generator(device="cuda").manual_seed(B)
+    scale = 1.0 / math.sqrt(d)
+    kc = (torch.randn((nblocks, hkv, 16, d), generator=gen, device="cuda") * scale).half()
+    vc = (torch.randn((nblocks, hkv, 16, d), generator=gen, device="cuda") * scale).half()
+    q = (torch.randn((B, hq * d), generator=gen, device="cuda") * scale).half()
+    row_first = (ctx - 1).astype(np.int32)
+    row_count = np.ones(B, np.int32)
+    cu = np.arange(B + 1, dtype=np.int32)
+    split = 512
+    sp = (ctx + split - 1) // split
+    cu_s = np.concatenate([[0], np.cumsum(sp)]).astype(np.int32)
+    cu_q = np.zeros(B + 1, np.int32)
+    out = torch.zeros((B, hq * d), dtype=torch.int16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    keep = [dev(x) for x in (row_first, row_count, cu, ctx.astype(np.int32), tables, cu_s, cu_q)]
+    check(lib().hllm_b200_attention(ptr(q), ptr(kc), ptr(vc), *[ptr(t) for t in keep], B,
+                                    int(cu_s[-1]), 0, hq, hkv, d, mb, split, ptr(out), hq * d, B,
+                                    nblocks, ptr(status), stream()))
+    sync()
+    assert int(host(status)[0]) == 0
+    got = f16_vals(host(out, np.uint16))
+    assert np.isfinite(got).all()
+    kcv, vcv, qv = kc.view(torch.int16), vc.view(torch.int16), q.view(torch.int16)
+    for r in [0, 1] + list(rng.choice(np.arange(2, B), 10, replace=False)):
+        pages = torch.from_numpy(tables[r, :need[r]].astype(np.int64)).cuda()
+        ref = oracle_row(host(kcv[pages], np.uint16), host(vcv[pages], np.uint16),
+                         host(qv[r], np.uint16), int(ctx[r]), hq, hkv, d)
+        np.testing.assert_allclose(got[r], ref, rtol=5e-3, atol=3e-3, err_msg=f"row {r}")
 
 
 # ----------------------------------------------------------------------------- sampler
