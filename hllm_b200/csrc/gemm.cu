@@ -119,14 +119,14 @@ __device__ __forceinline__ int2 tile_ctas(const GemmParams& p, int tile, int gri
                    static_cast<int>(((u0 + p.kb_count) * G - 1) / p.units));
 }
 
-// Stream-K fixup by the CTA that completed `tile` (128 epilogue threads): the
-// tile's segments, slots of CTAs c0..c1, are added in CTA order and the sum
-// goes through the epilogue.  Thread t covers features 4 (t % 32) .. + 3 of
-// the tile and every fourth token column from t / 32, with float4 loads of
-// all segments issued before they are added.
+// Stream-K fixup of columns [cb, ce) of `tile` by one of its CTAs (128
+// epilogue threads): the tile's segments, slots of CTAs c0..c1, are added in
+// CTA order and the sum goes through the epilogue.  Thread t covers features
+// 4 (t % 32) .. + 3 of the tile and every fourth column from cb + t / 32, with
+// the float4 loads of all segments issued before they are added.
 template <int BN, int NA>
 __device__ __noinline__ void stream_k_fixup(const GemmParams& p, int tile, int c0, int c1,
-                                            int grid, int t) {
+                                            int cb, int ce, int grid, int t) {
   const int nseg = c1 - c0 + 1;
   const float* seg[kGemmMaxSegsPerTile];
 #pragma unroll
@@ -139,8 +139,8 @@ __device__ __noinline__ void stream_k_fixup(const GemmParams& p, int tile, int c
   const int q = (t & 31) * 4;
   const int m = m_tile * kGemmBlockM + q;
   const int n0 = n_tile * BN;
-  const int nvalid = min(BN, p.n - n0);
-  for (int col = t >> 5; col < nvalid; col += 4) {
+  ce = min(ce, p.n - n0);
+  for (int col = cb + (t >> 5); col < ce; col += 4) {
     float4 v0[kGemmMaxSegsPerTile], v1[kGemmMaxSegsPerTile];
 #pragma unroll
     for (int s = 0; s < kGemmMaxSegsPerTile; ++s) {
@@ -172,6 +172,22 @@ __device__ __noinline__ void stream_k_fixup(const GemmParams& p, int tile, int c
   }
 }
 
+// Waits (bounded) until *ctr reaches `target`; false and the timeout bit on
+// *status if it does not within kWaitLimitNs.
+__device__ __forceinline__ bool wait_count(const int* ctr, int target, uint32_t* status) {
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if ((i & 63u) == 63u && globaltimer_ns() - start > kWaitLimitNs) {
+      atomicOr(status, kDevWaitTimeout);
+      return false;
+    }
+    __nanosleep(100);
+  }
+}
+
 template <int BN, int NA>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
@@ -186,7 +202,6 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  int* fix_first = reinterpret_cast<int*>(tmem_slot + 1);  // stream-K: completing CTA's c0, or -1
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -340,24 +355,33 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(&tempty[b]);  // the accumulator is free for the next segment
       if (slot) {
-        // Count this segment in at its tile; the CTA that brings the count to
-        // the tile's segment total reduces the tile.  The release fence makes
-        // this CTA's slot visible before its count; the completing CTA's fence
-        // after the count orders its slot reads after every other count.
+        // Count this segment in at its tile (release: the slot is visible
+        // before the count).
         __threadfence();
         named_bar_sync(1, 128);
-        if (t == 0) {
-          const int2 cs = tile_ctas(p, sg.tile, grid);
-          const int landed_segs = atomicAdd(p.counters + sg.tile, 1) + 1;
-          const bool last = landed_segs == cs.y - cs.x + 1;
-          if (last) p.counters[sg.tile] = 0;  // ready for the next launch
-          *fix_first = last ? cs.x : -1;
-        }
+        if (t == 0) atomicAdd(p.counters + 2 * sg.tile, 1);
+      }
+    }
+    if (p.stream_k) {
+      // Every CTA of the grid is resident (one per SM) and has written all of
+      // its slots before any waits, so each tile's CTAs meet at its counter
+      // and split the reduction: CTA c0 + k adds columns [BN k / nseg,
+      // BN (k + 1) / nseg) of the tile's segments in CTA order.  The last CTA
+      // to finish a tile returns both of its counters to zero.
+      cursor = ub;
+      for (int j = 0; next_segment(p, cursor, ue, j, sg); ++j) {
+        const int2 cs = tile_ctas(p, sg.tile, grid);
+        const int nseg = cs.y - cs.x + 1;
+        const int k = static_cast<int>(blockIdx.x) - cs.x;
+        bool arrived = true;
+        if (t == 0) arrived = wait_count(p.counters + 2 * sg.tile, nseg, p.status);
+        if (!named_bar_all(1, 128, t != 0 || arrived)) break;
+        __threadfence();
+        stream_k_fixup<BN, NA>(p, sg.tile, cs.x, cs.y, BN * k / nseg, BN * (k + 1) / nseg, grid, t);
         named_bar_sync(1, 128);
-        if (*fix_first >= 0) {
-          __threadfence();
-          const int2 cs = tile_ctas(p, sg.tile, grid);
-          stream_k_fixup<BN, NA>(p, sg.tile, cs.x, cs.y, grid, t);
+        if (t == 0 && atomicAdd(p.counters + 2 * sg.tile + 1, 1) == nseg - 1) {
+          p.counters[2 * sg.tile] = 0;
+          p.counters[2 * sg.tile + 1] = 0;
         }
       }
     }
@@ -461,6 +485,9 @@ GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override, in
   grid = std::max<long long>(1, std::min<long long>(grid, pl.units));
   pl.stream_k = pl.tiles < 2 * grid;
   if (pl.stream_k) {
+    // The tile reduction has each tile's CTAs wait for one another: they must
+    // all be resident, one CTA per SM.
+    grid = std::min<long long>(grid, sm_count);
     // Each tile's segments must fit the consumer's segment list, and the
     // segment map holds a bounded number of tiles.
     grid = std::min<long long>(grid, pl.tiles * (kGemmMaxSegsPerTile - 2));

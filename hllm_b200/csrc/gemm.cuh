@@ -12,11 +12,12 @@
 //               applies the epilogue itself;
 //   stream-K -- (fewer tiles) the tiles' K blocks are dealt out evenly to one
 //               CTA per SM; each CTA writes the F32 sums of its (at most three)
-//               tile segments to its own slots and counts itself in at the
-//               tile's counter.  The CTA that completes a tile adds the tile's
-//               slots in CTA order -- a fixed order, so results do not depend
-//               on which CTA finishes last -- applies the epilogue and returns
-//               the counter to zero.  No CTA waits on another.
+//               tile segments to its own slots and counts itself in at each
+//               tile's counter.  Once a tile's CTAs have all counted in (they
+//               are all resident: one CTA per SM), each adds its share of the
+//               tile's columns over the tile's slots in CTA order -- a fixed
+//               order, so results do not depend on timing -- and applies the
+//               epilogue.  Waits are bounded.
 #pragma once
 
 #include <cuda.h>
@@ -71,9 +72,9 @@ struct GemmPlan {
 // this) and tiles per plan (more tiles than this always run direct).
 constexpr int kGemmMaxSegsPerTile = 16;
 constexpr int kGemmMaxStreamKTiles = 512;
-// Ints of per-tile completion counters a stream-K launch needs (zero before
-// the first launch; every launch leaves them zero).
-constexpr size_t kGemmCounterInts = kGemmMaxStreamKTiles;
+// Ints of per-tile counters (arrivals, departures) a stream-K launch needs
+// (zero before the first launch; every launch leaves them zero).
+constexpr size_t kGemmCounterInts = 2 * kGemmMaxStreamKTiles;
 
 GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override = 0,
                    int grid_override = 0);
