@@ -54,7 +54,6 @@ METRIC = "Qwen3-4B F16 ragged-batch tokens/s at 1/2/4/8 B200; p50 TTFT; HBM GB/s
 SEED = 20261201
 MAX_ACTIVE = 64
 CHUNK = 512
-GEN_FRACTION = 288.0 / 1128.0  # generated share of processed tokens in the trace (sets LM-head work)
 PIPELINE_LIMIT_S = 300.0  # wall-clock limit of a multi-GPU (pipeline) run
 
 
@@ -368,6 +367,59 @@ def run_host_phase(stage, cfg, trace, steps, first_timed, K):
     return ms, tokens, generated, h2d / max(1, K), d2h / max(1, K), ttft
 
 
+def run_arrival_phase(stage, cfg, seconds: float = 4.0):
+    """Open-loop TTFT: requests arrive at their trace's Poisson times (8 req/s)
+    in wall-clock time, are admitted once arrived (at most 64 running), and
+    run through the public call; TTFT = first token - arrival, for requests
+    that arrive within `seconds`.  Returns (ttft ms list, steps run)."""
+    from hllm_b200 import DecodeBatchItem, TokenInput
+    from hllm_b200.workload import MixedPlanner, make_trace
+    V = cfg.vocabulary_size
+    trace = make_trace(SEED + 7)
+    planner = MixedPlanner(trace, max_active=MAX_ACTIVE, prefill_budget=CHUNK)
+    seqs, last_tok, ttft = {}, {}, []
+    t0 = time.perf_counter()
+    steps = 0
+    while True:
+        now = time.perf_counter() - t0
+        planner.admit(on_admit=lambda r: seqs.__setitem__(r.rid, stage.allocate_sequence(r.capacity)),
+                      until=now)
+        rows = planner.plan()
+        if not rows:
+            nxt = planner.trace[planner.next_req].arrival if planner.next_req < len(trace) else None
+            if nxt is None or nxt > seconds:
+                break
+            time.sleep(max(0.0, nxt - now))
+            continue
+        items = []
+        for row in rows:
+            r, s = row.req, seqs[row.req.rid]
+            if row.decode:
+                ids = [last_tok[r.rid]]
+                s.prefill_only = False
+            else:
+                ids = prompt_ids(r.rid, r.prompt_len, V)[row.first_position:
+                                                         row.first_position + row.tokens].tolist()
+                s.prefill_only = not row.sample
+            items.append(DecodeBatchItem(TokenInput(ids), row.first_position, s))
+        outs = stage.execute_mixed_batch(items)
+        done_t = time.perf_counter() - t0
+        steps += 1
+        for row, out in zip(rows, outs):
+            if row.sample:
+                last_tok[row.req.rid] = out.id
+                if not row.decode and row.req.arrival <= seconds:
+                    ttft.append((done_t - row.req.arrival) * 1e3)
+        for r in planner.commit(rows):
+            stage.release(seqs.pop(r.rid))
+        if done_t > seconds and not any(r.arrival <= seconds and r.generated == 0
+                                        for r in planner.active):
+            break
+    for s in seqs.values():
+        stage.release(s)
+    return ttft, steps
+
+
 def reference_threads() -> int:
     """Host threads this process may run on."""
     try:
@@ -400,14 +452,44 @@ def _parallel(threads: int, fn) -> float:
     return wall
 
 
-class ReferenceSample:
-    """The reference CPU math on a bounded Qwen3-4B sample: one layer (the
-    model is 36 such layers) and the LM head, with one independent decode
-    stream per host thread.  The reference CPU stage is single-threaded
-    (cpp/src/cpu has no threading), so all host cores are used by running
-    streams side by side over the shared weights."""
+def workload_mix(steps, first_timed):
+    """The timed steps' token mix: decode rows' context lengths, prefill rows'
+    (first position, tokens), and the number of sampled rows."""
+    dec_ctx, pre_rows, samples = [], [], 0
+    for _, rows, _ in steps[first_timed:]:
+        for rid, first, count, sample, decode in rows:
+            if decode:
+                dec_ctx.append(first + 1)
+            else:
+                pre_rows.append((first, count))
+            samples += int(sample)
+    return dec_ctx, pre_rows, samples
 
-    def __init__(self, threads: int, tokens: int, use_ref=True):
+
+def _midpoints(values, n):
+    """n values at the quantile midpoints of `values` (sorted)."""
+    v = sorted(values)
+    return [v[min(len(v) - 1, (2 * i + 1) * len(v) // (2 * n))] for i in range(n)]
+
+
+class ReferenceSample:
+    """The reference CPU math on a bounded sample of the configuration-3
+    workload: one Qwen3-4B layer (the model is 36 such layers) and the LM head,
+    one independent stream per host thread.  The reference CPU stage is
+    single-threaded (cpp/src/cpu has no threading), so all host cores are used
+    by running streams side by side over the shared weights.
+
+    Stream i decodes at a context length taken from the timed GPU steps'
+    decode rows (their quantile midpoints) and prefills a short chunk at a
+    position taken from the timed steps' prefill tokens; each stream's KV cache
+    is first filled to that length with synthetic keys and values (the cost of
+    a step depends on the context length, not on the cached values).  Per-token
+    layer costs then give tokens/s for the timed steps' own mix of decode
+    tokens, prefill tokens and sampled rows."""
+
+    PREFILL_TOKENS = 8
+
+    def __init__(self, threads: int, mix, use_ref=True, decode_steps: int = 2):
         import oracle
         from hllm_b200.workload import QWEN3_4B as Q
         spec = oracle.ModelSpec(Q["hidden_size"], Q["intermediate_size"], Q["attention_heads"],
@@ -419,42 +501,90 @@ class ReferenceSample:
         self.kind = "reference" if (use_ref and oracle.ref() is not None) else "port"
         weights = oracle.synth_weights(spec, SEED, layers=[0])
         self.model = oracle.OracleModel(spec, weights, 0, 1, use_ref=(self.kind == "reference"))
+        dec_ctx, pre_rows, self.samples = mix
+        self.decode_tokens = len(dec_ctx)
+        self.prefill_tokens = sum(c for _, c in pre_rows)
+        pre_pos = [f + j for f, c in pre_rows for j in range(c)]
+        self.dec_ctx = _midpoints(dec_ctx, threads)
+        self.pre_pos = _midpoints(pre_pos, threads) if pre_pos else [0] * threads
         rng = np.random.default_rng(1)
-        self.x = (rng.standard_normal((4, spec.hidden_size)) * 0.02).astype(np.float32)
-        self.seqs = [self.model.new_sequence(tokens + 8) for _ in range(threads)]
-        self.pos = [4] * threads
-        _parallel(threads, lambda i: self.model.forward(self.x, 0, self.seqs[i]))  # 4-token context
+        self.x = (rng.standard_normal((self.PREFILL_TOKENS, spec.hidden_size)) * 0.02).astype(
+            np.float32)
+        cap = max(self.dec_ctx) + decode_steps + 8
+        self.dec_seqs, self.pos = [], []
+        for i, c in enumerate(self.dec_ctx):
+            seq = self.model.new_sequence(cap)
+            self.model.fill_context(seq, c - 1, seed=i)
+            self.dec_seqs.append(seq)
+            self.pos.append(c - 1)
         self.model.logits(self.x[:1])  # builds the reference's head matrix once (untimed)
 
     def decode(self, steps: int) -> float:
         """`steps` decode tokens through the layer on every stream; wall seconds."""
         def run(i):
             for _ in range(steps):
-                self.model.forward(self.x[:1], self.pos[i], self.seqs[i])
+                self.model.forward(self.x[:1], self.pos[i], self.dec_seqs[i])
                 self.pos[i] += 1
         return _parallel(self.threads, run)
+
+    def prefill(self) -> float:
+        """A PREFILL_TOKENS-token chunk through the layer on every stream, each at
+        its sampled position; wall seconds (cache fills are not timed)."""
+        seqs = []
+        for i, p in enumerate(self.pre_pos):
+            seq = self.model.new_sequence(p + self.PREFILL_TOKENS + 1)
+            if p:
+                self.model.fill_context(seq, p, seed=1000 + i)
+            seqs.append(seq)
+        wall = _parallel(self.threads,
+                         lambda i: self.model.forward(self.x, self.pre_pos[i], seqs[i]))
+        for seq in seqs:
+            self.model.free_sequence(seq)
+        return wall
 
     def head(self) -> float:
         """One LM-head row on every stream; wall seconds."""
         return _parallel(self.threads, lambda i: self.model.logits(self.x[:1]))
 
-    def tokens_per_s(self, layer_wall: float, steps: int, head_wall: float) -> float:
-        """Whole-model decode tokens/s: 36 token-layers plus GEN_FRACTION LM-head
-        rows per token, at the throughput all streams reached together."""
-        t_layer = layer_wall / (steps * self.threads)
+    def rates(self, dec_wall: float, steps: int, pre_wall: float, head_wall: float):
+        """(tokens/s over the timed mix, decode tokens/s, prefill tokens/s,
+        per-token-layer decode s, prefill s, per-row head s), all streams
+        together."""
+        t_dec = dec_wall / (steps * self.threads)
+        t_pre = pre_wall / (self.PREFILL_TOKENS * self.threads)
         t_head = head_wall / self.threads
-        return 1.0 / (self.spec.layers * t_layer + GEN_FRACTION * t_head)
+        L = self.spec.layers
+        total = L * (self.decode_tokens * t_dec + self.prefill_tokens * t_pre) + \
+            self.samples * t_head
+        mixed = (self.decode_tokens + self.prefill_tokens) / total
+        return (mixed, 1.0 / (L * t_dec + t_head), 1.0 / (L * t_pre), t_dec, t_pre, t_head)
+
+    def describe(self, t_dec, t_pre, t_head) -> str:
+        return (f"{self.threads} streams side by side (the reference CPU stage is "
+                f"single-threaded), one Qwen3-4B layer + the LM head, -O2 -ffp-contract=off: "
+                f"decode at the timed steps' context quantiles ({min(self.dec_ctx)}-"
+                f"{max(self.dec_ctx)} tokens, mean {np.mean(self.dec_ctx):.0f}) "
+                f"{t_dec * self.threads:.3f} s per token-layer per stream; a "
+                f"{self.PREFILL_TOKENS}-token prefill chunk at the timed prefill tokens' "
+                f"position quantiles (mean {np.mean(self.pre_pos):.0f}) "
+                f"{t_pre * self.threads:.3f} s per token-layer per stream; LM-head row "
+                f"{t_head * self.threads:.3f} s per stream; tokens/s = (decode + prefill tokens "
+                f"of the timed steps: {self.decode_tokens} + {self.prefill_tokens}) / (36 x token-"
+                f"layer costs + {self.samples} head rows), all streams together")
 
 
-def cpu_reference_sample(use_ref=True, layer_steps=3):
-    """(tokens/s, per-stream token-layer s, per-stream head-row s, kind, threads)
-    of a short ReferenceSample on all host threads."""
+def cpu_reference_sample(mix, use_ref=True, decode_steps=2):
+    """cpu_baseline of the timed mix on all host threads (a dict for the JSON line)."""
     threads = reference_threads()
-    ref = ReferenceSample(threads, layer_steps, use_ref)
-    wall = ref.decode(layer_steps)
+    ref = ReferenceSample(threads, mix, use_ref, decode_steps)
+    dec = ref.decode(decode_steps)
+    pre = ref.prefill()
     head = ref.head()
-    return (ref.tokens_per_s(wall, layer_steps, head), wall / layer_steps, head, ref.kind,
-            threads)
+    mixed, dec_rate, pre_rate, t_dec, t_pre, t_head = ref.rates(dec, decode_steps, pre, head)
+    return {"value": round(mixed, 5), "unit": "tokens/s", "cores": threads, "kind": ref.kind,
+            "decode_tokens_per_s": round(dec_rate, 5),
+            "prefill_tokens_per_s": round(pre_rate, 5),
+            "sample": ref.describe(t_dec, t_pre, t_head), "host_cores": host_cores()}
 
 
 def host_cores():
@@ -494,21 +624,17 @@ def ours(args, world, rank, local):
     # profile pass (events around every launch) for the roofline
     trace3, steps3 = plan_schedule(total_steps)
     _, _, _, prof, _ = run_device_phase(stage, cfg, trace3, steps3, first_timed, K, profile=True)
+    # open-loop arrivals for TTFT from each request's arrival
+    ttft_open, open_steps = run_arrival_phase(stage, cfg)
     stage.close()
     cpu = None
     if not args.no_cpu_baseline:
-        tps, t_layer, t_head, kind, threads = cpu_reference_sample()
-        cpu = {"value": round(tps, 5), "unit": "tokens/s", "cores": threads, "kind": kind,
-               "sample": (f"{threads} decode streams side by side (the reference CPU stage is "
-                          f"single-threaded), each 3 decode tokens through one Qwen3-4B layer "
-                          f"({t_layer:.3f} s per round of {threads}) + one LM-head row "
-                          f"({t_head:.3f} s per round), -O2 -ffp-contract=off; extrapolated as "
-                          f"36 layers + {GEN_FRACTION:.3f} LM-head rows per token"),
-               "host_cores": host_cores()}
+        cpu = cpu_reference_sample(workload_mix(steps, first_timed))
     hbm, _, tf_sust, _ = peaks()
     phases = phase_summary(*dev_steps, hbm, tf_sust)
     emit_line(args, 1, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d, d2h, ttft,
-              generated, prof, clock_info, cpu, parallelism="single stage", phases=phases)
+              generated, prof, clock_info, cpu, parallelism="single stage", phases=phases,
+              ttft_open=(ttft_open, open_steps))
 
 
 WORKLOAD = ("configuration 3: Qwen3-4B architecture with seeded random-init F16 weights "
@@ -524,7 +650,7 @@ def workload_config(world, parallelism, fast_forward):
 
 
 def emit_line(args, world, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d_step, d2h_step,
-              ttft, generated, prof, clock_info, cpu, parallelism, phases=None):
+              ttft, generated, prof, clock_info, cpu, parallelism, phases=None, ttft_open=None):
     """Prints the benchmark's JSON line (rank 0)."""
     K = args.steps
     steps_timed = K * world  # micro-batch steps completed in the timed region
@@ -572,7 +698,17 @@ def emit_line(args, world, dev_ms, dev_tokens, e2e_ms, e2e_tokens, launches, h2d
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(h2d_step), "d2h_bytes_per_step": int(d2h_step),
                 "ms_per_step": round(e2e_ms / steps_timed, 4)},
-        "ttft_p50_ms": round(statistics.median(ttft), 3) if ttft else None,
+        # open-loop TTFT (from arrival) where measured, else from admission
+        "ttft_p50_ms": (round(statistics.median(ttft_open[0]), 3)
+                        if ttft_open and ttft_open[0]
+                        else round(statistics.median(ttft), 3) if ttft else None),
+        "ttft": {"p50_ms": round(statistics.median(ttft_open[0]), 3),
+                 "p90_ms": round(float(np.percentile(ttft_open[0], 90)), 3),
+                 "requests": len(ttft_open[0]), "steps": ttft_open[1],
+                 "how": "open loop: requests arrive at their Poisson times (8 req/s) in wall-clock "
+                        "time for 4 s and run through the public call; first token - arrival"}
+                if ttft_open and ttft_open[0] else None,
+        "ttft_saturated_p50_ms": round(statistics.median(ttft), 3) if ttft else None,
         "output_tokens_per_s_e2e": round(generated / (e2e_ms / 1e3), 1),
         "roofline": roof, "kernels": kernels, "phases": phases, "cpu_baseline": cpu,
         "clocks": clock_info,
@@ -908,36 +1044,37 @@ def ours_pipeline(args, world, rank, local):
 
 def reference(args, world, rank):
     """The reference's CPU math as the baseline arm (rank 0 only), on all host
-    threads: one decode stream per thread through one Qwen3-4B layer, each
-    step one token on every stream, extrapolated to the model."""
+    threads, over the same timed steps' token mix as our arm: each step one
+    decode token through one Qwen3-4B layer on every stream (streams at the
+    timed steps' decode contexts), plus one prefill chunk and one LM-head row
+    per stream, weighted by the mix (ReferenceSample)."""
     if rank != 0:
         return
     import oracle
-    if oracle.ref() is None:
-        kind_note = "oracle/_ref absent: the C restatement of the reference CPU math"
-    else:
-        kind_note = "oracle/_ref: the reference's own CPU sources (-O2 -ffp-contract=off)"
+    W, K, F = args.warmup, args.steps, args.fast_forward
+    _, steps = plan_schedule(F + W + K)
     threads = reference_threads()
-    ref = ReferenceSample(threads, args.warmup + args.steps)
-    ref.decode(args.warmup)
-    wall = ref.decode(args.steps)
+    ref = ReferenceSample(threads, workload_mix(steps, F + W), decode_steps=W + K)
+    ref.decode(W)
+    wall = ref.decode(K)
+    pre = ref.prefill()
     head = ref.head()
-    value = ref.tokens_per_s(wall, args.steps, head)
+    value, dec_rate, pre_rate, t_dec, t_pre, t_head = ref.rates(wall, K, pre, head)
+    kind_note = ("oracle/_ref: the reference's own CPU sources" if oracle.ref() is not None
+                 else "oracle/_ref absent: the C restatement of the reference CPU math")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
+            "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(wall / K * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": workload_config(
-                world, f"reference CPU math on {threads} host threads, one decode stream each "
+                world, f"reference CPU math on {threads} host threads, one stream each "
                        f"(the reference CPU stage is single-threaded); a bounded sample of the "
-                       f"workload, see cpu_baseline.sample", args.fast_forward),
+                       f"workload, see cpu_baseline.sample", F),
             "cpu_baseline": {"value": round(value, 5), "unit": "tokens/s", "cores": threads,
-                             "kind": ref.kind,
-                             "sample": f"each step one decode token through one Qwen3-4B "
-                                       f"layer on each of {threads} streams ({kind_note}); "
-                                       f"tokens/s = 1 / (36 x step time / {threads} + "
-                                       f"{GEN_FRACTION:.3f} x LM-head round {head:.3f} s / "
-                                       f"{threads})"},
+                             "kind": ref.kind, "decode_tokens_per_s": round(dec_rate, 5),
+                             "prefill_tokens_per_s": round(pre_rate, 5),
+                             "sample": f"{kind_note}; each timed step one decode token per "
+                                       f"stream; " + ref.describe(t_dec, t_pre, t_head)},
             "e2e": {"value": round(value, 5), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

@@ -259,9 +259,13 @@ __global__ void __launch_bounds__(kDecThreads)
 // m16n8k16 tile (rows G..15 are zero), so QK^T and PV run on the tensor cores.
 // K/V pages (16 keys x d) stream through a per-warp cp.async ring in an
 // XOR-swizzled layout that ldmatrix reads without bank conflicts; a stream's
-// query heads ride in the ring stage of its first page.  The ring runs ahead
-// across stream boundaries, and block-table entries are fetched 32 pages at a
-// time, so no global load sits between one page and the next.
+// query heads ride in the ring stage of its first page.  One lane of the warp
+// fills the ring: each K and V page as 64-dimension TMA boxes of 16 keys with
+// the 128-byte swizzle (d / 64 boxes per page), the query heads as one bulk
+// copy, all completing on the stage's mbarrier; ldmatrix reads the swizzled
+// pages without bank conflicts.  The ring runs ahead across stream
+// boundaries, and block-table entries are fetched 32 pages at a time, so no
+// global load sits between one page and the next.
 // Ring depth: three stages (two pages in flight while one is computed); two
 // for d = 256, whose stages would not fit three deep in shared memory.
 template <int D>
@@ -269,14 +273,17 @@ __host__ __device__ constexpr int dec_stages() {
   return D >= 256 ? 2 : 3;
 }
 
+// Byte offset of 16-byte chunk `chunk` of key `row` in a page as the TMA boxes
+// write it: box chunk / 8 (2 KB each), rows of 128 bytes, chunk % 8 XOR row % 8.
 template <int D>
 __device__ __forceinline__ uint32_t page_off(int row, int chunk) {
-  return static_cast<uint32_t>(row * D * 2 + ((chunk ^ (row & 7)) * 16));
+  return static_cast<uint32_t>(((chunk >> 3) << 11) + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
 }
 
-// Bytes of one ring stage: K page, V page, the group's query heads.
+// Bytes of one ring stage: K page, V page, the group's query heads (1024-byte
+// multiples, so every page starts on a swizzle-atom boundary).
 __host__ __device__ constexpr uint32_t decode_stage_bytes(int d, int group) {
-  return 2u * 16u * d * 2u + ((static_cast<uint32_t>(group) * d * 2u + 127u) & ~127u);
+  return 2u * 16u * d * 2u + ((static_cast<uint32_t>(group) * d * 2u + 1023u) & ~1023u);
 }
 
 // Position in the page sequence: row, kv head, page within the stream, and
@@ -416,9 +423,12 @@ __device__ __noinline__ void decode_merge(const AttnArgs& a, size_t p0, int ns, 
 
 template <int D>
 __global__ void __launch_bounds__(128)
-    decode_attn_mma_kernel(const AttnArgs a) {
-  extern __shared__ __align__(128) uint8_t smem[];
+    decode_attn_mma_kernel(const __grid_constant__ TcMaps maps, const AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   constexpr uint32_t kPage = 16 * D * 2;  // bytes of one K (or V) page
+  constexpr int ST = dec_stages<D>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int w = blockIdx.x * 4 + warp;
   const int hkv = a.hkv;
@@ -477,7 +487,14 @@ __global__ void __launch_bounds__(128)
   }
   PageCursor ic = c;  // issue cursor, runs ahead of c
   const int n = static_cast<int>(p_end - p_begin);
-  uint8_t* ring = smem + warp * (dec_stages<D>() * stage_bytes);
+  uint8_t* ring = smem + warp * (ST * stage_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 4 * ST * stage_bytes) + warp * ST;
+  const uint32_t q_bytes = static_cast<uint32_t>(G) * D * 2;
+  if (lane == 0) {
+    for (int s = 0; s < ST; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
 
   // Block-table entries of the issue cursor's row, 32 pages per fetch.  The
   // first fetch, like everything above, reads only the packer's tables, so it
@@ -491,8 +508,9 @@ __global__ void __launch_bounds__(128)
                   : -1;
   }
   griddep_enter();
+  int issued = 0;
   auto issue = [&](int i) {
-    uint8_t* kd = ring + (i % dec_stages<D>()) * stage_bytes;
+    uint8_t* kd = ring + (i % ST) * stage_bytes;
     if (ic.r != tab_r || ic.q < tab_q0 || ic.q >= tab_q0 + 32) {
       tab_r = ic.r;
       tab_q0 = ic.q;
@@ -501,30 +519,29 @@ __global__ void __launch_bounds__(128)
                     ? __ldg(a.block_tables + static_cast<size_t>(ic.r) * a.max_blocks + qq)
                     : -1;
     }
-    const int bid = __shfl_sync(0xffffffffu, tab_val, ic.q - tab_q0);
-    if (i == 0 || ic.q == 0) {
-      // First page of a stream: its query heads ride along.
-      const __half* qs =
-          a.q + static_cast<size_t>(ic.t) * a.hq * D + static_cast<size_t>(ic.kvh) * G * D;
-      const uint32_t qd = smem_u32(kd + 2 * kPage);
-      for (int ch = lane; ch < G * D / 8; ch += 32) cp_async16(qd + ch * 16, qs + ch * 8);
-    }
+    const int bid_raw = __shfl_sync(0xffffffffu, tab_val, ic.q - tab_q0);
+    // First page of a stream: its query heads ride along.
+    const bool with_q = i == 0 || ic.q == 0;
+    const __half* qs =
+        a.q + static_cast<size_t>(ic.t) * a.hq * D + static_cast<size_t>(ic.kvh) * G * D;
     const int kvh = ic.kvh;
     cursor_next(a, ic);
-    if (bid < 0) {
-      if (lane == 0) atomicOr(a.status, kDevBadIndex);
-      return;
-    }
-    const size_t page = (static_cast<size_t>(bid) * hkv + kvh) * 16 * D;
-    const __half* ks = a.k_cache + page;
-    const __half* vs = a.v_cache + page;
-    const uint32_t kb = smem_u32(kd), vb = kb + kPage;
-    constexpr int kChunks = 16 * D / 8;  // 16-byte chunks per page
+    ++issued;
+    if (lane == 0) {
+      int bid = bid_raw;
+      if (bid < 0) {  // a missing block: reported, and a valid page read in its place
+        atomicOr(a.status, kDevBadIndex);
+        bid = 0;
+      }
+      const int y = (bid * hkv + kvh) * 16;
+      uint64_t* bar = &full[i % ST];
+      mbar_arrive_expect_tx(bar, 2 * kPage + (with_q ? q_bytes : 0u));
 #pragma unroll
-    for (int ch16 = lane; ch16 < kChunks; ch16 += 32) {
-      const int row = ch16 / (D / 8), ch = ch16 % (D / 8);
-      cp_async16(kb + page_off<D>(row, ch), ks + row * D + ch * 8);
-      cp_async16(vb + page_off<D>(row, ch), vs + row * D + ch * 8);
+      for (int h = 0; h < D / 64; ++h) {
+        tma_load_2d(kd + h * 2048, &maps.k, bar, h * 64, y);
+        tma_load_2d(kd + kPage + h * 2048, &maps.v, bar, h * 64, y);
+      }
+      if (with_q) bulk_load(kd + 2 * kPage, qs, q_bytes, bar);
     }
   };
 
@@ -535,16 +552,13 @@ __global__ void __launch_bounds__(128)
   float m = -INFINITY, l = 0.f;
 
 #pragma unroll
-  for (int i = 0; i < dec_stages<D>() - 1; ++i) {
+  for (int i = 0; i < ST - 1; ++i)
     if (i < n) issue(i);
-    cp_async_commit();
-  }
-  for (int i = 0; i < n; ++i) {
-    if (i + dec_stages<D>() - 1 < n) issue(i + dec_stages<D>() - 1);
-    cp_async_commit();
-    cp_async_wait<dec_stages<D>() - 1>();
-    __syncwarp();
-    const uint8_t* stage = ring + (i % dec_stages<D>()) * stage_bytes;
+  int i = 0;
+  for (; i < n; ++i) {
+    if (i + ST - 1 < n) issue(i + ST - 1);
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[i % ST], (i / ST) & 1u, a.status))) break;
+    const uint8_t* stage = ring + (i % ST) * stage_bytes;
     if (i == 0 || c.q == 0) {
       // A new stream: its query heads as A fragments, fresh softmax state.
       const uint8_t* qrow = stage + 2 * kPage + g * D * 2;
@@ -651,7 +665,9 @@ __global__ void __launch_bounds__(128)
     }
     cursor_next(a, c);
   }
-  cp_async_wait<0>();
+  // Pages still in flight land before the warp exits (only after a failed
+  // wait; bounded).
+  for (; i < issued; ++i) mbar_wait(&full[i % ST], (i / ST) & 1u, a.status);
 }
 
 // One CTA per (decode row, query head): merge the row's splits.
@@ -1090,9 +1106,10 @@ cudaError_t launch_prefill(const AttnArgs& a, int total_qtiles, cudaStream_t str
                           dim3(kPreThreads), S::kSmem + table, stream, a);
 }
 
+// Four warps' rings, their stage barriers and 1024 bytes of alignment slack.
 template <int D>
 size_t decode_mma_smem(int group) {
-  return static_cast<size_t>(4) * dec_stages<D>() * decode_stage_bytes(D, group);
+  return static_cast<size_t>(4) * dec_stages<D>() * (decode_stage_bytes(D, group) + 8) + 1024;
 }
 
 // Sets the kernel's shared-memory limit once and returns its resident CTAs per
@@ -1119,11 +1136,11 @@ int decode_mma_setup(int group) {
 }
 
 template <int D>
-cudaError_t launch_decode_mma(const AttnArgs& a, cudaStream_t stream) {
+cudaError_t launch_decode_mma(const AttnArgs& a, const TcMaps& maps, cudaStream_t stream) {
   const int group = a.hq / a.hkv;
   if (a.decode_ctas <= 0 || decode_mma_setup<D>(group) == 0) return cudaErrorInvalidValue;
   return launch_dependent(decode_attn_mma_kernel<D>, dim3(a.decode_ctas), dim3(128),
-                          decode_mma_smem<D>(group), stream, a);
+                          decode_mma_smem<D>(group), stream, maps, a);
 }
 
 }  // namespace
@@ -1148,7 +1165,8 @@ size_t attn_decode_part_floats(int rows, int hq, int hkv, int dim, int ctas) {
   return pieces * static_cast<size_t>(hq / hkv) * static_cast<size_t>(dim + 2);
 }
 
-cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t stream) {
+cudaError_t attn_decode_launch(const AttnArgs& a, const TcMaps& maps, int total_splits,
+                               cudaStream_t stream) {
   if (total_splits <= 0) return cudaSuccess;
   const int G = a.hq / a.hkv;
   if (G > kMaxGroup || a.dim % 4 != 0 || a.dim > 256 || G * a.dim / 4 > 4 * kDecThreads ||
@@ -1156,9 +1174,9 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t
     return cudaErrorInvalidValue;
   cudaError_t e;
   if (attn_decode_balanced(a.dim)) {
-    e = a.dim == 64    ? launch_decode_mma<64>(a, stream)
-        : a.dim == 128 ? launch_decode_mma<128>(a, stream)
-                       : launch_decode_mma<256>(a, stream);
+    e = a.dim == 64    ? launch_decode_mma<64>(a, maps, stream)
+        : a.dim == 128 ? launch_decode_mma<128>(a, maps, stream)
+                       : launch_decode_mma<256>(a, maps, stream);
   } else {
     // Other head sizes (e.g. the tiny fixtures): one CTA per (kv head, split).
     const size_t smem = kDecStages * 2 * 16 * a.dim * 2 +

@@ -9,7 +9,8 @@
 namespace hb {
 
 // TMA tensor maps of one layer's attention inputs: the query buffer (tcgen05
-// prefill) and the K and V caches, all with the 128-byte swizzle.
+// prefill) and the K and V caches (tcgen05 prefill and the balanced decode
+// pass), all with the 128-byte swizzle.
 struct TcMaps {
   CUtensorMap q;  // [tokens][Hq][d] F16, box 64 dims x group heads x 128/group tokens
   CUtensorMap k;  // [blocks * Hkv * 16][d] F16, box 64 dims x one 16-key page
@@ -49,10 +50,13 @@ int attn_qtile_tokens(int group);
 
 // Decode rows (one new token).  Head sizes 64/128/256: the decode rows' KV
 // pages are split evenly over 4 * decode_ctas warps regardless of row
-// lengths, and the pieces of a (row, kv head) are merged by its last warp to
-// finish (split_tokens/cu_splits unused).  Other head sizes: split-K over
+// lengths, each warp streaming its pages by TMA into its own ring, and the
+// pieces of a (row, kv head) are merged by its last warp to finish
+// (split_tokens/cu_splits unused).  Other head sizes: split-K over
 // split_tokens-key splits, one CTA per (kv head, split), then a combine pass.
-cudaError_t attn_decode_launch(const AttnArgs& a, int total_splits, cudaStream_t stream);
+// The balanced pass streams pages through maps.k / maps.v (attn_make_kv_maps).
+cudaError_t attn_decode_launch(const AttnArgs& a, const TcMaps& maps, int total_splits,
+                               cudaStream_t stream);
 int attn_decode_launches(int dim);
 bool attn_decode_balanced(int dim);
 // CTAs of the balanced decode pass (GQA group size `group` = Hq/Hkv) for

@@ -39,7 +39,7 @@ hllm_b200_status cuda_status(cudaError_t e) {
 // use and kept until the process exits.
 struct DeviceScratch {
   float* slots = nullptr;
-  int* counters = nullptr;
+  int* segmap = nullptr;
   uint32_t* status = nullptr;
   int sm_count = 0;
 };
@@ -56,8 +56,7 @@ hllm_b200_status scratch_for_device(DeviceScratch* out) {
     e = cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
       e = cudaMalloc(&s.slots, hb::gemm_max_slot_floats(s.sm_count) * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&s.counters, hb::kGemmCounterInts * sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(s.counters, 0, hb::kGemmCounterInts * sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&s.segmap, hb::kGemmMapInts * sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&s.status, 256);
     if (e == cudaSuccess) e = cudaMemset(s.status, 0, 256);
     if (e != cudaSuccess) {
@@ -102,15 +101,14 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
               " (use at most one CTA per SM)");
     return HLLM_B200_RESOURCE_EXHAUSTED;
   }
+  hb::GemmSlots slots{};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The tile counters start each call at zero, even after a kernel that ended
-  // early on a failed wait.
-  cudaError_t e = plan.stream_k
-                      ? cudaMemsetAsync(sc.counters, 0, hb::kGemmCounterInts * sizeof(int), s)
-                      : cudaSuccess;
-  if (e == cudaSuccess)
-    e = hb::gemm_launch(gw, gx, static_cast<int>(n), plan, static_cast<int>(epilogue), y,
-                        static_cast<int>(ldy), sc.slots, sc.counters, sc.status, s);
+  cudaError_t e = hb::gemm_launch(gw, gx, static_cast<int>(n), plan, static_cast<int>(epilogue), y,
+                                  static_cast<int>(ldy), sc.slots, sc.segmap, &slots, sc.status,
+                                  s);
+  if (e == cudaSuccess && plan.stream_k)
+    e = hb::gemm_finish_launch(slots, static_cast<int>(n), static_cast<int>(epilogue), y,
+                               static_cast<int>(ldy), s);
   return cuda_status(e);
 }
 
@@ -212,6 +210,18 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
                   hb::attn_prefill_tc_supported(static_cast<int>(dim), static_cast<int>(hq / hkv)) &&
                   !(env && env[0] == '0');
   hb::TcMaps maps{};
+  // The balanced decode pass reads its pages through TMA maps of the caches.
+  if (total_splits && hb::attn_decode_balanced(static_cast<int>(dim))) {
+    if (!kv_blocks) {
+      set_error("decode attention needs kv_blocks (the caches' extent)");
+      return HLLM_B200_INVALID_REQUEST;
+    }
+    if (!hb::attn_make_kv_maps(&maps, static_cast<int>(hkv), static_cast<int>(dim), k_cache,
+                               v_cache, static_cast<long long>(kv_blocks))) {
+      set_error("tensor map creation failed");
+      return HLLM_B200_INTERNAL;
+    }
+  }
   if (tc && !hb::attn_tc_make_maps(&maps, q, static_cast<long long>(q_tokens), static_cast<int>(hq),
                                    static_cast<int>(hkv), static_cast<int>(dim), k_cache, v_cache,
                                    static_cast<long long>(kv_blocks))) {
@@ -266,7 +276,7 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
     a.pre_part = base + kCounters + part_floats;
   }
   if (total_splits) {
-    e = hb::attn_decode_launch(a, static_cast<int>(total_splits), st);
+    e = hb::attn_decode_launch(a, maps, static_cast<int>(total_splits), st);
     if (e != cudaSuccess) return cuda_status(e);
   }
   return cuda_status(tc ? hb::attn_prefill_tc_launch(maps, a, static_cast<int>(total_qtiles), st)

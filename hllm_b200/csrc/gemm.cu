@@ -14,9 +14,8 @@
 // Work: a unit is one 64-wide K block of one output tile (128 weight rows x
 // BN tokens), tiles token-tile-fastest.  Direct plans give each CTA whole
 // tiles (c, c + G, ...) and apply the epilogue; stream-K plans give CTA c the
-// units [U*c/G, U*(c+1)/G), store each segment's F32 sums in the CTA's slot
-// for that tile, and the CTA that completes a tile reduces its slots in CTA
-// order and applies the epilogue (see gemm.cuh).
+// units [U*c/G, U*(c+1)/G) and store each segment's F32 sums in the CTA's slot
+// for that tile (see gemm.cuh).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -41,7 +40,8 @@ struct GemmParams {
   void* out;
   int ldo;
   float* slots;
-  int* counters;     // [tiles] segments of each stream-K tile that have landed
+  int* segmap;
+  int* segcount;
   uint32_t* status;
 };
 
@@ -107,84 +107,6 @@ __device__ __forceinline__ void apply_epilogue(const GemmParams& p, int n, int m
       const float s = a0 / (1.0f + expf(-a0));
       static_cast<__half*>(p.out)[idx] = __float2half_rn(s * a1);
     }
-  }
-}
-
-// CTAs that cover stream-K tile `tile`: c covers unit u iff
-// U*c/G <= u < U*(c+1)/G, i.e. c = floor(((u+1)G - 1)/U).
-__device__ __forceinline__ int2 tile_ctas(const GemmParams& p, int tile, int grid) {
-  const long long u0 = static_cast<long long>(tile) * p.kb_count;
-  const long long G = grid;
-  return make_int2(static_cast<int>(((u0 + 1) * G - 1) / p.units),
-                   static_cast<int>(((u0 + p.kb_count) * G - 1) / p.units));
-}
-
-// Stream-K fixup of columns [cb, ce) of `tile` by one of its CTAs (128
-// epilogue threads): the tile's segments, slots of CTAs c0..c1, are added in
-// CTA order and the sum goes through the epilogue.  Thread t covers features
-// 4 (t % 32) .. + 3 of the tile and every fourth column from cb + t / 32, with
-// the float4 loads of all segments issued before they are added.
-template <int BN, int NA>
-__device__ __noinline__ void stream_k_fixup(const GemmParams& p, int tile, int c0, int c1,
-                                            int cb, int ce, int grid, int t) {
-  const int nseg = c1 - c0 + 1;
-  const float* seg[kGemmMaxSegsPerTile];
-#pragma unroll
-  for (int s = 0; s < kGemmMaxSegsPerTile; ++s) {
-    const int c = min(c0 + s, c1);
-    const int tile0 = static_cast<int>(gemm_unit_begin(p.units, grid, c) / p.kb_count);
-    seg[s] = p.slots + static_cast<size_t>(c * kGemmSlotsPerCta + (tile - tile0)) * NA * BN * 128;
-  }
-  const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
-  const int q = (t & 31) * 4;
-  const int m = m_tile * kGemmBlockM + q;
-  const int n0 = n_tile * BN;
-  ce = min(ce, p.n - n0);
-  for (int col = cb + (t >> 5); col < ce; col += 4) {
-    float4 v0[kGemmMaxSegsPerTile], v1[kGemmMaxSegsPerTile];
-#pragma unroll
-    for (int s = 0; s < kGemmMaxSegsPerTile; ++s) {
-      if (s < nseg) {
-        v0[s] = __ldcg(reinterpret_cast<const float4*>(seg[s] + col * 128 + q));
-        if (NA == 2) v1[s] = __ldcg(reinterpret_cast<const float4*>(seg[s] + (BN + col) * 128 + q));
-      }
-    }
-    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
-#pragma unroll
-    for (int s = 0; s < kGemmMaxSegsPerTile; ++s) {
-      if (s < nseg) {
-        a0.x += v0[s].x;
-        a0.y += v0[s].y;
-        a0.z += v0[s].z;
-        a0.w += v0[s].w;
-        if (NA == 2) {
-          a1.x += v1[s].x;
-          a1.y += v1[s].y;
-          a1.z += v1[s].z;
-          a1.w += v1[s].w;
-        }
-      }
-    }
-    const float r0[4] = {a0.x, a0.y, a0.z, a0.w}, r1[4] = {a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      if (m + e < p.m) apply_epilogue(p, n0 + col, m + e, r0[e], r1[e]);
-  }
-}
-
-// Waits (bounded) until *ctr reaches `target`; false and the timeout bit on
-// *status if it does not within kWaitLimitNs.
-__device__ __forceinline__ bool wait_count(const int* ctr, int target, uint32_t* status) {
-  const uint64_t start = globaltimer_ns();
-  for (uint32_t i = 0;; ++i) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
-    if (v >= target) return true;
-    if ((i & 63u) == 63u && globaltimer_ns() - start > kWaitLimitNs) {
-      atomicOr(status, kDevWaitTimeout);
-      return false;
-    }
-    __nanosleep(100);
   }
 }
 
@@ -320,10 +242,7 @@ __global__ void __launch_bounds__(192, 1)
       const int n_tile = sg.tile % p.n_tiles, m_tile = sg.tile / p.n_tiles;
       const int b = j % S::kAccBufs;
       const uint32_t bph = (j / S::kAccBufs) & 1u;
-      const bool landed = mbar_wait(&tfull[b], bph, p.status);
-      // Stream-K epilogues meet at named barriers below, so a wait that ran
-      // out ends the loop for all 128 threads together.
-      if (p.stream_k ? !named_bar_all(1, 128, landed) : !landed) break;
+      if (!mbar_wait(&tfull[b], bph, p.status)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + b * NA * BN;
       const int m = m_tile * kGemmBlockM + t;
@@ -333,6 +252,17 @@ __global__ void __launch_bounds__(192, 1)
       if (p.stream_k) {
         const int slot_id = static_cast<int>(blockIdx.x) * kGemmSlotsPerCta + (sg.tile - first_tile);
         slot = p.slots + static_cast<size_t>(slot_id) * NA * BN * 128;
+        if (t == 0) {
+          // Record this slot in the tile's segment list (CTA order): CTA c covers
+          // unit u iff U*c/G <= u < U*(c+1)/G, i.e. c = floor(((u+1)G - 1)/U).
+          const long long u0 = static_cast<long long>(sg.tile) * p.kb_count;
+          const long long G = grid;
+          const int c_first = static_cast<int>(((u0 + 1) * G - 1) / p.units);
+          const int c_last = static_cast<int>(((u0 + p.kb_count) * G - 1) / p.units);
+          const int pos = static_cast<int>(blockIdx.x) - c_first;
+          p.segmap[sg.tile * kGemmMaxSegsPerTile + pos] = slot_id;
+          if (pos == 0) p.segcount[sg.tile] = c_last - c_first + 1;
+        }
       }
       for (int c = 0; c < BN / 16; ++c) {
         if (c * 16 >= nvalid) break;
@@ -353,37 +283,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty[b]);  // the accumulator is free for the next segment
-      if (slot) {
-        // Count this segment in at its tile (release: the slot is visible
-        // before the count).
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (t == 0) atomicAdd(p.counters + 2 * sg.tile, 1);
-      }
-    }
-    if (p.stream_k) {
-      // Every CTA of the grid is resident (one per SM) and has written all of
-      // its slots before any waits, so each tile's CTAs meet at its counter
-      // and split the reduction: CTA c0 + k adds columns [BN k / nseg,
-      // BN (k + 1) / nseg) of the tile's segments in CTA order.  The last CTA
-      // to finish a tile returns both of its counters to zero.
-      cursor = ub;
-      for (int j = 0; next_segment(p, cursor, ue, j, sg); ++j) {
-        const int2 cs = tile_ctas(p, sg.tile, grid);
-        const int nseg = cs.y - cs.x + 1;
-        const int k = static_cast<int>(blockIdx.x) - cs.x;
-        bool arrived = true;
-        if (t == 0) arrived = wait_count(p.counters + 2 * sg.tile, nseg, p.status);
-        if (!named_bar_all(1, 128, t != 0 || arrived)) break;
-        __threadfence();
-        stream_k_fixup<BN, NA>(p, sg.tile, cs.x, cs.y, BN * k / nseg, BN * (k + 1) / nseg, grid, t);
-        named_bar_sync(1, 128);
-        if (t == 0 && atomicAdd(p.counters + 2 * sg.tile + 1, 1) == nseg - 1) {
-          p.counters[2 * sg.tile] = 0;
-          p.counters[2 * sg.tile + 1] = 0;
-        }
-      }
+      mbar_arrive(&tempty[b]);
     }
   }
 
@@ -391,6 +291,26 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 5) tmem_dealloc(tmem_base, S::kTmemCols);
+}
+
+// ---------------------------------------------------------------- generic consumer
+__global__ void gemm_finish_kernel(const GemmSlots s, int rows, int epilogue, void* out, int ldo) {
+  griddep_enter();
+  const int n = blockIdx.y;
+  if (n >= rows) return;
+  for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < s.m; m += gridDim.x * blockDim.x) {
+    const float a0 = gemm_slot_sum(s, n, m, 0);
+    const size_t idx = static_cast<size_t>(n) * ldo + m;
+    switch (epilogue) {
+      case kEpiStoreF32: static_cast<float*>(out)[idx] = a0; break;
+      case kEpiStoreF16: static_cast<__half*>(out)[idx] = __float2half_rn(a0); break;
+      case kEpiResidual: static_cast<float*>(out)[idx] += a0; break;
+      default: {
+        const float a1 = gemm_slot_sum(s, n, m, 1);
+        static_cast<__half*>(out)[idx] = __float2half_rn(a0 / (1.0f + expf(-a0)) * a1);
+      }
+    }
+  }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -485,9 +405,6 @@ GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override, in
   grid = std::max<long long>(1, std::min<long long>(grid, pl.units));
   pl.stream_k = pl.tiles < 2 * grid;
   if (pl.stream_k) {
-    // The tile reduction has each tile's CTAs wait for one another: they must
-    // all be resident, one CTA per SM.
-    grid = std::min<long long>(grid, sm_count);
     // Each tile's segments must fit the consumer's segment list, and the
     // segment map holds a bounded number of tiles.
     grid = std::min<long long>(grid, pl.tiles * (kGemmMaxSegsPerTile - 2));
@@ -509,12 +426,11 @@ size_t gemm_max_slot_floats(int sm_count) {
 }
 
 cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const GemmPlan& pl,
-                        int epilogue, void* out, int ldo, float* slots, int* tile_counters,
-                        uint32_t* status, cudaStream_t stream) {
+                        int epilogue, void* out, int ldo, float* slots, int* segmap,
+                        GemmSlots* result, uint32_t* status, cudaStream_t stream) {
   if (n <= 0 || n > x.rows_cap || w.k_pad != x.k_pad) return cudaErrorInvalidValue;
-  if (pl.stream_k && (!slots || !tile_counters || pl.tiles > kGemmMaxStreamKTiles))
-    return cudaErrorInvalidValue;
-  if ((epilogue == kEpiSwiGLU) != (w.pair == 2)) return cudaErrorInvalidValue;
+  if (pl.stream_k && (!slots || !segmap || !result)) return cudaErrorInvalidValue;
+  if (!pl.stream_k && (epilogue == kEpiSwiGLU) != (w.pair == 2)) return cudaErrorInvalidValue;
   GemmParams p{};
   p.m = w.m;
   p.n = n;
@@ -528,8 +444,18 @@ cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const Ge
   p.out = out;
   p.ldo = ldo;
   p.slots = slots;
-  p.counters = tile_counters;
+  p.segmap = segmap;
+  p.segcount = segmap ? segmap + kGemmMaxStreamKTiles * kGemmMaxSegsPerTile : nullptr;
   p.status = status;
+  if (pl.stream_k) {
+    result->slots = slots;
+    result->segmap = p.segmap;
+    result->segcount = p.segcount;
+    result->bn = pl.bn;
+    result->n_tiles = pl.n_tiles;
+    result->pair = w.pair;
+    result->m = w.m;
+  }
   const int g = pl.grid;
   const int bi = pl.bn_index;
   if (w.pair == 1) {
@@ -547,6 +473,14 @@ cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const Ge
     case 64: return launch<64, 2>(w, x, bi, p, g, stream);
     default: return launch<128, 2>(w, x, bi, p, g, stream);
   }
+}
+
+cudaError_t gemm_finish_launch(const GemmSlots& s, int rows, int epilogue, void* out, int ldo,
+                               cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  const dim3 grid(static_cast<unsigned>((s.m + 255) / 256), static_cast<unsigned>(rows));
+  return launch_dependent(gemm_finish_kernel, grid, dim3(256), 0, stream, s, rows, epilogue, out,
+                          ldo);
 }
 
 }  // namespace hb

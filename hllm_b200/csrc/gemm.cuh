@@ -12,12 +12,10 @@
 //               applies the epilogue itself;
 //   stream-K -- (fewer tiles) the tiles' K blocks are dealt out evenly to one
 //               CTA per SM; each CTA writes the F32 sums of its (at most three)
-//               tile segments to its own slots and counts itself in at each
-//               tile's counter.  Once a tile's CTAs have all counted in (they
-//               are all resident: one CTA per SM), each adds its share of the
-//               tile's columns over the tile's slots in CTA order -- a fixed
-//               order, so results do not depend on timing -- and applies the
-//               epilogue.  Waits are bounded.
+//               tile segments to its own slots, and the kernel that consumes
+//               the result adds the slots of each element in CTA order
+//               (gemm_slot_sum) -- a fixed order, so results do not depend on
+//               timing.  No CTA waits on another.
 #pragma once
 
 #include <cuda.h>
@@ -68,13 +66,20 @@ struct GemmPlan {
   bool stream_k = false;
 };
 
-// Stream-K bounds: segments per tile (the plan keeps each tile's CTAs below
-// this) and tiles per plan (more tiles than this always run direct).
+// Where a stream-K GEMM left its result: the consumer sums, for element
+// (n, m) of accumulator `acc`, the slots of the CTAs that covered its tile.
+// The GEMM records them per tile: segcount[tile] slots, segmap[tile][k] in
+// CTA order.
 constexpr int kGemmMaxSegsPerTile = 16;
 constexpr int kGemmMaxStreamKTiles = 512;
-// Ints of per-tile counters (arrivals, departures) a stream-K launch needs
-// (zero before the first launch; every launch leaves them zero).
-constexpr size_t kGemmCounterInts = 2 * kGemmMaxStreamKTiles;
+struct GemmSlots {
+  const float* slots;   // [grid * 3][pair][bn][128]
+  const int* segmap;    // [kGemmMaxStreamKTiles][kGemmMaxSegsPerTile]
+  const int* segcount;  // [kGemmMaxStreamKTiles]
+  int bn, n_tiles, pair, m;
+};
+// Ints of segment-map storage that follows the slots.
+constexpr size_t kGemmMapInts = kGemmMaxStreamKTiles * (kGemmMaxSegsPerTile + 1);
 
 GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override = 0,
                    int grid_override = 0);
@@ -86,15 +91,69 @@ bool gemm_make_weight(GemmWeight* w, const void* base, int rows_total, int m, in
                       int second_row);
 bool gemm_make_input(GemmInput* x, const void* base, int rows_cap, int k_pad, int row_stride);
 
-// Runs the plan: out = epilogue(X W^T).  Stream-K plans also use `slots`
-// (gemm_slot_floats of the plan) and `tile_counters` (kGemmCounterInts,
-// zero-initialised).
+// Runs the plan.  Direct plans apply `epilogue` into out/ldo; stream-K plans
+// write `slots` and fill *result for the consumer.
 cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const GemmPlan& plan,
-                        int epilogue, void* out, int ldo, float* slots, int* tile_counters,
-                        uint32_t* status, cudaStream_t stream);
+                        int epilogue, void* out, int ldo, float* slots, int* segmap,
+                        GemmSlots* result, uint32_t* status, cudaStream_t stream);
 
+// Generic consumer: out = epilogue(sum of slots) for every (n < rows, m).
+cudaError_t gemm_finish_launch(const GemmSlots& s, int rows, int epilogue, void* out, int ldo,
+                               cudaStream_t stream);
+
+// ---------------------------------------------------------------- device side
 __host__ __device__ inline long long gemm_unit_begin(long long units, int grid, int c) {
   return units * c / grid;
 }
+
+#ifdef __CUDACC__
+// Sum of the slots holding element (n, m) of accumulator `acc`, in CTA order.
+__device__ inline float gemm_slot_sum(const GemmSlots& s, int n, int m, int acc) {
+  const int tile = (m >> 7) * s.n_tiles + n / s.bn;
+  const int count = __ldcg(s.segcount + tile);
+  const int* map = s.segmap + tile * kGemmMaxSegsPerTile;
+  const size_t within = static_cast<size_t>(acc) * s.bn * 128 +
+                        static_cast<size_t>(n % s.bn) * 128 + (m & 127);
+  const size_t slot_floats = static_cast<size_t>(s.pair) * s.bn * 128;
+  float sum = 0.f;
+  for (int k = 0; k < count; ++k)
+    sum += __ldcg(s.slots + static_cast<size_t>(__ldcg(map + k)) * slot_floats + within);
+  return sum;
+}
+
+// The same sum for four consecutive features m..m+3 (m % 4 == 0, one tile):
+// the tile's segment list is read once and the slot loads are issued together
+// before they are added (in CTA order, as gemm_slot_sum does).
+__device__ inline float4 gemm_slot_sum4(const GemmSlots& s, int n, int m, int acc) {
+  const int tile = (m >> 7) * s.n_tiles + n / s.bn;
+  const int count = __ldcg(s.segcount + tile);
+  const int4* map4 = reinterpret_cast<const int4*>(s.segmap + tile * kGemmMaxSegsPerTile);
+  const size_t within = static_cast<size_t>(acc) * s.bn * 128 +
+                        static_cast<size_t>(n % s.bn) * 128 + (m & 127);
+  const size_t slot_floats = static_cast<size_t>(s.pair) * s.bn * 128;
+  float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k0 = 0; k0 < count; k0 += 4) {
+    const int4 ids = __ldcg(map4 + (k0 >> 2));
+    const int id[4] = {ids.x, ids.y, ids.z, ids.w};
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      v[j] = k0 + j < count
+                 ? __ldcg(reinterpret_cast<const float4*>(
+                       s.slots + static_cast<size_t>(id[j]) * slot_floats + within))
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (k0 + j < count) {
+        sum.x += v[j].x;
+        sum.y += v[j].y;
+        sum.z += v[j].z;
+        sum.w += v[j].w;
+      }
+    }
+  }
+  return sum;
+}
+#endif
 
 }  // namespace hb

@@ -1,7 +1,7 @@
 // gemm_noalloc.cu -- a projection GEMM entry point that allocates nothing.
 //
 // hllm_b200_gemm keeps its stream-K scratch (F32 partial tiles and the
-// per-tile completion counters) in device memory that the library allocates on
+// per-tile segment lists) in device memory that the library allocates on
 // first use.  Some callers cannot let a library allocate device memory: a
 // serving process that fixes its device-memory budget when it starts and
 // admits every request against it (hLLM's worker reserves each request's
@@ -17,12 +17,11 @@
 // code is only a host-side stand-in).  That first call should come before any
 // stream capture on the device.
 //
-// Sharing: every call on a device uses the same arrays, which keep the last
-// call's contents.  Each call rewrites all of the partial sums it reads; the
-// per-tile completion counters and the status word must start at zero, so
-// each call clears them on its stream before the GEMM (a kernel that ended
-// early could have left a counter behind).  Calls whose GPU work overlaps (for
-// example on two streams) race on the arrays and must not be issued.
+// Sharing: every call on a device uses the same array, which keeps the last
+// call's contents.  Each call rewrites all of the scratch it reads, so nothing
+// has to start at zero, except the status word, which is cleared per call.
+// Calls whose GPU work overlaps (for example on two streams) race on the array
+// and must not be issued.
 #include <cuda_runtime.h>
 
 #include <map>
@@ -46,12 +45,12 @@ namespace {
 constexpr size_t kNoAllocSlotFloats = size_t{8} << 20;
 
 __device__ __align__(256) float g_noalloc_slots[kNoAllocSlotFloats];
-__device__ __align__(256) int g_noalloc_counters[hb::kGemmCounterInts];
+__device__ __align__(256) int g_noalloc_segmap[hb::kGemmMapInts];
 __device__ __align__(256) uint32_t g_noalloc_status[64];
 
 struct DevicePointers {
   float* slots = nullptr;
-  int* counters = nullptr;
+  int* segmap = nullptr;
   uint32_t* status = nullptr;
   int sm_count = 0;
 };
@@ -74,7 +73,7 @@ hllm_b200_status pointers_for_current_device(DevicePointers* out) {
   if (it == g_pointers.end()) {
     DevicePointers p;
     e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p.slots), g_noalloc_slots);
-    if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p.counters), g_noalloc_counters);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p.segmap), g_noalloc_segmap);
     if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p.status), g_noalloc_status);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&p.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess)
@@ -118,11 +117,13 @@ extern "C" hllm_b200_status hllm_b200_gemm_noalloc(const void* w, uint64_t m, ui
                     " (use fewer CTAs, fewer tokens per call, or hllm_b200_gemm)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemsetAsync(dp.status, 0, sizeof(uint32_t), s);
-  if (e == cudaSuccess && plan.stream_k)
-    e = cudaMemsetAsync(dp.counters, 0, hb::kGemmCounterInts * sizeof(int), s);
+  hb::GemmSlots slots{};
   if (e == cudaSuccess)
     e = hb::gemm_launch(gw, gx, static_cast<int>(n), plan, static_cast<int>(epilogue), y,
-                        static_cast<int>(ldy), dp.slots, dp.counters, dp.status, s);
+                        static_cast<int>(ldy), dp.slots, dp.segmap, &slots, dp.status, s);
+  if (e == cudaSuccess && plan.stream_k)
+    e = hb::gemm_finish_launch(slots, static_cast<int>(n), static_cast<int>(epilogue), y,
+                               static_cast<int>(ldy), s);
   if (e != cudaSuccess)
     return fail(e == cudaErrorInvalidValue ? HLLM_B200_INVALID_REQUEST : HLLM_B200_INTERNAL,
                 cudaGetErrorString(e));

@@ -1,6 +1,5 @@
 // kernels.cu -- packer, embedding, norms, q/k-norm + RoPE + paged-KV write,
 // boundary conversion and synthetic initialisation for the stage executor.
-#include <algorithm>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -161,7 +160,8 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
     const bool is_q = h < a.hq, is_k = !is_q && h < a.hq + a.hkv;
     float ss = 0.f;
     for (int i = lane * 4; i < d; i += 128) {  // d % 4 == 0 (checked at stage creation)
-      const float4 v = *reinterpret_cast<const float4*>(row + h * d + i);
+      const float4 v = a.from_slots ? gemm_slot_sum4(a.slots, t, h * d + i, 0)
+                                    : *reinterpret_cast<const float4*>(row + h * d + i);
       *reinterpret_cast<float4*>(x + i) = v;
       ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
@@ -209,41 +209,77 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
   }
 }
 
-// ---------------------------------------------------------------- residual norm
-// One CTA per token: RMSNorm of the F32 residual row (which the projection's
-// epilogue has just updated) into the next GEMM's F16 input.  The row is read
-// once into registers (up to 8 values a thread).
-constexpr int kNormMaxPerThread = 8;
-__global__ void residual_norm_kernel(const float* __restrict__ hidden, int width,
-                                     const float* __restrict__ w, float eps,
+// ---------------------------------------------------------------- residual + norm
+// One CTA per token: add the projection's slots into the F32 residual stream,
+// then RMSNorm the updated row into the next GEMM's F16 input.
+__global__ void residual_norm_kernel(float* __restrict__ hidden, int width, GemmSlots slots,
+                                     int has_slots, const float* __restrict__ w, float eps,
                                      __half* __restrict__ out, int ld_out) {
   griddep_enter();
   const int t = blockIdx.x;
-  const float* xr = hidden + static_cast<size_t>(t) * width;
-  float v[kNormMaxPerThread];
+  float* xr = hidden + static_cast<size_t>(t) * width;
   float ss = 0.f;
-#pragma unroll
-  for (int k = 0; k < kNormMaxPerThread; ++k) {
-    const int c = threadIdx.x + k * blockDim.x;
-    v[k] = c < width ? xr[c] : 0.f;
-    ss += v[k] * v[k];
+  if ((width & 3) == 0) {
+    // A warp covers 128 consecutive features = one GEMM tile row.
+    for (int c = threadIdx.x * 4; c < width; c += blockDim.x * 4) {
+      float4 v = *reinterpret_cast<const float4*>(xr + c);
+      if (has_slots) {
+        const float4 a = gemm_slot_sum4(slots, t, c, 0);
+        v.x += a.x;
+        v.y += a.y;
+        v.z += a.z;
+        v.w += a.w;
+        *reinterpret_cast<float4*>(xr + c) = v;
+      }
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+  } else {
+    for (int c = threadIdx.x; c < width; c += blockDim.x) {
+      float v = xr[c];
+      if (has_slots) {
+        v += gemm_slot_sum(slots, t, c, 0);
+        xr[c] = v;
+      }
+      ss += v * v;
+    }
   }
+  if (!w) return;
   __shared__ float red[32];
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float r = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    r = warp_sum(r);
-    if (threadIdx.x == 0) red[0] = r;
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
   }
   __syncthreads();
   const float inv = 1.0f / sqrtf(red[0] / static_cast<float>(width) + eps);
   __half* o = out + static_cast<size_t>(t) * ld_out;
-#pragma unroll
-  for (int k = 0; k < kNormMaxPerThread; ++k) {
-    const int c = threadIdx.x + k * blockDim.x;
-    if (c < width) o[c] = __float2half_rn(v[k] * inv * w[c]);
+  for (int c = threadIdx.x; c < width; c += blockDim.x) o[c] = __float2half_rn(xr[c] * inv * w[c]);
+}
+
+// cpp/src/cpu/llama.cpp:274-280: (g / (1 + exp(-g))) * u.
+__global__ void swiglu_kernel(GemmSlots slots, __half* __restrict__ act, int ld_act) {
+  griddep_enter();
+  const int t = blockIdx.y;
+  __half* out = act + static_cast<size_t>(t) * ld_act;
+  if ((slots.m & 3) == 0) {
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) * 4; i < slots.m;
+         i += gridDim.x * blockDim.x * 4) {
+      const float4 g = gemm_slot_sum4(slots, t, i, 0);
+      const float4 u = gemm_slot_sum4(slots, t, i, 1);
+      out[i] = __float2half_rn((g.x / (1.0f + expf(-g.x))) * u.x);
+      out[i + 1] = __float2half_rn((g.y / (1.0f + expf(-g.y))) * u.y);
+      out[i + 2] = __float2half_rn((g.z / (1.0f + expf(-g.z))) * u.z);
+      out[i + 3] = __float2half_rn((g.w / (1.0f + expf(-g.w))) * u.w);
+    }
+    return;
+  }
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < slots.m; i += gridDim.x * blockDim.x) {
+    const float g = gemm_slot_sum(slots, t, i, 0);
+    const float u = gemm_slot_sum(slots, t, i, 1);
+    out[i] = __float2half_rn((g / (1.0f + expf(-g))) * u);
   }
 }
 
@@ -346,14 +382,24 @@ cudaError_t qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream) {
   return launch_dependent(qkv_post_kernel, grid, dim3(kQkvWarps * 32), 0, stream, a);
 }
 
-cudaError_t residual_norm_launch(const float* hidden, int tokens, int width, const float* norm,
-                                 float eps, __half* out, int ld_out, cudaStream_t stream) {
+cudaError_t residual_norm_launch(float* hidden, int tokens, int width, const GemmSlots* slots,
+                                 const float* norm, float eps, __half* out, int ld_out,
+                                 cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
-  const int threads = std::min(1024, std::max(64, (width + kNormMaxPerThread - 1) /
-                                                      kNormMaxPerThread + 31) / 32 * 32);
-  if (threads * kNormMaxPerThread < width) return cudaErrorInvalidValue;
+  GemmSlots s{};
+  if (slots) s = *slots;
+  const int threads = width >= 1024 ? 512 : (width >= 256 ? 256 : 64);
   return launch_dependent(residual_norm_kernel, dim3(tokens), dim3(threads), 0, stream, hidden,
-                          width, norm, eps, out, ld_out);
+                          width, s, slots ? 1 : 0, norm, eps, out, ld_out);
+}
+
+cudaError_t swiglu_launch(const GemmSlots& slots, int tokens, __half* act, int ld_act,
+                          cudaStream_t stream) {
+  if (tokens <= 0) return cudaSuccess;
+  const int per_block = (slots.m & 3) == 0 ? 1024 : 256;
+  const dim3 grid(static_cast<unsigned>((slots.m + per_block - 1) / per_block),
+                  static_cast<unsigned>(tokens));
+  return launch_dependent(swiglu_kernel, grid, dim3(256), 0, stream, slots, act, ld_act);
 }
 
 cudaError_t last_token_launch(const int32_t* cu_seqlens, const int32_t* sample_rows, int count,

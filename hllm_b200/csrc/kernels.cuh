@@ -63,7 +63,9 @@ cudaError_t rmsnorm_launch(const float* x, int rows, int width, const float* w, 
 // (optional), RoPE (half rotation) at the token's position, q to `q_out`
 // [T][Hq*d] F16, k/v scattered to the paged cache at slot_mapping[t].
 struct QkvPostArgs {
-  const float* qkv;       // [T][ (Hq + 2 Hkv) d ] from the projection
+  const float* qkv;       // [T][ (Hq + 2 Hkv) d ] when the projection ran direct
+  GemmSlots slots;        // its stream-K slots otherwise
+  int from_slots;
   int tokens, hq, hkv, dim;
   const int32_t* positions;
   const int32_t* slot_mapping;
@@ -79,11 +81,17 @@ struct QkvPostArgs {
 };
 cudaError_t qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream);
 
-// RMSNorm of the residual rows after a projection added itself into them
-// (cpp/src/cpu/llama.cpp:268-272 and the next rms_norm):
-// out[t] = F16(hidden[t] * inv_rms(hidden[t]) * norm), width <= 8192.
-cudaError_t residual_norm_launch(const float* hidden, int tokens, int width, const float* norm,
-                                 float eps, __half* out, int ld_out, cudaStream_t stream);
+// Fused residual add + RMSNorm (cpp/src/cpu/llama.cpp:268-272 and the next
+// rms_norm): hidden[t] += the projection's stream-K slots (when `slots` is
+// given; a direct projection already added itself), then, when `norm` is
+// given, out[t] = F16(hidden[t] * inv_rms(hidden[t]) * norm).
+cudaError_t residual_norm_launch(float* hidden, int tokens, int width, const GemmSlots* slots,
+                                 const float* norm, float eps, __half* out, int ld_out,
+                                 cudaStream_t stream);
+
+// act[t][i] = F16(silu(g) * u) from a gate/up projection's stream-K slots.
+cudaError_t swiglu_launch(const GemmSlots& slots, int tokens, __half* act, int ld_act,
+                          cudaStream_t stream);
 
 // Row indices of the last token of each sampling row: idx[i] = cu_seqlens[rows[i]+1]-1.
 cudaError_t last_token_launch(const int32_t* cu_seqlens, const int32_t* sample_rows, int count,

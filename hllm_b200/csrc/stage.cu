@@ -183,8 +183,8 @@ struct hllm_b200_stage {
   // selects the mma.sync kernel instead (for comparisons).
   bool tc_prefill = false;
   std::vector<hb::TcMaps> tc_maps;
-  float* slots = nullptr;        // stream-K GEMM partial tiles
-  int* tile_counters = nullptr;  // their per-tile completion counters (kept at zero)
+  float* slots = nullptr;  // stream-K GEMM slots, consumed by the next kernel
+  int* segmap = nullptr;   // their per-tile segment lists
 
   // pinned host staging
   // Descriptor uploads go through a ring of pinned buffers so that enqueue-only
@@ -585,21 +585,29 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
     s->pre_counters = s->alloc<int>(s->pre_counter_ints);
   }
   s->slots = s->alloc<float>(hb::gemm_max_slot_floats(s->sm_count));
-  s->tile_counters = s->alloc<int>(hb::kGemmCounterInts);
+  s->segmap = s->alloc<int>(hb::kGemmMapInts);
   {
+    // TMA maps per layer: K and V for the balanced decode pass (head sizes
+    // 64/128/256) and, with the query buffer, for the tcgen05 prefill.
     const char* env = std::getenv("HLLM_B200_TC_PREFILL");
     s->tc_prefill = hb::attn_prefill_tc_supported(static_cast<int>(s->dim),
                                                   static_cast<int>(s->hq / s->hkv)) &&
                     !(env && env[0] == '0');
-    if (s->tc_prefill) {
+    if (s->tc_prefill || hb::attn_decode_balanced(static_cast<int>(s->dim))) {
       s->tc_maps.resize(std::max<size_t>(1, s->n_layers));
       for (size_t li = 0; li < s->n_layers; ++li) {
         const __half* kc = s->kv + li * s->kv_layer_elems;
-        if (!hb::attn_tc_make_maps(&s->tc_maps[li], s->q, static_cast<long long>(T),
-                                   static_cast<int>(s->hq), static_cast<int>(s->hkv),
-                                   static_cast<int>(s->dim), kc, kc + s->kv_layer_elems / 2,
-                                   static_cast<long long>(s->num_blocks)))
-          fail(HLLM_B200_INTERNAL, "tensor map creation failed");
+        const __half* vc = kc + s->kv_layer_elems / 2;
+        const bool ok =
+            s->tc_prefill
+                ? hb::attn_tc_make_maps(&s->tc_maps[li], s->q, static_cast<long long>(T),
+                                        static_cast<int>(s->hq), static_cast<int>(s->hkv),
+                                        static_cast<int>(s->dim), kc, vc,
+                                        static_cast<long long>(s->num_blocks))
+                : hb::attn_make_kv_maps(&s->tc_maps[li], static_cast<int>(s->hkv),
+                                        static_cast<int>(s->dim), kc, vc,
+                                        static_cast<long long>(s->num_blocks));
+        if (!ok) fail(HLLM_B200_INTERNAL, "tensor map creation failed");
       }
     }
   }
@@ -940,12 +948,14 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
       PLAUNCH(kProfNorm, 0, 0, hb::rmsnorm_launch(s->hidden, T, h, L.in_norm, eps, s->xn,
                                                    static_cast<int>(s->h_pad), nullptr, s->stream));
     const hb::GemmPlan pq = hb::gemm_plan(L.g_qkv, T, s->sm_count);
+    hb::GemmSlots qslots{};
     PLAUNCH(gk, gemm_bytes(s->qkvw, T, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->qkvw, T, s->h, 1),
             hb::gemm_launch(L.g_qkv, s->in_xn, T, pq, hb::kEpiStoreF32, s->qkv,
-                            static_cast<int>(s->qkvw), s->slots, s->tile_counters, s->status,
-                            s->stream));
+                            static_cast<int>(s->qkvw), s->slots, s->segmap, &qslots, s->status, s->stream));
     hb::QkvPostArgs qa{};
     qa.qkv = s->qkv;
+    qa.slots = qslots;
+    qa.from_slots = pq.stream_k ? 1 : 0;
     qa.tokens = T;
     qa.hq = static_cast<int>(s->hq);
     qa.hkv = static_cast<int>(s->hkv);
@@ -992,37 +1002,46 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     aa.ld_out = static_cast<int>(s->qw_pad);
     aa.status = s->status;
     if (p.total_splits) {
-      PLAUNCH(kProfAttnDecode, p.attn_dec_bytes, p.attn_dec_flops, hb::attn_decode_launch(aa, p.total_splits, s->stream));
+      PLAUNCH(kProfAttnDecode, p.attn_dec_bytes, p.attn_dec_flops,
+              hb::attn_decode_launch(aa, s->tc_maps.empty() ? hb::TcMaps{} : s->tc_maps[li],
+                                     p.total_splits, s->stream));
       s->launches += hb::attn_decode_launches(static_cast<int>(s->dim)) - 1;  // combine pass
     }
     if (p.total_qtiles)
       PLAUNCH(kProfAttnPrefill, p.attn_pre_bytes, p.attn_pre_flops,
               s->tc_prefill ? hb::attn_prefill_tc_launch(s->tc_maps[li], aa, p.total_qtiles, s->stream)
                             : hb::attn_prefill_launch(aa, p.total_qtiles, s->stream));
-    // o_proj adds itself into the residual stream, then the post-attention RMSNorm.
+    // o_proj, then the fused residual add + post-attention RMSNorm.
     const hb::GemmPlan po = hb::gemm_plan(L.g_o, T, s->sm_count);
+    hb::GemmSlots oslots{};
     PLAUNCH(gk, gemm_bytes(s->h, T, s->qw, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->qw, 1),
-            hb::gemm_launch(L.g_o, s->in_attn, T, po, hb::kEpiResidual, s->hidden, h, s->slots,
-                            s->tile_counters, s->status, s->stream));
+            hb::gemm_launch(L.g_o, s->in_attn, T, po, hb::kEpiResidual, s->hidden, h, s->slots, s->segmap,
+                            &oslots, s->status, s->stream));
     PLAUNCH(kProfNorm, 0, 0,
-            hb::residual_norm_launch(s->hidden, T, h, L.post_norm, eps, s->xn,
-                                     static_cast<int>(s->h_pad), s->stream));
-    // gate/up with SwiGLU in the GEMM's epilogue.
+            hb::residual_norm_launch(s->hidden, T, h, po.stream_k ? &oslots : nullptr,
+                                     L.post_norm, eps, s->xn, static_cast<int>(s->h_pad),
+                                     s->stream));
+    // gate/up with SwiGLU: in the GEMM epilogue, or from the stream-K slots.
     const hb::GemmPlan pg = hb::gemm_plan(L.g_gu, T, s->sm_count);
+    hb::GemmSlots gslots{};
     PLAUNCH(gk, gemm_bytes(s->I, T, s->h, 2, hb::kEpiSwiGLU), gemm_flops(s->I, T, s->h, 2),
             hb::gemm_launch(L.g_gu, s->in_xn, T, pg, hb::kEpiSwiGLU, s->act,
-                            static_cast<int>(s->I_pad), s->slots, s->tile_counters, s->status,
-                            s->stream));
-    // down_proj adds itself into the residual stream, then the next layer's input norm.
+                            static_cast<int>(s->I_pad), s->slots, s->segmap, &gslots, s->status, s->stream));
+    if (pg.stream_k)
+      PLAUNCH(kProfSwiglu, 0, 0,
+              hb::swiglu_launch(gslots, T, s->act, static_cast<int>(s->I_pad), s->stream));
+    // down_proj, then the residual add fused with the next layer's input norm.
     const hb::GemmPlan pd = hb::gemm_plan(L.g_down, T, s->sm_count);
+    hb::GemmSlots dslots{};
     PLAUNCH(gk, gemm_bytes(s->h, T, s->I, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->I, 1),
-            hb::gemm_launch(L.g_down, s->in_act, T, pd, hb::kEpiResidual, s->hidden, h, s->slots,
-                            s->tile_counters, s->status, s->stream));
+            hb::gemm_launch(L.g_down, s->in_act, T, pd, hb::kEpiResidual, s->hidden, h, s->slots, s->segmap,
+                            &dslots, s->status, s->stream));
     const float* next_norm = li + 1 < s->n_layers ? s->layers[li + 1].in_norm : nullptr;
-    if (next_norm)
+    if (pd.stream_k || next_norm)
       PLAUNCH(kProfNorm, 0, 0,
-              hb::residual_norm_launch(s->hidden, T, h, next_norm, eps, s->xn,
-                                       static_cast<int>(s->h_pad), s->stream));
+              hb::residual_norm_launch(s->hidden, T, h, pd.stream_k ? &dslots : nullptr,
+                                       next_norm, eps, s->xn, static_cast<int>(s->h_pad),
+                                       s->stream));
     s->mark("layer", static_cast<int64_t>(s->desc.layer_start + li));
   }
 
@@ -1035,11 +1054,15 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
                                 static_cast<int>(s->h_pad), s->last_idx, s->stream));
       s->mark("final_norm");
       const hb::GemmPlan ph = hb::gemm_plan(s->g_head, S, s->sm_count);
+      hb::GemmSlots hslots{};
       PLAUNCH(S <= 128 ? kProfGemmDecode : kProfGemmPrefill,
               gemm_bytes(s->V, S, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->V, S, s->h, 1),
               hb::gemm_launch(s->g_head, s->in_xs, S, ph, hb::kEpiStoreF32, s->logits,
-                              static_cast<int>(s->V), s->slots, s->tile_counters, s->status,
-                              s->stream));
+                              static_cast<int>(s->V), s->slots, s->segmap, &hslots, s->status, s->stream));
+      if (ph.stream_k)
+        PLAUNCH(kProfSwiglu, 0, 0,
+                hb::gemm_finish_launch(hslots, S, hb::kEpiStoreF32, s->logits,
+                                       static_cast<int>(s->V), s->stream));
       s->mark("lm_head");
       PLAUNCH(kProfSample, 0, 0, hb::sample_launch(s->logits, S, static_cast<int>(s->V), static_cast<int>(s->V),
                                s->d_params, s->sample_scratch, s->results, s->status, s->stream));
@@ -1053,12 +1076,10 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
   s->last_tokens = p.tokens;
 }
 
-// Kernels return their arrival counters (GEMM tiles, attention streams and
-// prefill tiles) to zero when they finish; a kernel that ended early on a
-// failed wait may leave one behind, so a failed step clears them all.
+// Attention kernels return their arrival counters (decode streams, prefill
+// tiles) to zero when they finish; a kernel that ended early on a failed wait
+// may leave one behind, so a failed step clears them.
 void reset_counters(hllm_b200_stage* s) {
-  check_cuda(cudaMemsetAsync(s->tile_counters, 0, hb::kGemmCounterInts * sizeof(int), s->stream),
-             "counter reset");
   check_cuda(cudaMemsetAsync(s->attn_counters, 0, s->attn_counter_ints * sizeof(int), s->stream),
              "counter reset");
   check_cuda(cudaMemsetAsync(s->pre_counters, 0, s->pre_counter_ints * sizeof(int), s->stream),

@@ -78,9 +78,13 @@ class MixedPlanner:
     next_req: int = 0
     step_index: int = 0
 
-    def admit(self, on_admit=None):
+    def admit(self, on_admit=None, until=None):
+        """Admits requests in trace order while slots are free; with `until`,
+        only requests that have arrived by then (open-loop arrivals)."""
         while len(self.active) < self.max_active and self.next_req < len(self.trace):
             r = self.trace[self.next_req]
+            if until is not None and r.arrival > until:
+                break
             self.next_req += 1
             r.admitted_step = self.step_index
             self.active.append(r)

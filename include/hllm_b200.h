@@ -349,13 +349,11 @@ hllm_b200_status hllm_b200_stage_read_logits(hllm_b200_stage* stage, float* out,
  * cpp/src/cpu/tensor.cpp:47-62).  W: F16 [m][k_pad] (pair == 2: [2*second_row..]
  * gate rows then up rows), X: F16 [n][k_pad] with zero padding columns,
  * k_pad % 64 == 0.  epilogue: 0 store F32, 1 store F16, 2 add into F32 Y,
- * 3 SwiGLU of the pair into F16 Y.  bn (16..256) and grid override the
- * plan's token-tile width and CTA count (0 = the plan's own); a split-K plan
- * uses at most one CTA per SM, since a tile's CTAs wait for one another.  Uses
- * a scratch area owned by the library (allocated on first use per device)
- * sized for one CTA per SM.  A device wait inside the kernel that runs out
- * (2 s) ends the kernel early; this asynchronous entry point does not report
- * it (hllm_b200_step does). */
+ * 3 SwiGLU of the pair into F16 Y.  Uses a scratch area owned by the library
+ * (allocated on first use per device) that holds one CTA per SM: a split with
+ * a larger grid is refused with HLLM_B200_RESOURCE_EXHAUSTED.  A device wait
+ * inside the kernel that runs out (2 s) ends the kernel early; this
+ * asynchronous entry point does not report it (hllm_b200_step does). */
 hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint32_t pair,
                                 uint64_t second_row, const void* x, uint64_t n, uint32_t epilogue,
                                 void* y, uint64_t ldy, uint32_t bn, uint32_t grid, void* stream);
@@ -365,9 +363,8 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
  * a serving process that fixes its device budget at start-up and admits
  * requests against it, or a host that owns all of a plugin's device memory.
  * Its split-K scratch is a static device array of 32 MiB of partial sums, plus
- * 4 KiB of per-tile counters (1024 ints) and a 256-byte status word,
- * that every GPU loading the library holds until the process exits.  Each call
- * clears the counters and the status word on its stream before the GEMM.
+ * 34 KiB of per-tile segment lists (512 x 17 ints) and a 256-byte status word,
+ * that every GPU loading the library holds until the process exits.
  * Splits that need more partial-sum storage than that are rejected with
  * HLLM_B200_RESOURCE_EXHAUSTED and a message; plans that need none always run.
  * The first call on a device, with that device current, resolves the array's
@@ -402,7 +399,8 @@ hllm_b200_status hllm_b200_pack(const int32_t* row_slot, const int32_t* row_firs
  * cpp/src/cpu/llama.cpp:67-112).  q F16 [q_tokens][Hq*d]; caches F16
  * [kv_blocks][Hkv][16][d]; packer outputs as above; out F16 [tokens][ld_out].
  * Decode rows (one token): for head sizes 64/128/256 the decode rows' KV
- * pages are split evenly over one wave of warps and the pieces of each
+ * pages are split evenly over one wave of warps, each streaming its pages by
+ * TMA (kv_blocks bounds the maps and is required), and the pieces of each
  * (row, kv head) are merged by its last warp (cu_splits and split_tokens only
  * bound the work); other head sizes use split-K over `split_tokens`-key
  * splits.  Prefill rows: causal tiles of hllm_b200_attention_qtile_tokens(

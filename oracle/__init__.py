@@ -143,6 +143,7 @@ def ref():
         r.ref_cache_length.restype = C.c_uint64
         r.ref_cache_length.argtypes = [C.c_void_p]
         r.ref_cache_read.argtypes = [C.c_void_p, _F, _F]
+        r.ref_cache_append.argtypes = [C.c_void_p, C.c_uint64, _F, _F]
         r.ref_transformer_layer.argtypes = [_F, C.c_uint64, C.POINTER(Layer), C.POINTER(Config),
                                             C.c_uint64, C.c_void_p, _F]
         r.ref_final_logits.argtypes = [_F, C.c_uint64, C.c_uint64, _F, _F, C.c_uint64,
@@ -437,6 +438,27 @@ class OracleModel:
                 keep.append((k, v))
                 caches.append(KV(capacity, s.key_value_heads, s.head_dimension, 0, fp(k), fp(v)))
         return OracleSequence(caches, keep)
+
+    def fill_context(self, seq: OracleSequence, length: int, seed: int = 0):
+        """Sets every owned layer's cache of a fresh sequence to `length`
+        positions of seeded synthetic keys and values (N(0, 1) scaled by
+        1/sqrt(d)), as if that much context had been processed: the cost of
+        later steps depends on the context length, not on its values."""
+        s = self.spec
+        rng = np.random.default_rng(seed)
+        width = s.key_value_heads * s.head_dimension
+        for li in range(len(seq.caches)):
+            k = (rng.standard_normal((length, width)) / np.sqrt(s.head_dimension)).astype(np.float32)
+            v = (rng.standard_normal((length, width)) / np.sqrt(s.head_dimension)).astype(np.float32)
+            if self.use_ref:
+                if ref().ref_cache_append(seq.caches[li], length, fp(k), fp(v)) != 0:
+                    raise ValueError("reference cache rejected the context")
+            else:
+                kk, vv = seq.keep[li]
+                kk[:length] = k.reshape(length, s.key_value_heads, s.head_dimension)
+                vv[:length] = v.reshape(length, s.key_value_heads, s.head_dimension)
+                seq.caches[li].length = length
+        seq.length = length
 
     def free_sequence(self, seq: OracleSequence):
         if self.use_ref:

@@ -106,6 +106,18 @@ void* ref_cache_new(std::uint64_t capacity, std::uint64_t heads, std::uint64_t d
 }
 void ref_cache_free(void* cache) { delete static_cast<LayerKvCache*>(cache); }
 std::uint64_t ref_cache_length(void* cache) { return static_cast<LayerKvCache*>(cache)->length(); }
+// Appends `rows` positions of keys and values ([rows][heads * dim] each) at the
+// cache's end through the reference's own LayerKvCache::append; 0 on success.
+int ref_cache_append(void* cache, std::uint64_t rows, const float* keys, const float* values) {
+  try {
+    auto* c = static_cast<LayerKvCache*>(cache);
+    const std::size_t width = c->heads() * c->head_dimension();
+    c->append(c->length(), matrix(keys, rows, width), matrix(values, rows, width));
+    return 0;
+  } catch (const std::exception& e) {
+    return status_of(e);
+  }
+}
 // Reads the cache as [length][heads][dim].
 void ref_cache_read(void* cache, float* keys, float* values) {
   auto* c = static_cast<LayerKvCache*>(cache);

@@ -98,20 +98,19 @@ def test_gemm_swiglu_pair(I, k, n, grid):
     np.testing.assert_allclose(f16_vals(host(Y, np.uint16)), ref, rtol=3e-3, atol=3e-3)
 
 
-def test_gemm_split_grid_is_capped_at_one_cta_per_sm():
-    """A split-K tile's CTAs wait for one another, so they must all be
-    resident: a grid override of two CTAs per SM is reduced to one per SM (and
-    stays inside the library's scratch), and the result is still the product."""
+def test_gemm_refuses_a_grid_beyond_its_scratch():
+    """The library's stream-K scratch holds one CTA per SM: a grid override of
+    two CTAs per SM with wide tiles would write past it and is refused before
+    any launch."""
     torch = torch_cuda()
-    rng = np.random.default_rng(11)
     m, k, n = 2560, 4096, 256
-    Wb = f16_bits(rng.standard_normal((m, k)).astype(np.float32) * 0.02)
-    Xb = f16_bits(rng.standard_normal((n, k)).astype(np.float32))
-    ref = f16_vals(Xb).astype(np.float64) @ f16_vals(Wb).astype(np.float64).T
+    W = torch.zeros((m, k), dtype=torch.float16, device="cuda")
+    X = torch.zeros((n, k), dtype=torch.float16, device="cuda")
     Y = torch.zeros((n, m), dtype=torch.float32, device="cuda")
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    run_gemm(dev(Wb), dev(Xb), n, 0, Y, m, k, bn=256, grid=2 * sms)
-    np.testing.assert_allclose(host(Y), ref, rtol=1e-4, atol=1e-4)
+    st = lib().hllm_b200_gemm(ptr(W), m, k, 1, 0, ptr(X), n, 0, ptr(Y), m, 256, 2 * sms, stream())
+    assert st == _lib.RESOURCE_EXHAUSTED
+    assert "scratch holds" in _lib.last_error()
 
 
 # ----------------------------------------------------------------------------- RMSNorm
