@@ -14,12 +14,15 @@
 //               softmax has written P, O += P V into the TMEM output;
 //   warps 0-3 -- softmax, one query row (TMEM lane) per thread: row maximum,
 //               P = 2^(s * scale * log2 e - m) as F16 into shared memory in the
-//               swizzled K-major layout the MMA reads, the running sum, and the
-//               rescale of O in TMEM when a row's maximum moved; at the end
+//               swizzled K-major layout the MMA reads, the running sum, and,
+//               when a row's maximum passed its reference m by more than 2^8,
+//               a new reference and the rescale of O in TMEM; at the end
 //               O / l to the output, or, with several key splits, the split's
 //               rows and (m, l) for the last split to merge in split order.
 // The MMA for S on tile i+1 is issued before the PV of tile i, so it runs
-// while the softmax works on tile i.  The V tile is the PV MMA's B operand as
+// while the softmax works on tile i; the softmax of tile i waits for the PV of
+// tile i - 2 (its P buffer) and only on a rescale for that of tile i - 1, so
+// it overlaps the PV of tile i - 1.  The V tile is the PV MMA's B operand as
 // it lies (MN-major: 64 dims per 128-byte row, one row per key), so no
 // transpose is needed.  Scores of keys past a row's position or past the
 // context are masked to p = 0; pages past the context are filled from a valid
@@ -94,9 +97,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* kv_empty = bars + 5;  // [2]
   uint64_t* s_full = bars + 7;    // [2]
   uint64_t* s_empty = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_done = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* p_full = bars + 11;   // [2] by tile parity
+  uint64_t* o_done = bars + 13;   // [2] by tile parity: PV of that tile complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int G = a.hq / a.hkv;
@@ -126,8 +129,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&p_full[b], 128);
+      mbar_init(&o_done[b], 1);
+    }
     fence_mbar_init();
   }
   if (warp == 5) {
@@ -232,7 +237,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       };
       auto issue_pv = [&](int i) -> bool {
         const int s = i & 1;
-        if (!mbar_wait(p_full, i & 1u, a.status)) return false;
+        if (!mbar_wait(&p_full[i & 1], (i >> 1) & 1u, a.status)) return false;
         if (!mbar_wait(&v_full[s], (i >> 1) & 1u, a.status)) return false;
         tc_fence_after();
         const uint32_t p0 = smem_u32(smem + S::kP + s * S::kPBytes);
@@ -244,7 +249,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    sw128_desc_mn(v0 + ks * 2048, S::kAtom), idesc_pv,
                    (i > 0 || ks > 0) ? 1u : 0u);
         }
-        umma_commit(o_done);
+        umma_commit(&o_done[i & 1]);
         umma_commit(&kv_empty[s]);
         return true;
       };
@@ -261,6 +266,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int pos = first + tok0 + tl;
     const float sl2 = a.scale * kTcLog2e;
     const uint32_t lanes = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // m is the reference of this row's exponentials: raised only when a
+    // tile's maximum exceeds it by more than kLazy (log2 units), so most
+    // tiles need no rescale of O and P stays below 2^kLazy.
+    constexpr float kLazy = 8.f;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int i = 0; i < n; ++i) {
@@ -274,73 +283,90 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t sa = lanes + S::kTmemS + sb * kTcKeys;
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kTcKeys / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32_nowait(sa + c * 32, v);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t v0[32], v1[32];
+        tmem_ld32_nowait(sa + h * 64, v0);
+        tmem_ld32_nowait(sa + h * 64 + 32, v1);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c * 32 + j <= lim) mx = fmaxf(mx, __uint_as_float(v[j]));
+        for (int j = 0; j < 32; ++j) {
+          if (h * 64 + j <= lim) mx = fmaxf(mx, __uint_as_float(v0[j]));
+          if (h * 64 + 32 + j <= lim) mx = fmaxf(mx, __uint_as_float(v1[j]));
+        }
       }
-      const float m_new = fmaxf(m, mx * sl2);
+      const float mt = mx * sl2;
+      float alpha = 1.f;
+      if (mt > m + kLazy || (m == -INFINITY && mt > -INFINITY)) {
+        alpha = ex2f(m - mt);  // 0 while m is -inf
+        m = mt;
+      }
       // A row with no valid key yet keeps m = -inf; the reference point 0 then
       // makes every p exactly 0 (no inf - inf).
-      const float ref = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = ex2f(m - ref);
-      m = m_new;
+      const float ref = m == -INFINITY ? 0.f : m;
+      // P goes to buffer i & 1, which the PV of tile i - 2 read.
+      if (i >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_done[sb], ((i - 2) >> 1) & 1u, a.status));
+        if (!ok) break;
+      }
       uint8_t* prow = smem + S::kP + sb * S::kPBytes + row * 128;
       float rs = 0.f;
 #pragma unroll
-      for (int c = 0; c < kTcKeys / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32_nowait(sa + c * 32, v);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t v[2][32];
+        tmem_ld32_nowait(sa + h * 64, v[0]);
+        tmem_ld32_nowait(sa + h * 64 + 32, v[1]);
         tmem_ld_wait();
-        uint32_t pk[16];
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float p0 = c * 32 + j <= lim ? ex2f(fmaf(__uint_as_float(v[j]), sl2, -ref)) : 0.f;
-          const float p1 =
-              c * 32 + j + 1 <= lim ? ex2f(fmaf(__uint_as_float(v[j + 1]), sl2, -ref)) : 0.f;
-          rs += p0 + p1;
-          pk[j >> 1] = half2_bits(p0, p1);
-        }
-        // Keys c*32 .. c*32+31 are 16-byte chunks kc = 4c .. 4c+3 of the row:
-        // swizzle column kc / 8, chunk kc % 8 XOR the row (128-byte swizzle).
+        for (int hh = 0; hh < 2; ++hh) {
+          const int c = 2 * h + hh;
+          uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int kc = c * 4 + q;
-          uint8_t* dst = prow + (kc >> 3) * S::kAtom + (((kc & 7) ^ (row & 7)) << 4);
-          *reinterpret_cast<uint4*>(dst) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          for (int j = 0; j < 32; j += 2) {
+            const float p0 =
+                c * 32 + j <= lim ? ex2f(fmaf(__uint_as_float(v[hh][j]), sl2, -ref)) : 0.f;
+            const float p1 =
+                c * 32 + j + 1 <= lim ? ex2f(fmaf(__uint_as_float(v[hh][j + 1]), sl2, -ref)) : 0.f;
+            rs += p0 + p1;
+            pk[j >> 1] = half2_bits(p0, p1);
+          }
+          // Keys c*32 .. c*32+31 are 16-byte chunks kc = 4c .. 4c+3 of the row:
+          // swizzle column kc / 8, chunk kc % 8 XOR the row (128-byte swizzle).
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int kc = c * 4 + q;
+            uint8_t* dst = prow + (kc >> 3) * S::kAtom + (((kc & 7) ^ (row & 7)) << 4);
+            *reinterpret_cast<uint4*>(dst) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
         }
       }
       tc_fence_before();
       mbar_arrive(&s_empty[sb]);
       l = l * alpha + rs;
-      if (i > 0) {
-        // O holds PV of the earlier tiles once their MMAs completed; rescale
-        // it to this tile's maximum (skipped where no row of the warp moved).
-        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (i - 1) & 1u, a.status));
+      if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // O holds the PV of the earlier tiles once tile i - 1's completed;
+        // rescale it to the new reference.
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_done[(i - 1) & 1], ((i - 1) >> 1) & 1u, a.status));
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < DP / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32_nowait(lanes + S::kTmemO + c * 32, v);
-            tmem_ld_wait();
+        for (int c = 0; c < DP / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32_nowait(lanes + S::kTmemO + c * 32, v);
+          tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
-            tmem_st32(lanes + S::kTmemO + c * 32, v);
-          }
-          tmem_st_wait();
+          for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * alpha);
+          tmem_st32(lanes + S::kTmemO + c * 32, v);
         }
+        tmem_st_wait();
       }
       fence_proxy_async();  // P is read by the tensor cores (async proxy)
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[sb]);
     }
-    if (ok && n > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (n - 1) & 1u, a.status));
+    if (ok && n > 0)
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&o_done[(n - 1) & 1], ((n - 1) >> 1) & 1u, a.status));
     if (ok && n > 0) tc_fence_after();
 
     __half* out_row = tl < ntok ? a.out + static_cast<size_t>(t_base + tok0 + tl) * a.ld_out +
