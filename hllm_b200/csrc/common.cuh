@@ -176,30 +176,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
-// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, bytes % 16 == 0).
-__device__ __forceinline__ void l2_prefetch(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-// A range of device memory that a kernel asks L2 to fetch ahead of the kernel
-// that reads it next (the next projection's weights, which never change).
-struct L2Range {
-  const void* base = nullptr;
-  size_t bytes = 0;  // multiple of 16
-};
-// This CTA's share of `r` in 32 KB pieces, issued by the lanes of warp 0.
-// Launch-independent data only, so kernels call it before griddep_enter().
-__device__ __forceinline__ void l2_prefetch_share(const L2Range& r) {
-  if (!r.base || threadIdx.x >= 32) return;
-  constexpr size_t kPiece = 32 << 10;
-  const size_t pieces = (r.bytes + kPiece - 1) / kPiece;
-  const size_t ctas = static_cast<size_t>(gridDim.x) * gridDim.y * gridDim.z;
-  const size_t cta = blockIdx.x + static_cast<size_t>(gridDim.x) * (blockIdx.y + static_cast<size_t>(gridDim.y) * blockIdx.z);
-  for (size_t i = cta * 32 + threadIdx.x; i < pieces; i += ctas * 32) {
-    const size_t off = i * kPiece;
-    const size_t n = r.bytes - off < kPiece ? r.bytes - off : kPiece;
-    l2_prefetch(static_cast<const uint8_t*>(r.base) + off, static_cast<uint32_t>(n));
-  }
-}
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -143,7 +143,6 @@ constexpr int kMaxHeadDim = 256;
 
 __global__ void __launch_bounds__(kQkvWarps * 32)
     qkv_post_kernel(QkvPostArgs a) {
-  l2_prefetch_share(a.prefetch);
   griddep_enter();
   __shared__ __align__(16) float buf[kQkvWarps][kMaxHeadDim];
   const int t = blockIdx.x;
@@ -215,8 +214,7 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
 // then RMSNorm the updated row into the next GEMM's F16 input.
 __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, GemmSlots slots,
                                      int has_slots, const float* __restrict__ w, float eps,
-                                     __half* __restrict__ out, int ld_out, L2Range prefetch) {
-  l2_prefetch_share(prefetch);
+                                     __half* __restrict__ out, int ld_out) {
   griddep_enter();
   const int t = blockIdx.x;
   float* xr = hidden + static_cast<size_t>(t) * width;
@@ -262,9 +260,7 @@ __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, Gemm
 }
 
 // cpp/src/cpu/llama.cpp:274-280: (g / (1 + exp(-g))) * u.
-__global__ void swiglu_kernel(GemmSlots slots, __half* __restrict__ act, int ld_act,
-                              L2Range prefetch) {
-  l2_prefetch_share(prefetch);
+__global__ void swiglu_kernel(GemmSlots slots, __half* __restrict__ act, int ld_act) {
   griddep_enter();
   const int t = blockIdx.y;
   __half* out = act + static_cast<size_t>(t) * ld_act;
@@ -388,23 +384,22 @@ cudaError_t qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream) {
 
 cudaError_t residual_norm_launch(float* hidden, int tokens, int width, const GemmSlots* slots,
                                  const float* norm, float eps, __half* out, int ld_out,
-                                 cudaStream_t stream, L2Range prefetch) {
+                                 cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
   GemmSlots s{};
   if (slots) s = *slots;
   const int threads = width >= 1024 ? 512 : (width >= 256 ? 256 : 64);
   return launch_dependent(residual_norm_kernel, dim3(tokens), dim3(threads), 0, stream, hidden,
-                          width, s, slots ? 1 : 0, norm, eps, out, ld_out, prefetch);
+                          width, s, slots ? 1 : 0, norm, eps, out, ld_out);
 }
 
 cudaError_t swiglu_launch(const GemmSlots& slots, int tokens, __half* act, int ld_act,
-                          cudaStream_t stream, L2Range prefetch) {
+                          cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
   const int per_block = (slots.m & 3) == 0 ? 1024 : 256;
   const dim3 grid(static_cast<unsigned>((slots.m + per_block - 1) / per_block),
                   static_cast<unsigned>(tokens));
-  return launch_dependent(swiglu_kernel, grid, dim3(256), 0, stream, slots, act, ld_act,
-                          prefetch);
+  return launch_dependent(swiglu_kernel, grid, dim3(256), 0, stream, slots, act, ld_act);
 }
 
 cudaError_t last_token_launch(const int32_t* cu_seqlens, const int32_t* sample_rows, int count,

@@ -5,7 +5,6 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "common.cuh"
 #include "gemm.cuh"
 
 namespace hb {
@@ -79,7 +78,6 @@ struct QkvPostArgs {
   __half* q_out;          // [T][Hq d]
   __half* k_cache;        // [blocks][Hkv][16][d] of this layer
   __half* v_cache;
-  L2Range prefetch;       // weights of a later kernel to start fetching into L2
 };
 cudaError_t qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream);
 
@@ -89,11 +87,11 @@ cudaError_t qkv_post_launch(const QkvPostArgs& a, cudaStream_t stream);
 // given, out[t] = F16(hidden[t] * inv_rms(hidden[t]) * norm).
 cudaError_t residual_norm_launch(float* hidden, int tokens, int width, const GemmSlots* slots,
                                  const float* norm, float eps, __half* out, int ld_out,
-                                 cudaStream_t stream, L2Range prefetch = {});
+                                 cudaStream_t stream);
 
 // act[t][i] = F16(silu(g) * u) from a gate/up projection's stream-K slots.
 cudaError_t swiglu_launch(const GemmSlots& slots, int tokens, __half* act, int ld_act,
-                          cudaStream_t stream, L2Range prefetch = {});
+                          cudaStream_t stream);
 
 // Row indices of the last token of each sampling row: idx[i] = cu_seqlens[rows[i]+1]-1.
 cudaError_t last_token_launch(const int32_t* cu_seqlens, const int32_t* sample_rows, int count,

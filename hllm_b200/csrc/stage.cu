@@ -182,9 +182,6 @@ struct hllm_b200_stage {
   // the query buffer and the layer's K/V caches.  HLLM_B200_TC_PREFILL=0
   // selects the mma.sync kernel instead (for comparisons).
   bool tc_prefill = false;
-  // Latency-bound consumer kernels start fetching the next projection's
-  // weights into L2 (HLLM_B200_L2_PREFETCH=0 turns it off, for comparisons).
-  bool l2_prefetch = true;
   std::vector<hb::TcMaps> tc_maps;
   float* slots = nullptr;  // stream-K GEMM slots, consumed by the next kernel
   int* segmap = nullptr;   // their per-tile segment lists
@@ -592,8 +589,6 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
   {
     // TMA maps per layer: K and V for the balanced decode pass (head sizes
     // 64/128/256) and, with the query buffer, for the tcgen05 prefill.
-    const char* pf = std::getenv("HLLM_B200_L2_PREFETCH");
-    s->l2_prefetch = !(pf && pf[0] == '0');
     const char* env = std::getenv("HLLM_B200_TC_PREFILL");
     s->tc_prefill = hb::attn_prefill_tc_supported(static_cast<int>(s->dim),
                                                   static_cast<int>(s->hq / s->hkv)) &&
@@ -856,13 +851,6 @@ double gemm_bytes(double m, double n, double k, int pair, int epilogue) {
 }
 double gemm_flops(double m, double n, double k, int pair) { return 2.0 * pair * m * n * k; }
 
-// The L2 prefetch range of a weight matrix of `elems` F16 values (empty when
-// prefetching is off).
-hb::L2Range weights_of(const hllm_b200_stage* s, const void* base, size_t elems) {
-  if (!s->l2_prefetch || !base) return {};
-  return {base, elems * sizeof(__half)};
-}
-
 void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan& p,
                   const void* device_input) {
   const size_t R = s->R_max;
@@ -983,7 +971,6 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     qa.q_out = s->q;
     qa.k_cache = kc;
     qa.v_cache = vc;
-    qa.prefetch = weights_of(s, L.o, s->h * s->qw_pad);
     PLAUNCH(kProfQkv, 0, 0, hb::qkv_post_launch(qa, s->stream));
     hb::AttnArgs aa{};
     aa.q = s->q;
@@ -1033,7 +1020,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     PLAUNCH(kProfNorm, 0, 0,
             hb::residual_norm_launch(s->hidden, T, h, po.stream_k ? &oslots : nullptr,
                                      L.post_norm, eps, s->xn, static_cast<int>(s->h_pad),
-                                     s->stream, weights_of(s, L.gate_up, 2 * s->I * s->h_pad)));
+                                     s->stream));
     // gate/up with SwiGLU: in the GEMM epilogue, or from the stream-K slots.
     const hb::GemmPlan pg = hb::gemm_plan(L.g_gu, T, s->sm_count);
     hb::GemmSlots gslots{};
@@ -1042,8 +1029,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
                             static_cast<int>(s->I_pad), s->slots, s->segmap, &gslots, s->status, s->stream));
     if (pg.stream_k)
       PLAUNCH(kProfSwiglu, 0, 0,
-              hb::swiglu_launch(gslots, T, s->act, static_cast<int>(s->I_pad), s->stream,
-                                weights_of(s, L.down, s->h * s->I_pad)));
+              hb::swiglu_launch(gslots, T, s->act, static_cast<int>(s->I_pad), s->stream));
     // down_proj, then the residual add fused with the next layer's input norm.
     const hb::GemmPlan pd = hb::gemm_plan(L.g_down, T, s->sm_count);
     hb::GemmSlots dslots{};
@@ -1053,12 +1039,9 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     const float* next_norm = li + 1 < s->n_layers ? s->layers[li + 1].in_norm : nullptr;
     if (pd.stream_k || next_norm)
       PLAUNCH(kProfNorm, 0, 0,
-              hb::residual_norm_launch(
-                  s->hidden, T, h, pd.stream_k ? &dslots : nullptr, next_norm, eps, s->xn,
-                  static_cast<int>(s->h_pad), s->stream,
-                  li + 1 < s->n_layers
-                      ? weights_of(s, s->layers[li + 1].qkv, s->qkvw * s->h_pad)
-                      : hb::L2Range{}));  // the LM head (0.78 GB) streams at the roof already
+              hb::residual_norm_launch(s->hidden, T, h, pd.stream_k ? &dslots : nullptr,
+                                       next_norm, eps, s->xn, static_cast<int>(s->h_pad),
+                                       s->stream));
     s->mark("layer", static_cast<int64_t>(s->desc.layer_start + li));
   }
 
