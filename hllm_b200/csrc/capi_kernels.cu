@@ -39,7 +39,6 @@ hllm_b200_status cuda_status(cudaError_t e) {
 // use and kept until the process exits.
 struct DeviceScratch {
   float* slots = nullptr;
-  int* segmap = nullptr;
   uint32_t* status = nullptr;
   int sm_count = 0;
 };
@@ -56,7 +55,6 @@ hllm_b200_status scratch_for_device(DeviceScratch* out) {
     e = cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
       e = cudaMalloc(&s.slots, hb::gemm_max_slot_floats(s.sm_count) * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&s.segmap, hb::kGemmMapInts * sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&s.status, 256);
     if (e == cudaSuccess) e = cudaMemset(s.status, 0, 256);
     if (e != cudaSuccess) {
@@ -104,7 +102,7 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
   hb::GemmSlots slots{};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = hb::gemm_launch(gw, gx, static_cast<int>(n), plan, static_cast<int>(epilogue), y,
-                                  static_cast<int>(ldy), sc.slots, sc.segmap, &slots, sc.status,
+                                  static_cast<int>(ldy), sc.slots, &slots, sc.status,
                                   s);
   if (e == cudaSuccess && plan.stream_k)
     e = hb::gemm_finish_launch(slots, static_cast<int>(n), static_cast<int>(epilogue), y,
@@ -179,6 +177,7 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
   a.dim = static_cast<int>(dim);
   a.max_blocks = static_cast<int>(max_blocks);
   a.split_tokens = static_cast<int>(split_tokens);
+  a.kv_prefetch = 6;
   a.qtile_tokens = hb::attn_qtile_tokens(static_cast<int>(hq / hkv));
   a.scale = 1.0f / std::sqrt(static_cast<float>(dim));
   a.out = reinterpret_cast<__half*>(out);

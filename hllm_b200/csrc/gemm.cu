@@ -40,8 +40,6 @@ struct GemmParams {
   void* out;
   int ldo;
   float* slots;
-  int* segmap;
-  int* segcount;
   uint32_t* status;
 };
 
@@ -252,17 +250,6 @@ __global__ void __launch_bounds__(192, 1)
       if (p.stream_k) {
         const int slot_id = static_cast<int>(blockIdx.x) * kGemmSlotsPerCta + (sg.tile - first_tile);
         slot = p.slots + static_cast<size_t>(slot_id) * NA * BN * 128;
-        if (t == 0) {
-          // Record this slot in the tile's segment list (CTA order): CTA c covers
-          // unit u iff U*c/G <= u < U*(c+1)/G, i.e. c = floor(((u+1)G - 1)/U).
-          const long long u0 = static_cast<long long>(sg.tile) * p.kb_count;
-          const long long G = grid;
-          const int c_first = static_cast<int>(((u0 + 1) * G - 1) / p.units);
-          const int c_last = static_cast<int>(((u0 + p.kb_count) * G - 1) / p.units);
-          const int pos = static_cast<int>(blockIdx.x) - c_first;
-          p.segmap[sg.tile * kGemmMaxSegsPerTile + pos] = slot_id;
-          if (pos == 0) p.segcount[sg.tile] = c_last - c_first + 1;
-        }
       }
       for (int c = 0; c < BN / 16; ++c) {
         if (c * 16 >= nvalid) break;
@@ -426,10 +413,10 @@ size_t gemm_max_slot_floats(int sm_count) {
 }
 
 cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const GemmPlan& pl,
-                        int epilogue, void* out, int ldo, float* slots, int* segmap,
-                        GemmSlots* result, uint32_t* status, cudaStream_t stream) {
+                        int epilogue, void* out, int ldo, float* slots, GemmSlots* result,
+                        uint32_t* status, cudaStream_t stream) {
   if (n <= 0 || n > x.rows_cap || w.k_pad != x.k_pad) return cudaErrorInvalidValue;
-  if (pl.stream_k && (!slots || !segmap || !result)) return cudaErrorInvalidValue;
+  if (pl.stream_k && (!slots || !result)) return cudaErrorInvalidValue;
   if (!pl.stream_k && (epilogue == kEpiSwiGLU) != (w.pair == 2)) return cudaErrorInvalidValue;
   GemmParams p{};
   p.m = w.m;
@@ -444,13 +431,12 @@ cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const Ge
   p.out = out;
   p.ldo = ldo;
   p.slots = slots;
-  p.segmap = segmap;
-  p.segcount = segmap ? segmap + kGemmMaxStreamKTiles * kGemmMaxSegsPerTile : nullptr;
   p.status = status;
   if (pl.stream_k) {
     result->slots = slots;
-    result->segmap = p.segmap;
-    result->segcount = p.segcount;
+    result->units = pl.units;
+    result->grid = pl.grid;
+    result->kb_count = pl.kb_count;
     result->bn = pl.bn;
     result->n_tiles = pl.n_tiles;
     result->pair = w.pair;

@@ -67,19 +67,18 @@ struct GemmPlan {
 };
 
 // Where a stream-K GEMM left its result: the consumer sums, for element
-// (n, m) of accumulator `acc`, the slots of the CTAs that covered its tile.
-// The GEMM records them per tile: segcount[tile] slots, segmap[tile][k] in
-// CTA order.
+// (n, m) of accumulator `acc`, the slots of the CTAs that covered its tile, in
+// CTA order.  Which CTAs those are, and which of each CTA's slots holds the
+// tile, follow from the plan (units dealt U*c/G .. U*(c+1)/G to CTA c), so no
+// index is stored: the consumer issues all slot loads at once.
 constexpr int kGemmMaxSegsPerTile = 16;
 constexpr int kGemmMaxStreamKTiles = 512;
 struct GemmSlots {
   const float* slots;   // [grid * 3][pair][bn][128]
-  const int* segmap;    // [kGemmMaxStreamKTiles][kGemmMaxSegsPerTile]
-  const int* segcount;  // [kGemmMaxStreamKTiles]
+  long long units;      // tiles x K blocks
+  int grid, kb_count;
   int bn, n_tiles, pair, m;
 };
-// Ints of segment-map storage that follows the slots.
-constexpr size_t kGemmMapInts = kGemmMaxStreamKTiles * (kGemmMaxSegsPerTile + 1);
 
 GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override = 0,
                    int grid_override = 0);
@@ -94,8 +93,8 @@ bool gemm_make_input(GemmInput* x, const void* base, int rows_cap, int k_pad, in
 // Runs the plan.  Direct plans apply `epilogue` into out/ldo; stream-K plans
 // write `slots` and fill *result for the consumer.
 cudaError_t gemm_launch(const GemmWeight& w, const GemmInput& x, int n, const GemmPlan& plan,
-                        int epilogue, void* out, int ldo, float* slots, int* segmap,
-                        GemmSlots* result, uint32_t* status, cudaStream_t stream);
+                        int epilogue, void* out, int ldo, float* slots, GemmSlots* result,
+                        uint32_t* status, cudaStream_t stream);
 
 // Generic consumer: out = epilogue(sum of slots) for every (n < rows, m).
 cudaError_t gemm_finish_launch(const GemmSlots& s, int rows, int epilogue, void* out, int ldo,
@@ -107,49 +106,52 @@ __host__ __device__ inline long long gemm_unit_begin(long long units, int grid, 
 }
 
 #ifdef __CUDACC__
+// Slot of CTA c that holds `tile` (c's units start at tile ub(c) / kb_count).
+__device__ __forceinline__ size_t gemm_slot_of(const GemmSlots& s, int c, int tile) {
+  const int first_tile = static_cast<int>(gemm_unit_begin(s.units, s.grid, c) / s.kb_count);
+  return static_cast<size_t>(c) * kGemmSlotsPerCta + (tile - first_tile);
+}
+// CTAs [c0, c1] that covered `tile`: c covers unit u iff U*c/G <= u < U*(c+1)/G.
+__device__ __forceinline__ int2 gemm_tile_ctas(const GemmSlots& s, int tile) {
+  const long long u0 = static_cast<long long>(tile) * s.kb_count;
+  return make_int2(static_cast<int>(((u0 + 1) * s.grid - 1) / s.units),
+                   static_cast<int>(((u0 + s.kb_count) * s.grid - 1) / s.units));
+}
+
 // Sum of the slots holding element (n, m) of accumulator `acc`, in CTA order.
 __device__ inline float gemm_slot_sum(const GemmSlots& s, int n, int m, int acc) {
   const int tile = (m >> 7) * s.n_tiles + n / s.bn;
-  const int count = __ldcg(s.segcount + tile);
-  const int* map = s.segmap + tile * kGemmMaxSegsPerTile;
+  const int2 cs = gemm_tile_ctas(s, tile);
   const size_t within = static_cast<size_t>(acc) * s.bn * 128 +
                         static_cast<size_t>(n % s.bn) * 128 + (m & 127);
   const size_t slot_floats = static_cast<size_t>(s.pair) * s.bn * 128;
   float sum = 0.f;
-  for (int k = 0; k < count; ++k)
-    sum += __ldcg(s.slots + static_cast<size_t>(__ldcg(map + k)) * slot_floats + within);
+  for (int c = cs.x; c <= cs.y; ++c) sum += __ldcg(s.slots + gemm_slot_of(s, c, tile) * slot_floats + within);
   return sum;
 }
 
 // The same sum for four consecutive features m..m+3 (m % 4 == 0, one tile):
-// the tile's segment list is read once and the slot loads are issued together
-// before they are added (in CTA order, as gemm_slot_sum does).
+// the slot loads are issued together before they are added in CTA order.
 __device__ inline float4 gemm_slot_sum4(const GemmSlots& s, int n, int m, int acc) {
   const int tile = (m >> 7) * s.n_tiles + n / s.bn;
-  const int count = __ldcg(s.segcount + tile);
-  const int4* map4 = reinterpret_cast<const int4*>(s.segmap + tile * kGemmMaxSegsPerTile);
+  const int2 cs = gemm_tile_ctas(s, tile);
   const size_t within = static_cast<size_t>(acc) * s.bn * 128 +
                         static_cast<size_t>(n % s.bn) * 128 + (m & 127);
   const size_t slot_floats = static_cast<size_t>(s.pair) * s.bn * 128;
+  float4 v[kGemmMaxSegsPerTile];
+#pragma unroll
+  for (int k = 0; k < kGemmMaxSegsPerTile; ++k)
+    if (cs.x + k <= cs.y)
+      v[k] = __ldcg(reinterpret_cast<const float4*>(
+          s.slots + gemm_slot_of(s, cs.x + k, tile) * slot_floats + within));
   float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int k0 = 0; k0 < count; k0 += 4) {
-    const int4 ids = __ldcg(map4 + (k0 >> 2));
-    const int id[4] = {ids.x, ids.y, ids.z, ids.w};
-    float4 v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      v[j] = k0 + j < count
-                 ? __ldcg(reinterpret_cast<const float4*>(
-                       s.slots + static_cast<size_t>(id[j]) * slot_floats + within))
-                 : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (k0 + j < count) {
-        sum.x += v[j].x;
-        sum.y += v[j].y;
-        sum.z += v[j].z;
-        sum.w += v[j].w;
-      }
+  for (int k = 0; k < kGemmMaxSegsPerTile; ++k) {
+    if (cs.x + k <= cs.y) {
+      sum.x += v[k].x;
+      sum.y += v[k].y;
+      sum.z += v[k].z;
+      sum.w += v[k].w;
     }
   }
   return sum;

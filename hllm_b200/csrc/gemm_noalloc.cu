@@ -1,16 +1,15 @@
 // gemm_noalloc.cu -- a projection GEMM entry point that allocates nothing.
 //
-// hllm_b200_gemm keeps its stream-K scratch (F32 partial tiles and the
-// per-tile segment lists) in device memory that the library allocates on
-// first use.  Some callers cannot let a library allocate device memory: a
-// serving process that fixes its device-memory budget when it starts and
-// admits every request against it (hLLM's worker reserves each request's
-// bytes before running it, cpp/src/worker/control_service.cpp:391-461, so a
-// buffer allocated later is outside the accounting and can fail under load),
-// and hosts that own all device memory of a plugin.  This variant's scratch is
-// a file-scope static __device__ array of a fixed maximum size, part of the
-// library image: every GPU that loads the library holds it until the process
-// exits.
+// hllm_b200_gemm keeps its stream-K scratch (F32 partial tiles) in device
+// memory that the library allocates on first use.  Some callers cannot let a
+// library allocate device memory: a serving process that fixes its
+// device-memory budget when it starts and admits every request against it
+// (hLLM's worker reserves each request's bytes before running it,
+// cpp/src/worker/control_service.cpp:391-461, so a buffer allocated later is
+// outside the accounting and can fail under load), and hosts that own all
+// device memory of a plugin.  This variant's scratch is a file-scope static
+// __device__ array of a fixed maximum size, part of the library image: every
+// GPU that loads the library holds it until the process exits.
 //
 // Set-up: the first call on a device, with that device current, resolves the
 // array's device address with cudaGetSymbolAddress (the array's name in host
@@ -45,12 +44,10 @@ namespace {
 constexpr size_t kNoAllocSlotFloats = size_t{8} << 20;
 
 __device__ __align__(256) float g_noalloc_slots[kNoAllocSlotFloats];
-__device__ __align__(256) int g_noalloc_segmap[hb::kGemmMapInts];
 __device__ __align__(256) uint32_t g_noalloc_status[64];
 
 struct DevicePointers {
   float* slots = nullptr;
-  int* segmap = nullptr;
   uint32_t* status = nullptr;
   int sm_count = 0;
 };
@@ -73,7 +70,6 @@ hllm_b200_status pointers_for_current_device(DevicePointers* out) {
   if (it == g_pointers.end()) {
     DevicePointers p;
     e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p.slots), g_noalloc_slots);
-    if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p.segmap), g_noalloc_segmap);
     if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p.status), g_noalloc_status);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&p.sm_count, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess)
@@ -120,7 +116,7 @@ extern "C" hllm_b200_status hllm_b200_gemm_noalloc(const void* w, uint64_t m, ui
   hb::GemmSlots slots{};
   if (e == cudaSuccess)
     e = hb::gemm_launch(gw, gx, static_cast<int>(n), plan, static_cast<int>(epilogue), y,
-                        static_cast<int>(ldy), dp.slots, dp.segmap, &slots, dp.status, s);
+                        static_cast<int>(ldy), dp.slots, &slots, dp.status, s);
   if (e == cudaSuccess && plan.stream_k)
     e = hb::gemm_finish_launch(slots, static_cast<int>(n), static_cast<int>(epilogue), y,
                                static_cast<int>(ldy), s);

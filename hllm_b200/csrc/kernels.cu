@@ -218,44 +218,68 @@ __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, Gemm
   griddep_enter();
   const int t = blockIdx.x;
   float* xr = hidden + static_cast<size_t>(t) * width;
+  __half* o = out + static_cast<size_t>(t) * ld_out;
+  __shared__ float red[32];
+  auto block_sum = [&](float v) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float r = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+      r = warp_sum(r);
+      if (threadIdx.x == 0) red[0] = r;
+    }
+    __syncthreads();
+    return red[0];
+  };
+  constexpr int kVec = 4;  // float4 groups a thread keeps in registers
+  if ((width & 3) == 0 && width <= static_cast<int>(blockDim.x) * 4 * kVec) {
+    // A warp covers 128 consecutive features = one GEMM tile row; the row
+    // stays in registers between the sum of squares and the output.
+    float4 v[kVec];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kVec; ++k) {
+      const int c = (threadIdx.x + k * blockDim.x) * 4;
+      if (c < width) {
+        v[k] = *reinterpret_cast<const float4*>(xr + c);
+        if (has_slots) {
+          const float4 a = gemm_slot_sum4(slots, t, c, 0);
+          v[k].x += a.x;
+          v[k].y += a.y;
+          v[k].z += a.z;
+          v[k].w += a.w;
+          *reinterpret_cast<float4*>(xr + c) = v[k];
+        }
+        ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+      }
+    }
+    if (!w) return;
+    const float inv = 1.0f / sqrtf(block_sum(ss) / static_cast<float>(width) + eps);
+#pragma unroll
+    for (int k = 0; k < kVec; ++k) {
+      const int c = (threadIdx.x + k * blockDim.x) * 4;
+      if (c < width) {
+        const float4 g = *reinterpret_cast<const float4*>(w + c);
+        const __half2 lo = __floats2half2_rn(v[k].x * inv * g.x, v[k].y * inv * g.y);
+        const __half2 hi = __floats2half2_rn(v[k].z * inv * g.z, v[k].w * inv * g.w);
+        *reinterpret_cast<__half2*>(o + c) = lo;
+        *reinterpret_cast<__half2*>(o + c + 2) = hi;
+      }
+    }
+    return;
+  }
   float ss = 0.f;
-  if ((width & 3) == 0) {
-    // A warp covers 128 consecutive features = one GEMM tile row.
-    for (int c = threadIdx.x * 4; c < width; c += blockDim.x * 4) {
-      float4 v = *reinterpret_cast<const float4*>(xr + c);
-      if (has_slots) {
-        const float4 a = gemm_slot_sum4(slots, t, c, 0);
-        v.x += a.x;
-        v.y += a.y;
-        v.z += a.z;
-        v.w += a.w;
-        *reinterpret_cast<float4*>(xr + c) = v;
-      }
-      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+    float v = xr[c];
+    if (has_slots) {
+      v += gemm_slot_sum(slots, t, c, 0);
+      xr[c] = v;
     }
-  } else {
-    for (int c = threadIdx.x; c < width; c += blockDim.x) {
-      float v = xr[c];
-      if (has_slots) {
-        v += gemm_slot_sum(slots, t, c, 0);
-        xr[c] = v;
-      }
-      ss += v * v;
-    }
+    ss += v * v;
   }
   if (!w) return;
-  __shared__ float red[32];
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    v = warp_sum(v);
-    if (threadIdx.x == 0) red[0] = v;
-  }
-  __syncthreads();
-  const float inv = 1.0f / sqrtf(red[0] / static_cast<float>(width) + eps);
-  __half* o = out + static_cast<size_t>(t) * ld_out;
+  const float inv = 1.0f / sqrtf(block_sum(ss) / static_cast<float>(width) + eps);
   for (int c = threadIdx.x; c < width; c += blockDim.x) o[c] = __float2half_rn(xr[c] * inv * w[c]);
 }
 

@@ -182,9 +182,10 @@ struct hllm_b200_stage {
   // the query buffer and the layer's K/V caches.  HLLM_B200_TC_PREFILL=0
   // selects the mma.sync kernel instead (for comparisons).
   bool tc_prefill = false;
+  // Decode attention's L2 lookahead in pages per stream (HLLM_B200_KV_PREFETCH).
+  int kv_prefetch = 6;
   std::vector<hb::TcMaps> tc_maps;
   float* slots = nullptr;  // stream-K GEMM slots, consumed by the next kernel
-  int* segmap = nullptr;   // their per-tile segment lists
 
   // pinned host staging
   // Descriptor uploads go through a ring of pinned buffers so that enqueue-only
@@ -585,10 +586,10 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
     s->pre_counters = s->alloc<int>(s->pre_counter_ints);
   }
   s->slots = s->alloc<float>(hb::gemm_max_slot_floats(s->sm_count));
-  s->segmap = s->alloc<int>(hb::kGemmMapInts);
   {
     // TMA maps per layer: K and V for the balanced decode pass (head sizes
     // 64/128/256) and, with the query buffer, for the tcgen05 prefill.
+    if (const char* kp = std::getenv("HLLM_B200_KV_PREFETCH")) s->kv_prefetch = std::atoi(kp);
     const char* env = std::getenv("HLLM_B200_TC_PREFILL");
     s->tc_prefill = hb::attn_prefill_tc_supported(static_cast<int>(s->dim),
                                                   static_cast<int>(s->hq / s->hkv)) &&
@@ -951,7 +952,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     hb::GemmSlots qslots{};
     PLAUNCH(gk, gemm_bytes(s->qkvw, T, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->qkvw, T, s->h, 1),
             hb::gemm_launch(L.g_qkv, s->in_xn, T, pq, hb::kEpiStoreF32, s->qkv,
-                            static_cast<int>(s->qkvw), s->slots, s->segmap, &qslots, s->status, s->stream));
+                            static_cast<int>(s->qkvw), s->slots, &qslots, s->status, s->stream));
     hb::QkvPostArgs qa{};
     qa.qkv = s->qkv;
     qa.slots = qslots;
@@ -991,6 +992,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     aa.split_tokens = p.split_tokens;
     aa.qtile_tokens = p.qtile_tokens;
     aa.decode_ctas = p.decode_ctas;
+    aa.kv_prefetch = s->kv_prefetch;
     aa.prefill_splits = p.prefill_splits;
     aa.pre_part = s->pre_part;
     aa.pre_counters = s->pre_counters;
@@ -1015,7 +1017,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     const hb::GemmPlan po = hb::gemm_plan(L.g_o, T, s->sm_count);
     hb::GemmSlots oslots{};
     PLAUNCH(gk, gemm_bytes(s->h, T, s->qw, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->qw, 1),
-            hb::gemm_launch(L.g_o, s->in_attn, T, po, hb::kEpiResidual, s->hidden, h, s->slots, s->segmap,
+            hb::gemm_launch(L.g_o, s->in_attn, T, po, hb::kEpiResidual, s->hidden, h, s->slots,
                             &oslots, s->status, s->stream));
     PLAUNCH(kProfNorm, 0, 0,
             hb::residual_norm_launch(s->hidden, T, h, po.stream_k ? &oslots : nullptr,
@@ -1026,7 +1028,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     hb::GemmSlots gslots{};
     PLAUNCH(gk, gemm_bytes(s->I, T, s->h, 2, hb::kEpiSwiGLU), gemm_flops(s->I, T, s->h, 2),
             hb::gemm_launch(L.g_gu, s->in_xn, T, pg, hb::kEpiSwiGLU, s->act,
-                            static_cast<int>(s->I_pad), s->slots, s->segmap, &gslots, s->status, s->stream));
+                            static_cast<int>(s->I_pad), s->slots, &gslots, s->status, s->stream));
     if (pg.stream_k)
       PLAUNCH(kProfSwiglu, 0, 0,
               hb::swiglu_launch(gslots, T, s->act, static_cast<int>(s->I_pad), s->stream));
@@ -1034,7 +1036,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     const hb::GemmPlan pd = hb::gemm_plan(L.g_down, T, s->sm_count);
     hb::GemmSlots dslots{};
     PLAUNCH(gk, gemm_bytes(s->h, T, s->I, 1, hb::kEpiResidual), gemm_flops(s->h, T, s->I, 1),
-            hb::gemm_launch(L.g_down, s->in_act, T, pd, hb::kEpiResidual, s->hidden, h, s->slots, s->segmap,
+            hb::gemm_launch(L.g_down, s->in_act, T, pd, hb::kEpiResidual, s->hidden, h, s->slots,
                             &dslots, s->status, s->stream));
     const float* next_norm = li + 1 < s->n_layers ? s->layers[li + 1].in_norm : nullptr;
     if (pd.stream_k || next_norm)
@@ -1058,7 +1060,7 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
       PLAUNCH(S <= 128 ? kProfGemmDecode : kProfGemmPrefill,
               gemm_bytes(s->V, S, s->h, 1, hb::kEpiStoreF32), gemm_flops(s->V, S, s->h, 1),
               hb::gemm_launch(s->g_head, s->in_xs, S, ph, hb::kEpiStoreF32, s->logits,
-                              static_cast<int>(s->V), s->slots, s->segmap, &hslots, s->status, s->stream));
+                              static_cast<int>(s->V), s->slots, &hslots, s->status, s->stream));
       if (ph.stream_k)
         PLAUNCH(kProfSwiglu, 0, 0,
                 hb::gemm_finish_launch(hslots, S, hb::kEpiStoreF32, s->logits,

@@ -363,8 +363,8 @@ hllm_b200_status hllm_b200_gemm(const void* w, uint64_t m, uint64_t k_pad, uint3
  * a serving process that fixes its device budget at start-up and admits
  * requests against it, or a host that owns all of a plugin's device memory.
  * Its split-K scratch is a static device array of 32 MiB of partial sums, plus
- * 34 KiB of per-tile segment lists (512 x 17 ints) and a 256-byte status word,
- * that every GPU loading the library holds until the process exits.
+ * a 256-byte status word, that every GPU loading the library holds until the
+ * process exits.
  * Splits that need more partial-sum storage than that are rejected with
  * HLLM_B200_RESOURCE_EXHAUSTED and a message; plans that need none always run.
  * The first call on a device, with that device current, resolves the array's
