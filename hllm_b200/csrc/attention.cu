@@ -509,36 +509,17 @@ __global__ void __launch_bounds__(128)
   }
   griddep_enter();
   int issued = 0;
-  const int pf = min(a.kv_prefetch, 31);
-  auto prefetch_page = [&](int bid, int kvh) {
-    const int y = (bid * hkv + kvh) * 16;
-#pragma unroll
-    for (int h = 0; h < D / 64; ++h) {
-      tma_prefetch_2d(&maps.k, h * 64, y);
-      tma_prefetch_2d(&maps.v, h * 64, y);
-    }
-  };
   auto issue = [&](int i) {
     uint8_t* kd = ring + (i % ST) * stage_bytes;
-    bool fresh = false;
     if (ic.r != tab_r || ic.q < tab_q0 || ic.q >= tab_q0 + 32) {
       tab_r = ic.r;
       tab_q0 = ic.q;
-      fresh = true;
       const int qq = ic.q + lane;
       tab_val = qq < ic.pages && qq < a.max_blocks
                     ? __ldg(a.block_tables + static_cast<size_t>(ic.r) * a.max_blocks + qq)
                     : -1;
     }
     const int bid_raw = __shfl_sync(0xffffffffu, tab_val, ic.q - tab_q0);
-    if (pf > 0) {
-      // L2 lookahead along this stream: page q + pf now, and on a fresh
-      // table window the pages q + 1 .. q + pf - 1 too (one lane each).
-      const int ahead = ic.q + pf - tab_q0;
-      const int pbid = __shfl_sync(0xffffffffu, tab_val, ahead & 31);
-      if (lane == 0 && ahead < 32 && pbid >= 0) prefetch_page(pbid, ic.kvh);
-      if (fresh && lane >= 1 && lane < pf && tab_val >= 0) prefetch_page(tab_val, ic.kvh);
-    }
     // First page of a stream: its query heads ride along.
     const bool with_q = i == 0 || ic.q == 0;
     const __half* qs =

@@ -33,8 +33,6 @@ struct AttnArgs {
   int qtile_tokens;            // query tokens per prefill tile
   float scale;                 // 1/sqrt(d)
   int decode_ctas;             // balanced decode grid (attn_decode_ctas), head sizes 64/128/256
-  int kv_prefetch;             // balanced decode: pages of a stream prefetched into L2 ahead
-                               // of its ring loads (0 = none)
   float* part_o;               // partial outputs: [splits][Hq][d] (combine path) or
                                // [pieces][Hq/Hkv][d] (balanced path)
   float* part_ml;              // matching running max, denominator pairs

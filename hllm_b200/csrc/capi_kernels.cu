@@ -177,7 +177,6 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
   a.dim = static_cast<int>(dim);
   a.max_blocks = static_cast<int>(max_blocks);
   a.split_tokens = static_cast<int>(split_tokens);
-  a.kv_prefetch = 6;
   a.qtile_tokens = hb::attn_qtile_tokens(static_cast<int>(hq / hkv));
   a.scale = 1.0f / std::sqrt(static_cast<float>(dim));
   a.out = reinterpret_cast<__half*>(out);

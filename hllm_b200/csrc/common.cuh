@@ -147,14 +147,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
-// Prefetch of one 2-D box into L2 (no shared memory, no completion; boxes
-// outside the tensor are ignored).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t c0, int32_t c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(c0), "r"(c1)
-               : "memory");
-}
 // 2-D tiled load with an L2 eviction-priority hint (policy from createpolicy).
 __device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map,
                                                  uint64_t* bar, int32_t c0, int32_t c1,

@@ -199,11 +199,14 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 5) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc(kGemmBlockM, BN, 0);
       uint32_t it = 0;
       long long cursor = ub;
       Segment sg;
       for (int j = 0; next_segment(p, cursor, ue, j, sg); ++j) {
+        // The last token tile of a ragged N multiplies only its valid
+        // columns, rounded up to the MMA's 16-column step.
+        const int nv = min(BN, p.n - (sg.tile % p.n_tiles) * BN);
+        const uint32_t idesc = umma_idesc(kGemmBlockM, min(BN, (nv + 15) & ~15), 0);
         const int b = j % S::kAccBufs;
         const uint32_t bph = (j / S::kAccBufs) & 1u;
         if (!mbar_wait(&tempty[b], bph ^ 1u, p.status)) goto mma_done;
@@ -396,6 +399,8 @@ GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override, in
     // segment map holds a bounded number of tiles.
     grid = std::min<long long>(grid, pl.tiles * (kGemmMaxSegsPerTile - 2));
     if (pl.tiles > kGemmMaxStreamKTiles) pl.stream_k = false;
+    // the consumers locate slots with 32-bit arithmetic on units x grid
+    if (pl.units * (grid + 1) >= (1LL << 31)) pl.stream_k = false;
   }
   if (!pl.stream_k) grid = std::min<long long>(grid, pl.tiles);
   pl.grid = static_cast<int>(grid);

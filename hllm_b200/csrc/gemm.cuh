@@ -106,16 +106,20 @@ __host__ __device__ inline long long gemm_unit_begin(long long units, int grid, 
 }
 
 #ifdef __CUDACC__
-// Slot of CTA c that holds `tile` (c's units start at tile ub(c) / kb_count).
-__device__ __forceinline__ size_t gemm_slot_of(const GemmSlots& s, int c, int tile) {
-  const int first_tile = static_cast<int>(gemm_unit_begin(s.units, s.grid, c) / s.kb_count);
-  return static_cast<size_t>(c) * kGemmSlotsPerCta + (tile - first_tile);
-}
 // CTAs [c0, c1] that covered `tile`: c covers unit u iff U*c/G <= u < U*(c+1)/G.
+// The plan keeps U*G below 2^31, so 32-bit arithmetic is exact.
 __device__ __forceinline__ int2 gemm_tile_ctas(const GemmSlots& s, int tile) {
-  const long long u0 = static_cast<long long>(tile) * s.kb_count;
-  return make_int2(static_cast<int>(((u0 + 1) * s.grid - 1) / s.units),
-                   static_cast<int>(((u0 + s.kb_count) * s.grid - 1) / s.units));
+  const unsigned u0 = static_cast<unsigned>(tile) * static_cast<unsigned>(s.kb_count);
+  const unsigned g = static_cast<unsigned>(s.grid), u = static_cast<unsigned>(s.units);
+  return make_int2(static_cast<int>(((u0 + 1) * g - 1) / u),
+                   static_cast<int>(((u0 + s.kb_count) * g - 1) / u));
+}
+// Slot of the first CTA c0 of `tile` (c0's units may start in an earlier
+// tile).  Every later CTA of the tile starts inside it, so its slot is c * 3.
+__device__ __forceinline__ int gemm_first_slot(const GemmSlots& s, int c0, int tile) {
+  const unsigned begin = static_cast<unsigned>(s.units) * static_cast<unsigned>(c0) /
+                         static_cast<unsigned>(s.grid);
+  return c0 * kGemmSlotsPerCta + (tile - static_cast<int>(begin / static_cast<unsigned>(s.kb_count)));
 }
 
 // Sum of the slots holding element (n, m) of accumulator `acc`, in CTA order.
@@ -125,33 +129,42 @@ __device__ inline float gemm_slot_sum(const GemmSlots& s, int n, int m, int acc)
   const size_t within = static_cast<size_t>(acc) * s.bn * 128 +
                         static_cast<size_t>(n % s.bn) * 128 + (m & 127);
   const size_t slot_floats = static_cast<size_t>(s.pair) * s.bn * 128;
-  float sum = 0.f;
-  for (int c = cs.x; c <= cs.y; ++c) sum += __ldcg(s.slots + gemm_slot_of(s, c, tile) * slot_floats + within);
+  float sum = __ldcg(s.slots + static_cast<size_t>(gemm_first_slot(s, cs.x, tile)) * slot_floats + within);
+  for (int c = cs.x + 1; c <= cs.y; ++c)
+    sum += __ldcg(s.slots + static_cast<size_t>(c) * kGemmSlotsPerCta * slot_floats + within);
   return sum;
 }
 
 // The same sum for four consecutive features m..m+3 (m % 4 == 0, one tile):
-// the slot loads are issued together before they are added in CTA order.
+// slot loads go out four at a time (a few registers each, so the consumer
+// kernels keep their occupancy) and are added in CTA order.
 __device__ inline float4 gemm_slot_sum4(const GemmSlots& s, int n, int m, int acc) {
   const int tile = (m >> 7) * s.n_tiles + n / s.bn;
   const int2 cs = gemm_tile_ctas(s, tile);
   const size_t within = static_cast<size_t>(acc) * s.bn * 128 +
                         static_cast<size_t>(n % s.bn) * 128 + (m & 127);
   const size_t slot_floats = static_cast<size_t>(s.pair) * s.bn * 128;
-  float4 v[kGemmMaxSegsPerTile];
-#pragma unroll
-  for (int k = 0; k < kGemmMaxSegsPerTile; ++k)
-    if (cs.x + k <= cs.y)
-      v[k] = __ldcg(reinterpret_cast<const float4*>(
-          s.slots + gemm_slot_of(s, cs.x + k, tile) * slot_floats + within));
+  const float* base = s.slots + within;
+  const int first = gemm_first_slot(s, cs.x, tile);
   float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c0 = cs.x; c0 <= cs.y; c0 += 4) {
+    float4 v[4];
 #pragma unroll
-  for (int k = 0; k < kGemmMaxSegsPerTile; ++k) {
-    if (cs.x + k <= cs.y) {
-      sum.x += v[k].x;
-      sum.y += v[k].y;
-      sum.z += v[k].z;
-      sum.w += v[k].w;
+    for (int j = 0; j < 4; ++j) {
+      const int c = c0 + j;
+      const int slot = c == cs.x ? first : c * kGemmSlotsPerCta;
+      v[j] = c <= cs.y ? __ldcg(reinterpret_cast<const float4*>(
+                             base + static_cast<size_t>(slot) * slot_floats))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (c0 + j <= cs.y) {
+        sum.x += v[j].x;
+        sum.y += v[j].y;
+        sum.z += v[j].z;
+        sum.w += v[j].w;
+      }
     }
   }
   return sum;

@@ -182,8 +182,6 @@ struct hllm_b200_stage {
   // the query buffer and the layer's K/V caches.  HLLM_B200_TC_PREFILL=0
   // selects the mma.sync kernel instead (for comparisons).
   bool tc_prefill = false;
-  // Decode attention's L2 lookahead in pages per stream (HLLM_B200_KV_PREFETCH).
-  int kv_prefetch = 6;
   std::vector<hb::TcMaps> tc_maps;
   float* slots = nullptr;  // stream-K GEMM slots, consumed by the next kernel
 
@@ -589,7 +587,6 @@ void build_stage(hllm_b200_stage* s, const hllm_b200_stage_desc& d) {
   {
     // TMA maps per layer: K and V for the balanced decode pass (head sizes
     // 64/128/256) and, with the query buffer, for the tcgen05 prefill.
-    if (const char* kp = std::getenv("HLLM_B200_KV_PREFETCH")) s->kv_prefetch = std::atoi(kp);
     const char* env = std::getenv("HLLM_B200_TC_PREFILL");
     s->tc_prefill = hb::attn_prefill_tc_supported(static_cast<int>(s->dim),
                                                   static_cast<int>(s->hq / s->hkv)) &&
@@ -992,7 +989,6 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
     aa.split_tokens = p.split_tokens;
     aa.qtile_tokens = p.qtile_tokens;
     aa.decode_ctas = p.decode_ctas;
-    aa.kv_prefetch = s->kv_prefetch;
     aa.prefill_splits = p.prefill_splits;
     aa.pre_part = s->pre_part;
     aa.pre_counters = s->pre_counters;
