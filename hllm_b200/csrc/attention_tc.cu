@@ -27,7 +27,7 @@
 // transpose is needed.  Scores of keys past a row's position or past the
 // context are masked to p = 0; pages past the context are filled from a valid
 // page so that no stale shared memory is multiplied in.  Every wait is bounded
-// (common.cuh).  No TMA multicast.
+// (common.cuh); every CTA issues its own TMA copies.
 #include <cudaTypedefs.h>
 #include <math.h>
 
