@@ -395,8 +395,8 @@ GemmPlan gemm_plan(const GemmWeight& w, int n, int sm_count, int bn_override, in
   grid = std::max<long long>(1, std::min<long long>(grid, pl.units));
   pl.stream_k = pl.tiles < 2 * grid;
   if (pl.stream_k) {
-    // Each tile's segments must fit the consumer's segment list, and the
-    // segment map holds a bounded number of tiles.
+    // A tile is split over at most kGemmMaxSegsPerTile CTAs (bounding the
+    // consumers' slot loads), and stream-K is kept to plans of few tiles.
     grid = std::min<long long>(grid, pl.tiles * (kGemmMaxSegsPerTile - 2));
     if (pl.tiles > kGemmMaxStreamKTiles) pl.stream_k = false;
     // the consumers locate slots with 32-bit arithmetic on units x grid
