@@ -11,8 +11,8 @@
 //
 //   decode rows:  head sizes 64/128/256 -- the batch's KV pages split evenly
 //                 over one wave of warps (ranges cross row boundaries), QK^T
-//                 and PV on the tensor cores (mma.sync), pieces merged by the
-//                 last warp of each (row, kv head).  Other head sizes -- split-K
+//                 and PV on the tensor cores (mma.sync), split streams' pieces
+//                 merged by a second, small pass.  Other head sizes -- split-K
 //                 with one CTA per (kv head, context split) streaming 16-token
 //                 pages with cp.async.bulk (mbarrier completion, bounded
 //                 waits), then a combine pass.
@@ -252,8 +252,9 @@ __global__ void __launch_bounds__(kDecThreads)
 // stream it touches it keeps a piece (m, l, unnormalised O of the G query
 // heads).  A stream inside one warp is normalised and stored at once;
 // otherwise its pieces go to part_o/part_ml at index (stream + warp) -- unique,
-// since both grow along the sequence -- and the last of the stream's warps to
-// arrive merges them in warp order (deterministic).
+// since both grow along the sequence -- and the warp holding the stream's first
+// page records the stream's warp range.  The merge pass (decode_merge_kernel)
+// then combines each split stream's pieces in warp order (deterministic).
 //
 // Per warp: the G query heads of the kv head are the first G rows of an
 // m16n8k16 tile (rows G..15 are zero), so QK^T and PV run on the tensor cores.
@@ -335,11 +336,14 @@ __device__ __forceinline__ void load_row_pages(const AttnArgs& a, int base, int 
 }
 
 // Merges the ns pieces of one stream (pieces p0 + s * G + g, s < ns, g < G)
-// in piece order and stores the G normalised head outputs at `out`.
+// in piece order and stores the G normalised head outputs at `out`.  Called
+// by `warps` warps of a CTA: few pieces are merged by warp 0 in one round of
+// loads; otherwise warp `warp` takes heads warp, warp + warps, ...
 template <int D>
 __device__ __noinline__ void decode_merge(const AttnArgs& a, size_t p0, int ns, int G,
-                                          __half* out, int lane) {
+                                          __half* out, int lane, int warp, int warps) {
   if (G * ns <= 32 && (G & (G - 1)) == 0) {
+    if (warp != 0) return;
     // One (piece, head) per lane: j = s * G + g.  Lanes with equal g are the
     // lanes j ^ (multiples of G), so xor shuffles reduce per head.
     const int j = lane;
@@ -390,8 +394,8 @@ __device__ __noinline__ void decode_merge(const AttnArgs& a, size_t p0, int ns, 
     }
     return;
   }
-  // Many pieces (or a group size that is not a power of two): one head at a time.
-  for (int gg = 0; gg < G; ++gg) {
+  // Many pieces (or a group size that is not a power of two): a head per warp.
+  for (int gg = warp; gg < G; gg += warps) {
     const float* ml = a.part_ml + (p0 + gg) * 2;
     const size_t mls = static_cast<size_t>(G) * 2;
     float mm = -INFINITY;
@@ -627,6 +631,10 @@ __global__ void __launch_bounds__(128)
       const int w0 = static_cast<int>(((f0 + 1) * W - 1) / total);
       const int w1 = static_cast<int>(((f0 + c.pages) * W - 1) / total);
       __half* out = a.out + static_cast<size_t>(c.t) * a.ld_out + static_cast<size_t>(c.kvh) * G * D;
+      const int stream = c.r * hkv + c.kvh;
+      // The warp that holds the stream's first page records which warps hold
+      // its pieces, for the merge pass (every stream, every launch).
+      if (w == w0 && lane == 0) a.counters[stream] = w0 | (w1 << 16);
       if (w0 == w1) {  // the whole stream in this warp: normalise and store
         if (g < G) {
           const float inv = 1.0f / lt;
@@ -635,9 +643,7 @@ __global__ void __launch_bounds__(128)
             *reinterpret_cast<__half2*>(out + g * D + db * 8 + (lane & 3) * 2) =
                 __floats2half2_rn(o[db][0] * inv, o[db][1] * inv);
         }
-      } else {
-        const int stream = c.r * hkv + c.kvh;
-        if (g < G) {
+      } else if (g < G) {  // one piece of a split stream; the merge pass combines them
           const size_t piece = static_cast<size_t>(stream + w) * G + g;
           float* dst = a.part_o + piece * D;
 #pragma unroll
@@ -647,20 +653,6 @@ __global__ void __launch_bounds__(128)
           if ((lane & 3) == 0)
             *reinterpret_cast<float2*>(a.part_ml + piece * 2) =
                 make_float2(m * 0.6931471805599453f, lt);  // natural-log domain
-        }
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-          int* counter = a.counters + stream;
-          last = atomicAdd(counter, 1) == w1 - w0;
-          if (last) *counter = 0;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          __threadfence();
-          decode_merge<D>(a, static_cast<size_t>(stream + w0) * G, w1 - w0 + 1, G, out, lane);
-        }
       }
     }
     cursor_next(a, c);
@@ -668,6 +660,32 @@ __global__ void __launch_bounds__(128)
   // Pages still in flight land before the warp exits (only after a failed
   // wait; bounded).
   for (; i < issued; ++i) mbar_wait(&full[i % ST], (i / ST) & 1u, a.status);
+}
+
+// The merge pass of the balanced decode kernel: one CTA per (decode row, kv
+// head) stream whose pages were split over several warps combines the pieces
+// in warp order and stores the normalised heads.  A separate pass keeps the
+// decode warps free of fences and arrival counters, whose round trips held up
+// the warps that end a split stream.
+template <int D>
+__global__ void __launch_bounds__(128) decode_merge_kernel(const AttnArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int stream = blockIdx.x;
+  const int r = stream / a.hkv, kvh = stream % a.hkv;
+  if (r >= a.rows || __ldg(a.row_count + r) != 1) return;
+  const int t = __ldg(a.cu_seqlens + r);
+  const int G = a.hq / a.hkv;
+  griddep_enter();
+  const int rec = __ldcg(a.counters + stream);
+  const int w0 = rec & 0xffff, w1 = rec >> 16;
+  if (w1 <= w0) return;
+  if (w1 >= a.decode_ctas * 4) {  // not a record of this pass's warps
+    if (lane == 0) atomicOr(a.status, kDevBadIndex);
+    return;
+  }
+  __half* out = a.out + static_cast<size_t>(t) * a.ld_out + static_cast<size_t>(kvh) * G * D;
+  decode_merge<D>(a, static_cast<size_t>(stream + w0) * G, w1 - w0 + 1, G, out, lane,
+                  threadIdx.x >> 5, 4);
 }
 
 // One CTA per (decode row, query head): merge the row's splits.
@@ -1139,8 +1157,11 @@ template <int D>
 cudaError_t launch_decode_mma(const AttnArgs& a, const TcMaps& maps, cudaStream_t stream) {
   const int group = a.hq / a.hkv;
   if (a.decode_ctas <= 0 || decode_mma_setup<D>(group) == 0) return cudaErrorInvalidValue;
-  return launch_dependent(decode_attn_mma_kernel<D>, dim3(a.decode_ctas), dim3(128),
-                          decode_mma_smem<D>(group), stream, maps, a);
+  const cudaError_t e = launch_dependent(decode_attn_mma_kernel<D>, dim3(a.decode_ctas), dim3(128),
+                                         decode_mma_smem<D>(group), stream, maps, a);
+  if (e != cudaSuccess) return e;
+  const unsigned streams = static_cast<unsigned>(a.rows) * static_cast<unsigned>(a.hkv);
+  return launch_dependent(decode_merge_kernel<D>, dim3(streams), dim3(128), 0, stream, a);
 }
 
 }  // namespace
@@ -1197,7 +1218,7 @@ cudaError_t attn_decode_launch(const AttnArgs& a, const TcMaps& maps, int total_
   return e;
 }
 
-int attn_decode_launches(int dim) { return attn_decode_balanced(dim) ? 1 : 2; }
+int attn_decode_launches(int) { return 2; }  // the pass and its merge / combine
 
 cudaError_t attn_prefill_launch(const AttnArgs& a, int total_qtiles, cudaStream_t stream) {
   if (total_qtiles <= 0) return cudaSuccess;

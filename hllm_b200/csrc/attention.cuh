@@ -36,7 +36,8 @@ struct AttnArgs {
   float* part_o;               // partial outputs: [splits][Hq][d] (combine path) or
                                // [pieces][Hq/Hkv][d] (balanced path)
   float* part_ml;              // matching running max, denominator pairs
-  int* counters;               // [rows][Hkv] zero-initialised; returned to zero after use
+  int* counters;               // [rows][Hkv] balanced decode: each stream's warp range,
+                               // written by the decode pass for its merge pass
   int prefill_splits;          // key splits per prefill tile (attn_prefill_splits), >= 1
   float* pre_part;             // [qtiles][Hkv][splits] x 64 rows x (DP + 2): split rows, (m, l)
   int* pre_counters;           // [qtiles][Hkv] zero-initialised; returned to zero after use
@@ -50,8 +51,8 @@ int attn_qtile_tokens(int group);
 
 // Decode rows (one new token).  Head sizes 64/128/256: the decode rows' KV
 // pages are split evenly over 4 * decode_ctas warps regardless of row
-// lengths, each warp streaming its pages by TMA into its own ring, and the
-// pieces of a (row, kv head) are merged by its last warp to finish
+// lengths, each warp streaming its pages by TMA into its own ring; a second
+// launch merges the pieces of each (row, kv head) split over several warps
 // (split_tokens/cu_splits unused).  Other head sizes: split-K over
 // split_tokens-key splits, one CTA per (kv head, split), then a combine pass.
 // The balanced pass streams pages through maps.k / maps.v (attn_make_kv_maps).

@@ -238,10 +238,11 @@ hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
       static_cast<int>(dim), static_cast<int>(hkv), static_cast<int>(total_qtiles), a.prefill_splits);
   if (part_floats || pre_floats) {
     // Split outputs live in a grow-only buffer per device, kept for the
-    // process: a fixed block of arrival counters at its head (decode: one per
-    // (row, kv head) in the first half; prefill: one per (tile, kv head) in the
-    // second half; zeroed on allocation and returned to zero by the kernels),
-    // then the decode pieces, then the prefill pieces.
+    // process: a fixed block of ints at its head (decode: one warp-range record
+    // per (row, kv head) in the first half, written by each decode pass;
+    // prefill: one arrival counter per (tile, kv head) in the second half,
+    // zeroed on allocation and returned to zero by the kernels), then the
+    // decode pieces, then the prefill pieces.
     static std::mutex mu;
     static std::map<int, std::pair<float*, size_t>> buffers;
     constexpr size_t kCounters = 1 << 16;

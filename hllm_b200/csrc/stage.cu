@@ -171,7 +171,7 @@ struct hllm_b200_stage {
   float* logits = nullptr;
   double* sample_scratch = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
-  int* attn_counters = nullptr;  // [R_max][Hkv] split arrival counters (self-resetting)
+  int* attn_counters = nullptr;  // [R_max][Hkv] decode streams' warp ranges (per launch)
   size_t attn_counter_ints = 0;
   float* pre_part = nullptr;     // prefill key-split pieces
   int* pre_counters = nullptr;   // [max qtiles][Hkv] split arrival counters (self-resetting)
@@ -1074,9 +1074,9 @@ void enqueue_step(hllm_b200_stage* s, const hllm_b200_row* rows, const StepPlan&
   s->last_tokens = p.tokens;
 }
 
-// Attention kernels return their arrival counters (decode streams, prefill
-// tiles) to zero when they finish; a kernel that ended early on a failed wait
-// may leave one behind, so a failed step clears them.
+// Prefill attention returns its arrival counters to zero when it finishes; a
+// kernel that ended early on a failed wait may leave one behind, so a failed
+// step clears them (and the decode streams' warp-range records).
 void reset_counters(hllm_b200_stage* s) {
   check_cuda(cudaMemsetAsync(s->attn_counters, 0, s->attn_counter_ints * sizeof(int), s->stream),
              "counter reset");
