@@ -54,7 +54,9 @@ METRIC = "Qwen3-4B F16 ragged-batch tokens/s at 1/2/4/8 B200; p50 TTFT; HBM GB/s
 SEED = 20261201
 MAX_ACTIVE = 64
 CHUNK = 512
-PIPELINE_LIMIT_S = 300.0  # wall-clock limit of a multi-GPU (pipeline) run
+PIPELINE_LIMIT_S = float(os.environ.get("HLLM_B200_PIPELINE_LIMIT_S", "300"))
+# wall-clock limit of a multi-GPU (pipeline) run
+PIPELINE_PROGRESS = {"phase": "init", "tick": -1, "where": "start"}  # reported on a stall
 
 
 def peaks():
@@ -858,10 +860,12 @@ def run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, h
     def tick(t, m, j):
         admits, rows, fin = plans[m][j]
         n_tok = sum(r[2] for r in rows)
+        PIPELINE_PROGRESS.update(tick=t, where="recv")
         ptr = None
         if not first:
             ptr = links.recv_activation(n_tok)  # posted before any synchronisation
         if t == T0:
+            PIPELINE_PROGRESS["where"] = "timing barrier"
             torch.cuda.synchronize()
             dist.barrier()
             if profile:
@@ -888,6 +892,7 @@ def run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, h
                 if j > 0:
                     prev = [r[0] for r in plans[m][j - 1][1] if r[3]]
                     if prev:
+                        PIPELINE_PROGRESS["where"] = "recv tokens"
                         for rid, tok in zip(prev, links.recv_tokens(len(prev))):
                             last_tok[(m, rid)] = int(tok)
                 ids = []
@@ -904,14 +909,17 @@ def run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, h
                     ids_dev[:n_tok].copy_(ids_host, non_blocking=True)
                 ptr = ids_dev.data_ptr()
                 h2d += 4 * n_tok
+        PIPELINE_PROGRESS["where"] = "step"
         _lib.check(L.hllm_b200_step_async(stage.handle, arr, len(rows), ptr))
         a, b = C.c_uint64(), C.c_uint64()
         _lib.check(L.hllm_b200_stage_last_transfer(stage.handle, C.byref(a), C.byref(b)))
         h2d += a.value
         d2h = b.value
+        PIPELINE_PROGRESS["where"] = "send"
         if not final:
             links.send_activation(boundary, n_tok)
         elif host_mode:
+            PIPELINE_PROGRESS["where"] = "sync for tokens"
             _lib.check(L.hllm_b200_stage_sync(stage.handle))
             samp = [r for r in rows if r[3]]
             if samp:
@@ -935,10 +943,12 @@ def run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, h
             acc["d2h"] += d2h
         if t == T1 - 1:
             end.record(stream)
+        PIPELINE_PROGRESS["where"] = "release"
         for rid in fin:
             stage.release(seqs[m].pop(rid))
 
     run_ticks(sched, rank, tick)
+    PIPELINE_PROGRESS.update(where="drain")
     links.drain()
     _lib.check(L.hllm_b200_stage_sync(stage.handle))
     torch.cuda.synchronize()
@@ -976,8 +986,10 @@ def ours_pipeline(args, world, rank, local):
     # with an error after PIPELINE_LIMIT_S seconds (a normal run takes a few
     # minutes at 8 GPUs).
     def stalled():
-        print(json.dumps({"error": f"pipeline run on rank {rank} exceeded {PIPELINE_LIMIT_S} s"}),
-              file=sys.stderr, flush=True)
+        import faulthandler
+        print(json.dumps({"error": f"pipeline run on rank {rank} exceeded {PIPELINE_LIMIT_S} s",
+                          "progress": PIPELINE_PROGRESS}), file=sys.stderr, flush=True)
+        faulthandler.dump_traceback(file=sys.stderr, all_threads=True)
         os._exit(3)
     watchdog = threading.Timer(PIPELINE_LIMIT_S, stalled)
     watchdog.daemon = True
@@ -994,6 +1006,7 @@ def ours_pipeline(args, world, rank, local):
     stream = torch.cuda.ExternalStream(L.hllm_b200_stage_stream(stage.handle))
     links = DeviceLinks(rank, world, stream, MAX_ACTIVE + CHUNK + 64, cfg.hidden_size,
                         token_group=token_group, pair_groups=pair_groups)
+    PIPELINE_PROGRESS["where"] = "connect"
     links.connect()
 
     def fresh_plans():
@@ -1006,14 +1019,18 @@ def ours_pipeline(args, world, rank, local):
 
     traces, plans = fresh_plans()
     clocks = ClockSampler(local) if rank == 0 else None
+    PIPELINE_PROGRESS["phase"] = "device"
     dev = run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, False,
                              clocks=clocks)
     traces, plans = fresh_plans()
+    PIPELINE_PROGRESS["phase"] = "e2e"
     e2e = run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, True)
     traces, plans = fresh_plans()
+    PIPELINE_PROGRESS["phase"] = "profile"
     prof = run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, False,
                               profile=True)[5]
     # times: max over ranks; tokens: completed on the last rank; launches: sum
+    PIPELINE_PROGRESS.update(phase="results", where="all_reduce")
     t = torch.tensor([dev[0], e2e[0]], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     n = torch.tensor([dev[1], e2e[1], dev[2], e2e[3], e2e[4], e2e[8]], dtype=torch.float64,

@@ -137,13 +137,21 @@ class HostLinks:
         return buf.numpy()
 
 
-def make_groups(world: int, pairs: bool = False, timeout_s: float = 120.0):
-    """The pipeline's process groups, created collectively by every rank:
-    (NCCL group of each neighbour pair (r, r + 1) when `pairs`, else None, so
-    that boundaries use the default group; gloo group {0, N - 1} for the
-    sampled tokens, with a `timeout_s` limit on each exchange).  The boundary
-    sends and receives run on the default group unless pairs are asked for:
-    that is the configuration exercised on two GPUs."""
+def make_groups(world: int, pairs: bool = True, timeout_s: float = 120.0):
+    """The pipeline's process groups, created collectively by every rank, in
+    one order: (NCCL group of each neighbour pair (r, r + 1), or None when
+    `pairs` is false so that boundaries use the default group; gloo group
+    {0, N - 1} for the sampled tokens, with a `timeout_s` limit on each
+    exchange).
+
+    The boundaries use the pair groups.  With a process group bound to its
+    device (eager NCCL initialisation), torch derives new communicators from
+    the default one by a split that every rank of the default group must
+    join; a point-to-point link first used on the default group would start
+    such a split on two ranks only, and at four ranks the others never join
+    (observed: ranks 0 and 3 waiting in their first send and receive).
+    ``new_group`` runs the split on every rank, so the pairs' communicators
+    exist before any link is used."""
     import datetime
     import torch.distributed as dist
     pair_groups = [dist.new_group([r, r + 1]) for r in range(world - 1)] if pairs else None
