@@ -962,8 +962,9 @@ def run_pipeline_phase(stage, cfg, rank, world, links, plans, traces, F, W, K, h
         for s in d.values():
             stage.release(s)
     ttft = []
-    if host_mode and (first or final):
-        # admission wall times live on rank 0, first tokens on the last rank
+    if host_mode:
+        # admission wall times live on rank 0, first tokens on the last rank;
+        # every rank of the token group takes part in the broadcast
         obj = [admit_wall if first else None]
         dist.broadcast_object_list(obj, src=0, group=links.token_group)
         if final:

@@ -17,8 +17,8 @@ Here every rank of a torch.distributed job owns one stage on its own B200:
   micro-batch (t - r) mod N (``Schedule``), so rank r + 1 receives at tick
   t + 1 what rank r sent at tick t, and the tokens the last rank samples at
   tick t are exactly what rank 0 needs at tick t + 1;
-* sampled token ids travel back from the last rank to rank 0 over a small
-  gloo group on the host (they feed rank 0's host-side inputs).
+* sampled token ids travel back from the last rank to rank 0 over a gloo
+  group on the host (they feed rank 0's host-side inputs).
 
 ``HostLinks`` carries the same messages between CPU processes over gloo, so
 the schedule and the message order can be tested without GPUs.
@@ -140,22 +140,24 @@ class HostLinks:
 def make_groups(world: int, pairs: bool = True, timeout_s: float = 120.0):
     """The pipeline's process groups, created collectively by every rank, in
     one order: (NCCL group of each neighbour pair (r, r + 1), or None when
-    `pairs` is false so that boundaries use the default group; gloo group
-    {0, N - 1} for the sampled tokens, with a `timeout_s` limit on each
-    exchange).
+    `pairs` is false so that boundaries use the default group; a gloo group of
+    all ranks for the sampled tokens, which only ranks 0 and N - 1 exchange,
+    with a `timeout_s` limit on each exchange).
 
-    The boundaries use the pair groups.  With a process group bound to its
-    device (eager NCCL initialisation), torch derives new communicators from
-    the default one by a split that every rank of the default group must
-    join; a point-to-point link first used on the default group would start
-    such a split on two ranks only, and at four ranks the others never join
-    (observed: ranks 0 and 3 waiting in their first send and receive).
-    ``new_group`` runs the split on every rank, so the pairs' communicators
-    exist before any link is used."""
+    Every group has every rank as a member or, for the NCCL pairs, is NCCL
+    itself.  With a process group bound to its device (eager NCCL
+    initialisation), ``new_group`` makes each rank outside a new group join a
+    no-colour split of the default NCCL communicator, which the group's
+    members also run only when the new group is NCCL.  A gloo group {0, N - 1}
+    therefore left ranks 1 .. N - 2 blocked in that split at N >= 3 (observed
+    at four GPUs: ranks 0 and 3 then waited in their first send and receive).
+    Separate pair groups give each link its own NCCL communicator and stream,
+    so a middle rank's receive from the left and send to the right do not
+    serialise on one communicator."""
     import datetime
     import torch.distributed as dist
     pair_groups = [dist.new_group([r, r + 1]) for r in range(world - 1)] if pairs else None
-    tokens = dist.new_group(sorted({0, world - 1}), backend="gloo",
+    tokens = dist.new_group(list(range(world)), backend="gloo",
                             timeout=datetime.timedelta(seconds=timeout_s))
     return pair_groups, tokens
 
@@ -176,7 +178,8 @@ def device_view(ptr: int, shape, dtype="float16"):
 
 class DeviceLinks:
     """A rank's links: NCCL point-to-point for F16 boundaries on the stage's
-    stream, and a host-side gloo group {0, N-1} for sampled tokens.
+    stream, and a host-side gloo group (all ranks; only 0 and N-1 exchange)
+    for sampled tokens.
 
     recv_activation posts the receive on the stage stream (the stage's next
     work waits for it; the host does not).  send_activation copies the
