@@ -143,79 +143,95 @@ constexpr int kMaxHeadDim = 256;
 
 __global__ void __launch_bounds__(kQkvWarps * 32)
     qkv_post_kernel(QkvPostArgs a) {
-  griddep_enter();
   __shared__ __align__(16) float buf[kQkvWarps][kMaxHeadDim];
+  constexpr int kPairs = kMaxHeadDim / 64;  // rotation pairs (i, i + d/2) per lane
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int d = a.dim, half = d / 2;
   const int heads = a.hq + 2 * a.hkv;
-  const float pos = static_cast<float>(a.positions[t]);
+  const int h = blockIdx.y * kQkvWarps + warp;  // one head per warp
+  const bool is_q = h < a.hq, is_k = !is_q && h < a.hq + a.hkv;
+  // Up to the dependency wait only the packer's tables and fixed weights are
+  // read: the position, the cache slot, this lane's rotation angles and norm
+  // weights.
+  const int ipos = a.positions[t];
   const int slot = a.slot_mapping[t];
-  if (slot < 0) return;  // the packer has already flagged the missing block
+  const float* nw = is_q ? a.q_norm : (is_k ? a.k_norm : nullptr);
+  float rc[kPairs], rs[kPairs], w0[kPairs], w1[kPairs];
+  if (h < heads && (is_q || is_k)) {
+    const bool table = a.rope_table && ipos < a.rope_positions;
+#pragma unroll
+    for (int k = 0; k < kPairs; ++k) {
+      const int i = lane + 32 * k;
+      rc[k] = 1.f;
+      rs[k] = 0.f;
+      w0[k] = w1[k] = 1.f;
+      if (i < half) {
+        if (table) {
+          const float2 cs = a.rope_table[static_cast<size_t>(ipos) * half + i];
+          rc[k] = cs.x;
+          rs[k] = cs.y;
+        } else {
+          const float angle = static_cast<float>(ipos) / a.rope_pow[i];
+          rc[k] = cosf(angle);
+          rs[k] = sinf(angle);
+        }
+        if (nw) {
+          w0[k] = nw[i];
+          w1[k] = nw[half + i];
+        }
+      }
+    }
+  }
+  griddep_enter();
+  if (h >= heads || slot < 0) return;  // a missing block: the packer has already flagged it
   const float* row = a.qkv + static_cast<size_t>(t) * heads * d;
   float* x = buf[warp];
-  // One warp per head: heads [blockIdx.y * warps, +warps) of token t.
-  for (int h = blockIdx.y * kQkvWarps + warp; h < heads && h < (blockIdx.y + 1) * kQkvWarps;
-       h += kQkvWarps) {
-    const bool is_q = h < a.hq, is_k = !is_q && h < a.hq + a.hkv;
-    float ss = 0.f;
-    for (int i = lane * 4; i < d; i += 128) {  // d % 4 == 0 (checked at stage creation)
-      const float4 v = a.from_slots ? gemm_slot_sum4(a.slots, t, h * d + i, 0)
-                                    : *reinterpret_cast<const float4*>(row + h * d + i);
-      *reinterpret_cast<float4*>(x + i) = v;
-      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  float ss = 0.f;
+  for (int i = lane * 4; i < d; i += 128) {  // d % 4 == 0 (checked at stage creation)
+    const float4 v = a.from_slots ? gemm_slot_sum4(a.slots, t, h * d + i, 0)
+                                  : *reinterpret_cast<const float4*>(row + h * d + i);
+    *reinterpret_cast<float4*>(x + i) = v;
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = warp_sum(ss);
+  __syncwarp();
+  if (!is_q && !is_k) {  // value head: stored as projected
+    const int kvh = h - a.hq - a.hkv;
+    __half* dst = a.v_cache + ((static_cast<size_t>(slot / 16) * a.hkv + kvh) * 16 + slot % 16) * d;
+    for (int i = lane * 2; i < d; i += 64)
+      *reinterpret_cast<__half2*>(dst + i) = __floats2half2_rn(x[i], x[i + 1]);
+    return;
+  }
+  const float inv = nw ? 1.0f / sqrtf(ss / static_cast<float>(d) + a.eps) : 1.f;
+  __half* dst;
+  if (is_q) {
+    dst = a.q_out + static_cast<size_t>(t) * a.hq * d + static_cast<size_t>(h) * d;
+  } else {
+    const int kvh = h - a.hq;
+    dst = a.k_cache + ((static_cast<size_t>(slot / 16) * a.hkv + kvh) * 16 + slot % 16) * d;
+  }
+#pragma unroll
+  for (int k = 0; k < kPairs; ++k) {
+    const int i = lane + 32 * k;
+    if (i < half) {
+      const float p0 = x[i] * (inv * w0[k]), p1 = x[half + i] * (inv * w1[k]);
+      dst[i] = __float2half_rn(p0 * rc[k] - p1 * rs[k]);
+      dst[half + i] = __float2half_rn(p1 * rc[k] + p0 * rs[k]);
     }
-    ss = warp_sum(ss);
-    __syncwarp();
-    if (!is_q && !is_k) {  // value head: stored as projected
-      const int kvh = h - a.hq - a.hkv;
-      __half* dst = a.v_cache +
-                    ((static_cast<size_t>(slot / 16) * a.hkv + kvh) * 16 + slot % 16) * d;
-      for (int i = lane; i < d; i += 32) dst[i] = __float2half_rn(x[i]);
-      __syncwarp();
-      continue;
-    }
-    const float* nw = is_q ? a.q_norm : a.k_norm;
-    if (nw) {
-      const float inv = 1.0f / sqrtf(ss / static_cast<float>(d) + a.eps);
-      for (int i = lane; i < d; i += 32) x[i] *= inv * nw[i];
-      __syncwarp();
-    }
-    __half* dst;
-    if (is_q) {
-      dst = a.q_out + static_cast<size_t>(t) * a.hq * d + static_cast<size_t>(h) * d;
-    } else {
-      const int kvh = h - a.hq;
-      dst = a.k_cache + ((static_cast<size_t>(slot / 16) * a.hkv + kvh) * 16 + slot % 16) * d;
-    }
-    const int ipos = a.positions[t];
-    const bool table = a.rope_table && ipos < a.rope_positions;
-    for (int i = lane; i < half; i += 32) {
-      float c, s;
-      if (table) {
-        const float2 cs = a.rope_table[static_cast<size_t>(ipos) * half + i];
-        c = cs.x;
-        s = cs.y;
-      } else {
-        const float angle = pos / a.rope_pow[i];
-        c = cosf(angle);
-        s = sinf(angle);
-      }
-      const float p0 = x[i], p1 = x[half + i];
-      dst[i] = __float2half_rn(p0 * c - p1 * s);
-      dst[half + i] = __float2half_rn(p1 * c + p0 * s);
-    }
-    __syncwarp();
   }
 }
 
 // ---------------------------------------------------------------- residual + norm
 // One CTA per token: add the projection's slots into the F32 residual stream,
-// then RMSNorm the updated row into the next GEMM's F16 input.
+// then RMSNorm the updated row into the next GEMM's F16 input.  EARLY_W reads
+// the norm weights before the dependency wait: a shorter chain for a few
+// rows (decode width), but four more registers a thread, which costs
+// occupancy when the rows take several waves.
+template <bool EARLY_W>
 __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, GemmSlots slots,
                                      int has_slots, const float* __restrict__ w, float eps,
                                      __half* __restrict__ out, int ld_out) {
-  griddep_enter();
   const int t = blockIdx.x;
   float* xr = hidden + static_cast<size_t>(t) * width;
   __half* o = out + static_cast<size_t>(t) * ld_out;
@@ -236,6 +252,16 @@ __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, Gemm
   if ((width & 3) == 0 && width <= static_cast<int>(blockDim.x) * 4 * kVec) {
     // A warp covers 128 consecutive features = one GEMM tile row; the row
     // stays in registers between the sum of squares and the output.
+    float4 g[kVec];
+    if (EARLY_W) {
+#pragma unroll
+      for (int k = 0; k < kVec; ++k) {
+        const int c = (threadIdx.x + k * blockDim.x) * 4;
+        g[k] = w && c < width ? *reinterpret_cast<const float4*>(w + c)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    griddep_enter();
     float4 v[kVec];
     float ss = 0.f;
 #pragma unroll
@@ -260,15 +286,16 @@ __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, Gemm
     for (int k = 0; k < kVec; ++k) {
       const int c = (threadIdx.x + k * blockDim.x) * 4;
       if (c < width) {
-        const float4 g = *reinterpret_cast<const float4*>(w + c);
-        const __half2 lo = __floats2half2_rn(v[k].x * inv * g.x, v[k].y * inv * g.y);
-        const __half2 hi = __floats2half2_rn(v[k].z * inv * g.z, v[k].w * inv * g.w);
+        if (!EARLY_W) g[k] = *reinterpret_cast<const float4*>(w + c);
+        const __half2 lo = __floats2half2_rn(v[k].x * inv * g[k].x, v[k].y * inv * g[k].y);
+        const __half2 hi = __floats2half2_rn(v[k].z * inv * g[k].z, v[k].w * inv * g[k].w);
         *reinterpret_cast<__half2*>(o + c) = lo;
         *reinterpret_cast<__half2*>(o + c + 2) = hi;
       }
     }
     return;
   }
+  griddep_enter();
   float ss = 0.f;
   for (int c = threadIdx.x; c < width; c += blockDim.x) {
     float v = xr[c];
@@ -413,7 +440,8 @@ cudaError_t residual_norm_launch(float* hidden, int tokens, int width, const Gem
   GemmSlots s{};
   if (slots) s = *slots;
   const int threads = width >= 1024 ? 512 : (width >= 256 ? 256 : 64);
-  return launch_dependent(residual_norm_kernel, dim3(tokens), dim3(threads), 0, stream, hidden,
+  return launch_dependent(tokens <= 128 ? residual_norm_kernel<true> : residual_norm_kernel<false>,
+                          dim3(tokens), dim3(threads), 0, stream, hidden,
                           width, s, slots ? 1 : 0, norm, eps, out, ld_out);
 }
 
