@@ -191,6 +191,87 @@ def prompt_ids(rid: int, n: int, vocab: int) -> np.ndarray:
     return np.random.default_rng((SEED, rid)).integers(0, vocab, n, dtype=np.int64)
 
 
+# ---------------------------------------------------------------------------- configuration 4
+C4_ACTIVE = 128
+
+
+def ours_c4(args, world, rank, local):
+    """Configuration 4 on one GPU: the Falcon3-3B geometry (d 256, 12 query / 4 KV
+    heads, untied head) with seeded random-init weights; a burst of 256
+    requests at t = 0, 128 running at once, prompts U[128, 2048], 256 output
+    tokens, temperature 0.7 / top-p 0.9 with a seed per request, and a random
+    25% cancelled mid-decode (their KV blocks and slots go to waiting requests).
+    The timed region is the whole burst, arrival to the last token, after
+    `--warmup` steps of a different burst on the same stage."""
+    import torch
+    from hllm_b200 import B200Stage, ModelConfig, _lib
+    from hllm_b200.workload import FALCON3_3B as Fm, MixedPlanner, make_burst_trace
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"workload": "c4", "unavailable": "configuration 4 runs on one GPU "
+                              "in bench.py; its pipeline at 2/4 GPUs is not wired"}), flush=True)
+        return
+    torch.cuda.set_device(local)
+    cfg = ModelConfig(Fm["hidden_size"], Fm["intermediate_size"], Fm["attention_heads"],
+                      Fm["key_value_heads"], Fm["head_dimension"], Fm["maximum_sequence_length"],
+                      Fm["rms_norm_epsilon"], Fm["rope_theta"], Fm["query_key_norm"],
+                      Fm["vocabulary_size"], Fm["layers"], Fm["tied"])
+    stage = B200Stage(cfg, 0, Fm["layers"], first=True, final=True, device=local,
+                      kv_pool_tokens=C4_ACTIVE * Fm["maximum_sequence_length"] + 4096,
+                      max_step_tokens=C4_ACTIVE + CHUNK + 64, max_step_rows=C4_ACTIVE + 16,
+                      max_sequences=C4_ACTIVE + 16)
+    stage.init_synthetic(SEED)
+
+    def plan(seed):
+        trace = make_burst_trace(seed)
+        planner = MixedPlanner(trace, max_active=C4_ACTIVE, prefill_budget=CHUNK)
+        steps = []
+        while planner.active or planner.next_req < len(trace):
+            admits = []
+            planner.admit(on_admit=admits.append)
+            rows = planner.plan()
+            info = [(r.req.rid, r.first_position, r.tokens, r.sample, r.decode) for r in rows]
+            fin = planner.commit(rows)
+            steps.append((admits, info, [r.rid for r in fin]))
+        return trace, steps
+
+    def sampling_for(rid):
+        return _lib.Sampling(0.7, 0.9, 0, 1000 + rid, 0, 0)
+
+    # warm-up: the first steps of another burst (its sequences are released after them)
+    wtrace, wsteps = plan(SEED + 1)
+    wsteps = wsteps[:args.warmup]
+    run_device_phase(stage, cfg, wtrace, wsteps, 0, len(wsteps), sampling_for=sampling_for)
+    trace, steps = plan(SEED)
+    clocks = ClockSampler(local)
+    ms, tokens, launches, _, clock_info = run_device_phase(stage, cfg, trace, steps, 0, len(steps),
+                                                            clocks=clocks,
+                                                            sampling_for=sampling_for)
+    step_rows, step_ms = run_device_phase.last_steps
+    stage.close()
+    decode_tokens = sum(sum(c for _, c, _ in rows) for rows, dec in step_rows if dec)
+    dec_ms = sum(t for (rows, dec), t in zip(step_rows, step_ms) if dec)
+    cancelled = sum(1 for r in trace if r.cancelled)
+    line = {
+        "metric": "Falcon3-3B F16 burst tokens/s (configuration 4)", "value": round(tokens / (ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": 1, "steps": len(steps), "warmup": len(wsteps),
+        "ms_per_step": round(ms / len(steps), 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 weights, f32 accumulate", "data": "synthetic",
+        "config": {"workload": "configuration 4: Falcon3-3B architecture (22 layers, hidden 3072, "
+                   "12 query / 4 KV heads, head_dim 256, untied head) with seeded random-init "
+                   "F16 weights; 256 requests arriving at t=0, 128 at once, prompts U[128, 2048], "
+                   "256 output tokens, temperature 0.7 / top-p 0.9 with per-request seeds, "
+                   f"{cancelled} of 256 cancelled mid-decode", "global_batch": C4_ACTIVE,
+                   "seq_len": Fm["maximum_sequence_length"], "parallelism": "single stage",
+                   "l2": "inputs larger than L2: 6.5 GB of weights and the KV cache stream every step"},
+        "burst_ms": round(ms, 1), "tokens": tokens,
+        "decode_only_steps": {"steps": sum(1 for _, d in step_rows if d),
+                              "tokens_per_s": round(decode_tokens / max(1e-9, dec_ms / 1e3), 1)},
+        "clocks": clock_info, "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------------------- our arm
 def make_stage(device: int, layer_start=0, layer_end=None, first=True, final=True,
                microbatches=1):
@@ -239,7 +320,7 @@ def read_profile(stage):
 
 
 def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, clocks=None,
-                     profiler_range=False):
+                     profiler_range=False, sampling_for=None):
     """Steps [0, first_timed + K) with device-resident ids; times the last K.
 
     With profiler_range the timed steps are bracketed by cudaProfilerStart/Stop, so
@@ -287,7 +368,7 @@ def run_device_phase(stage, cfg, trace, steps, first_timed, K, profile=False, cl
             arr[j].first_position = first
             arr[j].tokens = count
             arr[j].sample = int(sample)
-            arr[j].sampling = greedy
+            arr[j].sampling = sampling_for(rid) if sampling_for else greedy
         _lib.check(L.hllm_b200_step_async(stage.handle, arr, len(rows), base + 4 * offsets[i]))
         if i >= first_timed:
             tokens += sum(r[2] for r in rows)
@@ -1110,13 +1191,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--device-phase-only", action="store_true",
                     help="run only the device-resident phase (for profiler launch lists)")
+    ap.add_argument("--workload", default="c3", choices=["c3", "c4"],
+                    help="c3: the headline (configuration 3); c4: configuration 4's burst")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
+    if args.workload == "c4":
+        ours_c4(args, world, rank, local)
+    elif args.impl == "reference":
         reference(args, world, rank)
     else:
         ours(args, world, rank, local)

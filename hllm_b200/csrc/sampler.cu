@@ -110,12 +110,38 @@ __device__ uint64_t radix_select(const float* lg, const double* p, int n, uint64
     }
     __syncthreads();
     const uint64_t prefix = s.prefix, mask = s.mask;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const uint64_t key = sort_key(lg[i], i);
-      if (key < floor_key || (key & mask) != prefix) continue;
-      const int digit = static_cast<int>((key >> shift) & 255u);
-      atomicAdd(&s.mass[digit], p[i]);
-      atomicAdd(&s.count[digit], 1u);
+    // Whole warps walk the row (trip counts equal across a warp).  Keys of
+    // nearby logits share their high digits, so most of a warp's lanes often
+    // hit one bucket: the lanes that agree with the warp's first live lane
+    // add their mass through one shuffle reduction and one shared atomic.
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    for (int base = static_cast<int>(threadIdx.x) - lane; base < n;
+         base += static_cast<int>(blockDim.x)) {
+      const int i = base + lane;
+      int digit = -1;
+      double pm = 0.0;
+      if (i < n) {
+        const uint64_t key = sort_key(lg[i], i);
+        if (key >= floor_key && (key & mask) == prefix) {
+          digit = static_cast<int>((key >> shift) & 255u);
+          pm = p[i];
+        }
+      }
+      const unsigned live = __ballot_sync(0xffffffffu, digit >= 0);
+      if (live == 0) continue;
+      const int d0 = __shfl_sync(0xffffffffu, digit, __ffs(live) - 1);
+      const unsigned same = __ballot_sync(0xffffffffu, digit == d0);
+      double agg = digit == d0 ? pm : 0.0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) agg += __shfl_xor_sync(0xffffffffu, agg, o);
+      if (lane == __ffs(same) - 1) {
+        atomicAdd(&s.mass[d0], agg);
+        atomicAdd(&s.count[d0], static_cast<unsigned>(__popc(same)));
+      }
+      if (digit >= 0 && digit != d0) {
+        atomicAdd(&s.mass[digit], pm);
+        atomicAdd(&s.count[digit], 1u);
+      }
     }
     __syncthreads();
     if (threadIdx.x == 0) {

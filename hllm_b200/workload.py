@@ -15,6 +15,12 @@ Workload (configuration 3): 64 concurrent requests; Poisson arrivals at
 as a slot frees); prompt lengths log-normal (median 512, sigma 1.0) clipped to
 [32, 4096]; output lengths uniform in [64, 512]; uniform random token ids;
 greedy decoding.  All draws come from one recorded seed.
+
+Workload (configuration 4, ``make_burst_trace``): Falcon3-3B geometry; every
+request arrives at t = 0; prompt lengths uniform in [128, 2048]; 256 output
+tokens each; temperature 0.7 / top-p 0.9 with a seed per request; a random
+25% are cancelled mid-decode (after a uniform 1..255 of their tokens), which
+frees their KV blocks and slots for requests still waiting.  128 run at once.
 """
 from __future__ import annotations
 
@@ -28,6 +34,12 @@ QWEN3_4B = dict(hidden_size=2560, intermediate_size=9728, attention_heads=32, ke
                 query_key_norm=True, tied=True)
 
 
+FALCON3_3B = dict(hidden_size=3072, intermediate_size=9216, attention_heads=12,
+                  key_value_heads=4, head_dimension=256, layers=22, vocabulary_size=131072,
+                  maximum_sequence_length=2304, rms_norm_epsilon=1e-6, rope_theta=1e6,
+                  query_key_norm=False, tied=False)
+
+
 @dataclass
 class Request:
     rid: int
@@ -38,10 +50,15 @@ class Request:
     generated: int = 0
     admitted_step: int = -1
     first_token_step: int = -1
+    cancel_at: int = 0  # cancelled once this many tokens are generated (0: never)
+
+    @property
+    def cancelled(self) -> bool:
+        return 0 < self.cancel_at <= self.generated < self.output_len
 
     @property
     def done(self) -> bool:
-        return self.generated >= self.output_len
+        return self.generated >= self.output_len or self.cancelled
 
     @property
     def capacity(self) -> int:
@@ -57,6 +74,19 @@ def make_trace(seed: int, n_requests: int = 2048, rate: float = 8.0, median: flo
     outs = rng.integers(out_lo, out_hi + 1, n_requests)
     return [Request(i, float(arrivals[i]), int(prompts[i]), int(outs[i]))
             for i in range(n_requests)]
+
+
+def make_burst_trace(seed: int, n_requests: int = 256, prompt_lo: int = 128,
+                     prompt_hi: int = 2048, output_len: int = 256,
+                     cancel_fraction: float = 0.25):
+    """Configuration 4's bursty trace: every request arrives at t = 0, and a
+    random `cancel_fraction` of them are cancelled mid-decode."""
+    rng = np.random.default_rng(seed)
+    prompts = rng.integers(prompt_lo, prompt_hi + 1, n_requests)
+    cancel = rng.random(n_requests) < cancel_fraction
+    at = rng.integers(1, output_len, n_requests)
+    return [Request(i, 0.0, int(prompts[i]), output_len,
+                    cancel_at=int(at[i]) if cancel[i] else 0) for i in range(n_requests)]
 
 
 @dataclass
