@@ -136,8 +136,9 @@ __device__ inline float gemm_slot_sum(const GemmSlots& s, int n, int m, int acc)
 }
 
 // The same sum for four consecutive features m..m+3 (m % 4 == 0, one tile):
-// slot loads go out four at a time (a few registers each, so the consumer
-// kernels keep their occupancy) and are added in CTA order.
+// slot loads go out CHUNK at a time (four registers each, so a consumer picks
+// CHUNK against its occupancy) and are added in CTA order.
+template <int CHUNK = 4>
 __device__ inline float4 gemm_slot_sum4(const GemmSlots& s, int n, int m, int acc) {
   const int tile = (m >> 7) * s.n_tiles + n / s.bn;
   const int2 cs = gemm_tile_ctas(s, tile);
@@ -147,10 +148,10 @@ __device__ inline float4 gemm_slot_sum4(const GemmSlots& s, int n, int m, int ac
   const float* base = s.slots + within;
   const int first = gemm_first_slot(s, cs.x, tile);
   float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int c0 = cs.x; c0 <= cs.y; c0 += 4) {
-    float4 v[4];
+  for (int c0 = cs.x; c0 <= cs.y; c0 += CHUNK) {
+    float4 v[CHUNK];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < CHUNK; ++j) {
       const int c = c0 + j;
       const int slot = c == cs.x ? first : c * kGemmSlotsPerCta;
       v[j] = c <= cs.y ? __ldcg(reinterpret_cast<const float4*>(
@@ -158,7 +159,7 @@ __device__ inline float4 gemm_slot_sum4(const GemmSlots& s, int n, int m, int ac
                        : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < CHUNK; ++j) {
       if (c0 + j <= cs.y) {
         sum.x += v[j].x;
         sum.y += v[j].y;

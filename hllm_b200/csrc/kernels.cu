@@ -1,5 +1,6 @@
 // kernels.cu -- packer, embedding, norms, q/k-norm + RoPE + paged-KV write,
 // boundary conversion and synthetic initialisation for the stage executor.
+#include <algorithm>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -224,10 +225,11 @@ __global__ void __launch_bounds__(kQkvWarps * 32)
 
 // ---------------------------------------------------------------- residual + norm
 // One CTA per token: add the projection's slots into the F32 residual stream,
-// then RMSNorm the updated row into the next GEMM's F16 input.  EARLY_W reads
-// the norm weights before the dependency wait: a shorter chain for a few
-// rows (decode width), but four more registers a thread, which costs
-// occupancy when the rows take several waves.
+// then RMSNorm the updated row into the next GEMM's F16 input.  EARLY_W is the
+// decode-width form: a CTA of width/4 threads (one float4 of the row each)
+// reads its norm weights before the dependency wait and keeps eight slot
+// loads in flight -- a shorter chain for a few rows, at a register and thread
+// cost that would lower occupancy when the rows take several waves.
 template <bool EARLY_W>
 __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, GemmSlots slots,
                                      int has_slots, const float* __restrict__ w, float eps,
@@ -270,7 +272,8 @@ __global__ void residual_norm_kernel(float* __restrict__ hidden, int width, Gemm
       if (c < width) {
         v[k] = *reinterpret_cast<const float4*>(xr + c);
         if (has_slots) {
-          const float4 a = gemm_slot_sum4(slots, t, c, 0);
+          const float4 a =
+              EARLY_W ? gemm_slot_sum4<8>(slots, t, c, 0) : gemm_slot_sum4(slots, t, c, 0);
           v[k].x += a.x;
           v[k].y += a.y;
           v[k].z += a.z;
@@ -439,7 +442,9 @@ cudaError_t residual_norm_launch(float* hidden, int tokens, int width, const Gem
   if (tokens <= 0) return cudaSuccess;
   GemmSlots s{};
   if (slots) s = *slots;
-  const int threads = width >= 1024 ? 512 : (width >= 256 ? 256 : 64);
+  const int threads = tokens <= 128 && (width & 3) == 0 && width <= 4096
+                          ? std::max(64, (width / 4 + 31) / 32 * 32)
+                          : (width >= 1024 ? 512 : (width >= 256 ? 256 : 64));
   return launch_dependent(tokens <= 128 ? residual_norm_kernel<true> : residual_norm_kernel<false>,
                           dim3(tokens), dim3(threads), 0, stream, hidden,
                           width, s, slots ? 1 : 0, norm, eps, out, ld_out);
