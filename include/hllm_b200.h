@@ -400,16 +400,16 @@ hllm_b200_status hllm_b200_pack(const int32_t* row_slot, const int32_t* row_firs
  * [kv_blocks][Hkv][16][d]; packer outputs as above; out F16 [tokens][ld_out].
  * Decode rows (one token): for head sizes 64/128/256 the decode rows' KV
  * pages are split evenly over one wave of warps, each streaming its pages by
- * TMA (kv_blocks bounds the maps and is required), and the pieces of each
- * (row, kv head) are merged by its last warp (cu_splits and split_tokens only
- * bound the work); other head sizes use split-K over `split_tokens`-key
+ * TMA (kv_blocks bounds the maps and is required), and a second launch
+ * merges the pieces of each (row, kv head) split across warps (cu_splits and
+ * split_tokens only bound the work); other head sizes use split-K over `split_tokens`-key
  * splits.  Prefill rows: causal tiles of hllm_b200_attention_qtile_tokens(
  * Hq/Hkv) tokens, each tile's keys split over CTAs that fill one wave; for
  * head sizes 64 and 128 (GQA groups 1/2/4/8) on tcgen05 with S and O in TMEM
  * and TMA-fed K/V pages (q_tokens and kv_blocks bound the TMA maps; 0 selects
- * the mma.sync tiles, as HLLM_B200_TC_PREFILL=0 does).  Split outputs and
- * arrival counters live in a per-device workspace that the first call
- * allocates. */
+ * the mma.sync tiles, as HLLM_B200_TC_PREFILL=0 does).  Split outputs, the
+ * decode streams' warp ranges and the prefill arrival counters live in a
+ * per-device workspace that the first call allocates. */
 hllm_b200_status hllm_b200_attention(const uint16_t* q, const uint16_t* k_cache,
                                      const uint16_t* v_cache, const int32_t* row_first,
                                      const int32_t* row_count, const int32_t* cu_seqlens,
