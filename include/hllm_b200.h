@@ -401,9 +401,9 @@ hllm_b200_status hllm_b200_pack(const int32_t* row_slot, const int32_t* row_firs
  * Decode rows (one token): for head sizes 64/128/256 the decode rows' KV
  * pages are split evenly over one wave of warps, each streaming its pages by
  * TMA (kv_blocks bounds the maps and is required), and a second launch
- * merges the pieces of each (row, kv head) split across warps (cu_splits and
- * split_tokens only bound the work); other head sizes use split-K over `split_tokens`-key
- * splits.  Prefill rows: causal tiles of hllm_b200_attention_qtile_tokens(
+ * merges the pieces of each (row, kv head) split across warps (cu_splits
+ * and split_tokens only bound the work); other head sizes use split-K over
+ * `split_tokens`-key splits.  Prefill rows: causal tiles of hllm_b200_attention_qtile_tokens(
  * Hq/Hkv) tokens, each tile's keys split over CTAs that fill one wave; for
  * head sizes 64 and 128 (GQA groups 1/2/4/8) on tcgen05 with S and O in TMEM
  * and TMA-fed K/V pages (q_tokens and kv_blocks bound the TMA maps; 0 selects
